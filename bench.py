@@ -1,0 +1,371 @@
+#!/usr/bin/env python
+"""DiT-CFM sampler benchmark: mel frames/s through the 25-step CFG sampler.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload 2|5] [--utts B]
+
+A bench "step" is one full sampler run (all CFM steps) over the rank's batch.
+Default workload is BASELINE config 2 per rank: one utterance of T=800 frames
+(P=200 prompt frames), 25 Euler steps, CFG 0.7, random-init f16 weights
+~N(0, 0.02), inputs ~N(0, 1) (seed 1 + rank). Under torchrun each rank owns
+one GPU and its own utterances (weak scaling, no data-path collective); timing
+is CUDA events on the engine's stream, max over ranks.
+
+--impl reference times the reference's own CPU path (oracle/_ref, the
+reference's run_dit_estimator_step_cpu compiled from its sources) on the
+host's cores on a bounded sample of the same workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "index-tts2-metal_b200"
+for _p in (str(PKG), str(REPO / "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import mit2  # noqa: E402
+import workloads  # noqa: E402
+
+METRIC = "mel frames/s, 25-step CFG DiT CFM at 1/2/4/8 B200; ms per CFM step"
+UNIT = "mel frames/s"
+BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_seed0_baseline"
+REF_SAMPLE_FRAMES = 32
+
+
+def _env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, interval_ms: int = 20):
+        self.gpu = gpu_index
+        self.interval = interval_ms
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="itts_clocks_", suffix=".csv")[1])
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", str(self.interval)], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- reference arm
+
+def _ref_guided_step_sample(ref, u, frames: int, threads: int) -> float:
+    """Wall time of one guided CFM step (conditional + null estimator calls of
+    the reference's run_dit_estimator_step_cpu) on a `frames`-row slice of the
+    utterance, run concurrently on `threads` host threads."""
+    x = u.noise[:frames].copy()
+    px = u.prompt_x()[:frames]
+    cond = u.cond[:frames]
+    mask = np.ones(frames, np.uint32)
+    zp, zc, zs = np.zeros_like(px), np.zeros_like(cond), np.zeros_like(u.style)
+    errs = []
+
+    def work():
+        try:
+            ref.estimator(x, px, cond, u.style, 0.0, mask)
+            ref.estimator(x, zp, zc, zs, 0.0, mask)
+        except Exception as e:  # pragma: no cover
+            errs.append(e)
+
+    ths = [threading.Thread(target=work) for _ in range(threads)]
+    t0 = time.perf_counter()
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    dt = time.perf_counter() - t0
+    if errs:
+        raise errs[0]
+    return dt
+
+
+def _host_threads() -> int:
+    n = os.cpu_count() or 1
+    try:
+        import psutil
+
+        # the reference decodes every weight to fp32 per estimator call (~0.4 GB)
+        n = min(n, max(1, int(psutil.virtual_memory().available / 1.0e9)))
+    except Exception:
+        pass
+    return max(1, min(n, 64))
+
+
+def cpu_reference_rate(u, steps_cfm: int, threads: int, reps: int = 1):
+    import oracle
+
+    ref = oracle.RefOracle(BUNDLE_DIR)
+    ts = [_ref_guided_step_sample(ref, u, REF_SAMPLE_FRAMES, threads) for _ in range(reps)]
+    t = min(ts)
+    fps = threads * REF_SAMPLE_FRAMES / (steps_cfm * t)
+    return fps, t
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    import oracle
+
+    cfg = workloads.CONFIGS[args.workload]
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_cfm.so was not built"}))
+        return 0
+    mit2.make_dit_bundle(BUNDLE_DIR, seed=0, init="baseline")
+    u = workloads.config_utterances(args.workload, n=1)[0]
+    threads = _host_threads()
+    ref = oracle.RefOracle(BUNDLE_DIR)
+    for _ in range(args.warmup):
+        _ref_guided_step_sample(ref, u, REF_SAMPLE_FRAMES, threads)
+    t0 = time.perf_counter()
+    per = [_ref_guided_step_sample(ref, u, REF_SAMPLE_FRAMES, threads) for _ in range(args.steps)]
+    total = time.perf_counter() - t0
+    # frames of a full `steps_cfm` sampler run per sample, scaled from one guided step
+    fps = threads * REF_SAMPLE_FRAMES * args.steps / (cfg["steps"] * total)
+    sample = (f"per step: {threads} host threads each run one conditional + one null "
+              f"run_dit_estimator_step_cpu call on a {REF_SAMPLE_FRAMES}-frame slice of the config-{args.workload} "
+              f"utterance; frames/s = threads*{REF_SAMPLE_FRAMES}/({cfg['steps']} CFM steps * step time)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config {args.workload}", "T": cfg["T"], "steps_cfm": cfg["steps"], "cfg_rate": cfg["cfg"]},
+        "cpu_baseline": {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "per_step_s": per,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", type=int, choices=[2, 5], default=2)
+    ap.add_argument("--utts", type=int, default=None, help="utterances per GPU (default: 1 for config 2)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = _env_int("RANK", 0)
+    world = _env_int("WORLD_SIZE", 1)
+    local = _env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+
+    import itts_cfm
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    if rank == 0 or world == 1:
+        mit2.make_dit_bundle(BUNDLE_DIR, seed=0, init="baseline")
+    barrier()
+    cfg = workloads.CONFIGS[args.workload]
+    B = args.utts or (1 if args.workload == 2 else 64)
+    utts = workloads.config_utterances(args.workload, n=B, seed_offset=rank * 1000)
+    T = cfg["T"]
+    vl, pl, noise, px, cond, style = workloads.pad_batch(utts, T)
+    ctx = itts_cfm.Context(BUNDLE_DIR, device=local)
+    ctx.stage_padded(vl, pl, noise, px, cond, style, cfg["steps"], cfg["cfg"])
+    launches_per_step = ctx.launch_kernels()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+
+    for _ in range(args.warmup):
+        ctx.launch()
+    ctx.sync()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.05)
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        ctx.launch()
+    ev1.record(stream)
+    ev1.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ctx.sync()
+    frames_per_step = B * T * world
+    value = frames_per_step * args.steps / (ms / 1e3)
+
+    # e2e through the public API with pinned host buffers and host<->device copies.
+    pin = lambda a: torch.from_numpy(a).pin_memory().numpy()  # noqa: E731
+    h_noise, h_px, h_cond, h_style = pin(noise), pin(px), pin(cond), pin(style)
+    h_out = torch.empty((B, T, 80), dtype=torch.float32).pin_memory().numpy()
+    import ctypes as C
+
+    lib = itts_cfm.load()
+    vl_c, pl_c = np.ascontiguousarray(vl), np.ascontiguousarray(pl)
+
+    def e2e_once():
+        rc = lib.itts_cfm_run_padded(ctx.h, B, T, vl_c.ctypes.data_as(C.c_void_p), pl_c.ctypes.data_as(C.c_void_p),
+                                     h_noise.ctypes.data_as(C.c_void_p), h_px.ctypes.data_as(C.c_void_p),
+                                     h_cond.ctypes.data_as(C.c_void_p), h_style.ctypes.data_as(C.c_void_p),
+                                     cfg["steps"], float(cfg["cfg"]), h_out.ctypes.data_as(C.c_void_p))
+        if rc != 0:
+            raise RuntimeError(lib.itts_cfm_last_error(ctx.h).decode())
+
+    for _ in range(2):
+        e2e_once()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_once()
+    t_e2e = time.perf_counter() - t0
+    barrier()
+    t_e2e = max_over_ranks(t_e2e)
+    e2e_value = frames_per_step * args.steps / t_e2e
+    h2d = noise.nbytes + px.nbytes + cond.nbytes + style.nbytes + vl.nbytes + pl.nbytes + B * 2 * T * 4
+    d2h = B * T * 80 * 4 + 4
+
+    # Roofline of the dominant kernel (all tcgen05 GEMM launches), timed per launch.
+    ctx.stage_padded(vl, pl, noise, px, cond, style, cfg["steps"], cfg["cfg"])
+    prof = ctx.profile_step(reps=3)
+    prof.sort(key=lambda d: -d["ms"])
+    total_prof_ms = sum(d["ms"] for d in prof)
+    gemm = next(d for d in prof if d["name"] == "gemm")
+    peaks, peaks_kind = measured_peaks()
+    achieved = gemm["flops"] / (gemm["ms"] / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    traffic = None
+    tf = REPO / "profiles" / "gemm_traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get(f"config{args.workload}_bytes_per_launch")
+        except Exception:
+            traffic = None
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": traffic, "kernel": "gemm_tc_kernel (tcgen05, all GEMM launches of one CFM step)",
+                "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(gemm["launches"], 1),
+                "peak_source": f"MEASURED_PEAKS.json bf16_tflops ({peaks_kind}, burst)",
+                "time_share": gemm["ms"] / total_prof_ms if total_prof_ms else None,
+                "kernels": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in d.items()} for d in prof]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        if oracle.ref_available():
+            threads = _host_threads()
+            fps, t = cpu_reference_rate(utts[0], cfg["steps"], threads)
+            cpu = {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": (f"{threads} threads, each one guided CFM step (cond + null run_dit_estimator_step_cpu) "
+                              f"on a {REF_SAMPLE_FRAMES}-frame slice; {t:.2f} s; scaled to frames/s of a "
+                              f"{cfg['steps']}-step run")}
+
+    ctx.close()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"config {args.workload}: {B} utterance(s)/GPU, T={T}, P={cfg['P']}, "
+                                   f"{cfg['steps']} CFM steps, CFG {cfg['cfg']}",
+                       "utterances_per_gpu": B, "T": T, "steps_cfm": cfg["steps"], "cfg_rate": cfg["cfg"],
+                       "global_batch": B * world, "parallelism": f"utterance-sharded x{world}",
+                       "l2": "working set > L2: 182 MB of weights re-read every CFM step (126 MB L2)",
+                       "weights": "random-init f16 ~N(0,0.02), seed 0"},
+            "ms_per_cfm_step": ms / args.steps / cfg["steps"],
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line))
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,190 @@
+/*
+ * itts_cfm.h — C ABI of the B200 (sm_100a) IndexTTS2 S2Mel stage: the DiT
+ * estimator inside the conditional-flow-matching Euler sampler with
+ * classifier-free guidance.
+ *
+ * Every entry point returns an int status (ITTS_OK = 0, negative on error);
+ * no C++ exception crosses this boundary. Host buffers are owned by the
+ * caller; the context owns the device weights, t-conditioning tables,
+ * workspaces and CUDA graphs. A context is bound to one GPU and must be used
+ * from one host thread at a time.
+ *
+ * Layouts are row-major, token-major: a mel is [T, 80] float32, the content
+ * condition [T, 512], the style vector [192].
+ */
+#ifndef ITTS_CFM_H
+#define ITTS_CFM_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct itts_cfm_ctx itts_cfm_ctx;
+
+enum {
+  ITTS_OK = 0,
+  ITTS_EINVAL_SHAPE = -1, /* a size, count or pointer argument is out of range */
+  ITTS_EBUNDLE = -2,      /* the MIT2 bundle is missing, malformed or incomplete */
+  ITTS_ECUDA = -3,        /* a CUDA call failed (message in itts_cfm_last_error) */
+  ITTS_ETIMEOUT = -4,     /* a kernel abandoned a bounded device-side wait */
+  ITTS_ECAP = -5,         /* the request exceeds a documented capacity limit */
+  ITTS_ENODEV = -6        /* no usable sm_100 device with that id */
+};
+
+/* itts_cfm_create_ex flags */
+#define ITTS_CREATE_VERIFY_SHA256 0x1u
+
+/* Capacity limits. */
+#define ITTS_MAX_T 65536u          /* frames per utterance */
+#define ITTS_MIN_T 2u              /* reflect padding of the k=5 conv needs two rows */
+#define ITTS_MAX_STEPS 1000u
+#define ITTS_MAX_ROWS (1u << 22)   /* estimator rows per launch: utterances x branches x T */
+
+/* One utterance for itts_cfm_run_batch. */
+typedef struct {
+  const float* noise;  /* [T, 80] initial x (prompt rows are zeroed by the sampler) */
+  const float* prompt; /* [P, 80] prompt mel rows (may be NULL when P == 0) */
+  const float* cond;   /* [T, 512] content condition */
+  const float* style;  /* [192] style vector */
+  uint32_t T;
+  uint32_t P;
+  float* out_mel; /* [T, 80] result; prompt rows are 0 */
+} itts_cfm_utt;
+
+/* Per-kernel timing of one profiled sampler step (itts_cfm_profile_step). */
+typedef struct {
+  char name[32];
+  int32_t launches;
+  double ms;
+  double flops;
+  double bytes;
+} itts_kernel_stat;
+
+/*
+ * Load the estimator weights of an MIT2 bundle (manifest.json + weights.bin)
+ * onto `device`. Replaces mit2::Bundle construction plus the lazy resident
+ * weight upload of mit2::MetalContext (runtime/bundle.cpp:172,
+ * runtime/include/mit2/metal_context.hpp:151-234).
+ */
+int itts_cfm_create(const char* bundle_dir, int device, itts_cfm_ctx** out);
+int itts_cfm_create_ex(const char* bundle_dir, int device, uint32_t flags, itts_cfm_ctx** out);
+void itts_cfm_destroy(itts_cfm_ctx* ctx);
+/* Message of the last failure on this context ("" when none). */
+const char* itts_cfm_last_error(const itts_cfm_ctx* ctx);
+/* Message of the last itts_cfm_create failure on this thread. */
+const char* itts_cfm_create_error(void);
+const char* itts_cfm_strerror(int code);
+
+/*
+ * Full CFM sampler for one utterance: replaces run_cfm_euler_metal /
+ * run_cfm_euler_cpu (runtime/impl/dit_cfm_bigvgan.cpp:3121-3124, 2908).
+ * x starts at `noise`, prompt rows (< P) are zeroed before the loop and after
+ * every step, t runs 0 -> 1 in `steps` Euler steps of dt = 1/steps, and with
+ * cfg_rate > 0 the velocity is (1+cfg)·v(cond) − cfg·v(null), the null branch
+ * using zero prompt, condition and style. Writes the full mel [T, 80].
+ */
+int itts_cfm_run(itts_cfm_ctx* ctx, const float* noise, const float* prompt, const float* cond, const float* style,
+                 uint32_t T, uint32_t P, uint32_t steps, float cfg_rate, float* out_mel);
+
+/*
+ * Batched serving: utterances are sorted into length buckets
+ * (itts_cfm_bucket_len), padded with zero rows and key-padding masks, and run
+ * bucket by bucket. A padded utterance equals the single-utterance sampler run
+ * at the padded length with its mask (reflect padding and masking make it
+ * differ slightly from the unpadded run; bucket length == T gives exactly
+ * itts_cfm_run). Has no single reference function: it batches calls of
+ * run_cfm_euler_metal (runtime/impl/tts_synthesis/synthesis_pipeline.cpp:1085).
+ */
+int itts_cfm_run_batch(itts_cfm_ctx* ctx, uint32_t n, const itts_cfm_utt* utts, uint32_t steps, float cfg_rate);
+/* Padded length an utterance of T frames is bucketed to by itts_cfm_run_batch. */
+uint32_t itts_cfm_bucket_len(uint32_t T);
+
+/*
+ * B utterances that already share one padded length T. valid_len[b] frames
+ * are real (mask 1), the rest padding (mask 0); prompt_x is [B, T, 80] with
+ * the prompt mel in rows < prompt_len[b] and zeros elsewhere (the reference's
+ * prompt_x, runtime/impl/dit_cfm_bigvgan.cpp:2909-2913). Output [B, T, 80].
+ */
+int itts_cfm_run_padded(itts_cfm_ctx* ctx, uint32_t B, uint32_t T, const uint32_t* valid_len,
+                        const uint32_t* prompt_len, const float* noise, const float* prompt_x, const float* cond,
+                        const float* style, uint32_t steps, float cfg_rate, float* out_mel);
+
+/*
+ * One DiT estimator evaluation at timestep t for B utterances of T rows:
+ * replaces run_dit_estimator_step_cpu (runtime/impl/dit_cfm_bigvgan.cpp:1768-1788)
+ * and, with branches == 2, the batched conditional + null pass
+ * (run_dit_estimator_step_metal_cfg_transformer_batched_pass, :2001).
+ * x, prompt_x: [B, T, 80]; cond: [B, T, 512]; style: [B, 192];
+ * mask: [B, T] (0 = padded key); vel: [B, branches, T, 80] (branch 0 = conditional,
+ * branch 1 = null: zero prompt_x, cond and style).
+ */
+int itts_cfm_estimator(itts_cfm_ctx* ctx, uint32_t B, uint32_t T, uint32_t branches, const float* x,
+                       const float* prompt_x, const float* cond, const float* style, const uint32_t* mask, float t,
+                       float* vel);
+
+/*
+ * Device-resident staging (benchmarks): copy a padded batch into the
+ * context's workspace once, enqueue the sampler any number of times on the
+ * context's stream (inputs never leave HBM), then fetch the mel.
+ */
+int itts_cfm_stage_padded(itts_cfm_ctx* ctx, uint32_t B, uint32_t T, const uint32_t* valid_len,
+                          const uint32_t* prompt_len, const float* noise, const float* prompt_x, const float* cond,
+                          const float* style, uint32_t steps, float cfg_rate);
+int itts_cfm_launch(itts_cfm_ctx* ctx);
+int itts_cfm_sync(itts_cfm_ctx* ctx);
+int itts_cfm_fetch(itts_cfm_ctx* ctx, float* out_mel);
+/* The context's cudaStream_t (as void*), for event timing by the caller. */
+void* itts_cfm_stream(itts_cfm_ctx* ctx);
+/* Kernel launches one itts_cfm_launch of the staged batch performs (the
+ * kernel nodes of its captured CUDA graph), or a negative status. */
+int itts_cfm_launch_kernels(itts_cfm_ctx* ctx);
+
+/*
+ * Time every kernel of `reps` sampler steps of the staged batch with CUDA
+ * events around each launch (no graph). Fills up to `cap` entries.
+ */
+int itts_cfm_profile_step(itts_cfm_ctx* ctx, int reps, itts_kernel_stat* out, int cap, int* n_out);
+
+/* Algorithmic FLOPs of one guided step over S sequences of T rows. */
+double itts_cfm_step_flops(uint32_t S, uint32_t T);
+
+/*
+ * Kernel-level entry points on caller-owned DEVICE pointers, for parity tests
+ * of single kernels. They run on the context's stream and synchronise.
+ *
+ * itts_op_gemm: C[M,N] (f32, row stride ldc) = A[M,K] · B[N,K]^T + bias, A and B
+ * f16 row-major; with a1 != NULL the first kb_split*64 columns of K come from
+ * a0 and the rest from a1 (a concat without a buffer). Replaces the MPS GEMM
+ * of linear_rows_f32_pass (runtime/metal_context.mm:344-381).
+ */
+int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a1, uint32_t lda1, uint32_t k0,
+                 const void* b, uint32_t ldb, const float* bias, float* c, uint32_t ldc, uint32_t M, uint32_t N,
+                 uint32_t K, uint32_t bn);
+/*
+ * itts_op_conv5: reflect-padded k=5 "same" conv as an implicit GEMM.
+ * xp: [S*(T+4), 512] f16 rows already reflect-padded (2 halo rows each side per
+ * sequence); w: [N][5*512] f16 tap-major; out: [S*T, N] f32. Replaces
+ * cpu_conv1d_reflect_same (runtime/impl/tokenizer_tests.cpp:3866-3872).
+ */
+int itts_op_conv5(itts_cfm_ctx* ctx, const void* xp, uint32_t S, uint32_t T, const void* w, const float* bias,
+                  float* out, uint32_t N);
+/*
+ * itts_op_attention: masked MHA over packed qkv [S*T, 1536] f16 (q pre-scaled,
+ * RoPE already applied) -> out [S*T, 512] f16; row_mask [S*T] f32 (0 = masked key).
+ * Replaces mit2_dit_attention_sgq_batched_f32 (metal/kernels.metal:2625-2807).
+ */
+int itts_op_attention(itts_cfm_ctx* ctx, const void* qkv, const float* row_mask, void* out, uint32_t S, uint32_t T);
+/*
+ * itts_op_adarms: y = w ⊙ (x·rsqrt(mean x² + 1e-5) ⊙ gamma) + b, x [R,512] f32,
+ * wb = [w | b] (1024 f32), y f16. Replaces mit2_adaptive_rmsnorm_f32_rows
+ * (metal/kernels.metal:755-792).
+ */
+int itts_op_adarms(itts_cfm_ctx* ctx, const float* x, uint32_t R, const float* wb, const float* gamma, void* y);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ITTS_CFM_H */

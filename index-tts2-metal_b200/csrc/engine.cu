@@ -1,0 +1,538 @@
+// DiT-CFM sampler engine. Step schedule (one guided Euler step, both CFG
+// branches batched as rows [u0 cond | u0 null | u1 cond | ...]):
+//   merge GEMM (x slice, + step-invariant base) -> 13 x { [skip-in GEMM],
+//   AdaRMSNorm, QKV GEMM (+RoPE), attention, wo GEMM (+residual), AdaRMSNorm,
+//   w13 GEMM (+SwiGLU), w2 GEMM (+residual) } -> AdaRMSNorm -> skip_linear GEMM
+//   -> conv1|res GEMM (-> reflect-padded WaveNet input) -> 8 x { k=5 conv GEMM
+//   (+gate), res/skip GEMM (+update) } -> AdaLN -> final linear GEMM -> conv2
+//   GEMM -> CFG + Euler + prompt zero.
+// Follows run_cfm_euler_cpu / run_dit_estimator_step_cpu
+// (runtime/impl/dit_cfm_bigvgan.cpp:2908-2937, 1768-1788) and the single-pass
+// Metal schedule (runtime/impl/dit_cfm_bigvgan.cpp:2367-2713).
+#include "engine.hpp"
+
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+#include "kernels.cuh"
+
+namespace itts {
+
+namespace {
+
+struct Operand {
+  const __half* p = nullptr;
+  int cols = 0;  // logical columns (K extent)
+  int rows = 0;
+  int ld = 0;    // elements
+};
+
+GemmLaunch make_gemm(Operand a0, Operand a1, Operand b, int M, int N, int K, int a_mode, int kb_split,
+                     int kb_per_tap, int bn, int epi) {
+  GemmLaunch g;
+  std::memset(&g, 0, sizeof(g));
+  if (!make_tmap_f16(&g.tmA0, a0.p, a0.cols, a0.rows, a0.ld, 128))
+    throw std::runtime_error("gemm: tensor map for A0 rejected");
+  if (a1.p) {
+    if (!make_tmap_f16(&g.tmA1, a1.p, a1.cols, a1.rows, a1.ld, 128))
+      throw std::runtime_error("gemm: tensor map for A1 rejected");
+  } else {
+    g.tmA1 = g.tmA0;
+  }
+  if (!make_tmap_f16(&g.tmB, b.p, b.cols, b.rows, b.ld, static_cast<uint32_t>(bn)))
+    throw std::runtime_error("gemm: tensor map for B rejected");
+  g.args.M = M;
+  g.args.N = N;
+  g.args.num_kb = (K + 63) / 64;
+  g.args.a_mode = a_mode;
+  g.args.kb_split = kb_split;
+  g.args.kb_per_tap = kb_per_tap;
+  g.args.epi = epi;
+  g.bn = bn;
+  g.stages = 4;
+  return g;
+}
+
+template <typename T>
+T* carve(uint8_t*& cur, size_t count) {
+  T* p = reinterpret_cast<T*>(cur);
+  cur += (count * sizeof(T) + 255) & ~size_t(255);
+  return p;
+}
+
+uint32_t fbits(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  return u;
+}
+
+}  // namespace
+
+double step_flops(int S, int T) {
+  const double rows = static_cast<double>(S) * T;
+  // 73,523,200 MACs per row per step (merge x slice, 13 blocks, skip-ins,
+  // skip_linear, conv1, res, 8 WaveNet layers, final linear, conv2).
+  const double gemm = 2.0 * 73523200.0 * rows;
+  const double attn = static_cast<double>(S) * 13.0 * 4.0 * static_cast<double>(T) * T * 512.0;
+  return gemm + attn;
+}
+
+void Engine::check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cuda: ") + what + ": " + cudaGetErrorString(e));
+}
+
+Engine::Engine(const std::string& bundle_dir, int device, bool verify_sha256) : device_(device) {
+  int n = 0;
+  check(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (device < 0 || device >= n) throw std::runtime_error("device id out of range");
+  check(cudaSetDevice(device), "cudaSetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (major != 10 || minor != 0) throw std::runtime_error("this build targets sm_100a (B200) only");
+  Mit2Bundle bundle(bundle_dir, verify_sha256);
+  load_weights(bundle, &w_);
+  check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  check(cudaMalloc(&d_status_, sizeof(unsigned int)), "cudaMalloc status");
+  check(cudaMemset(d_status_, 0, sizeof(unsigned int)), "cudaMemset status");
+}
+
+Engine::~Engine() {
+  cudaSetDevice(device_);
+  if (stream_) cudaStreamSynchronize(stream_);
+  for (auto& kv : works_) {
+    for (auto& g : kv.second->graphs) cudaGraphExecDestroy(g.second);
+    if (kv.second->arena) cudaFree(kv.second->arena);
+  }
+  for (auto& kv : step_tables_) cudaFree(kv.second);
+  for (auto& kv : t_tables_) cudaFree(kv.second);
+  if (d_status_) cudaFree(d_status_);
+  if (stream_) cudaStreamDestroy(stream_);
+  free_weights(&w_);
+}
+
+unsigned int Engine::read_status() {
+  unsigned int v = 0;
+  check(cudaMemcpyAsync(&v, d_status_, sizeof(v), cudaMemcpyDeviceToHost, stream_), "status read");
+  check(cudaStreamSynchronize(stream_), "status sync");
+  return v;
+}
+
+void Engine::clear_status() { check(cudaMemsetAsync(d_status_, 0, sizeof(unsigned int), stream_), "status clear"); }
+
+// Builds the t-conditioning tables for a list of timesteps: timestep MLPs
+// (run_timestep_embedder_cpu, runtime/impl/gpt.cpp:5404-5422), then the
+// per-layer AdaRMS projections, transformer.norm, the final AdaLN modulation
+// of SiLU(t1) and the WaveNet global condition of t2 (the per-`steps` table of
+// runtime/impl/dit_cfm_bigvgan.cpp:2949-3023).
+static float* build_tables(const DevWeights& w, const std::vector<float>& tv, cudaStream_t st) {
+  const int n = static_cast<int>(tv.size());
+  float *d_t = nullptr, *emb = nullptr, *hid = nullptr, *t1 = nullptr, *t2 = nullptr, *tab = nullptr;
+  auto ck = [](cudaError_t e) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string("cuda: table build: ") + cudaGetErrorString(e));
+  };
+  ck(cudaMalloc(&d_t, n * sizeof(float)));
+  ck(cudaMalloc(&emb, static_cast<size_t>(n) * 256 * sizeof(float)));
+  ck(cudaMalloc(&hid, static_cast<size_t>(n) * 512 * sizeof(float)));
+  ck(cudaMalloc(&t1, static_cast<size_t>(n) * 512 * sizeof(float)));
+  ck(cudaMalloc(&t2, static_cast<size_t>(n) * 512 * sizeof(float)));
+  ck(cudaMalloc(&tab, static_cast<size_t>(n) * kTcondPerStep * sizeof(float)));
+  ck(cudaMemcpyAsync(d_t, tv.data(), n * sizeof(float), cudaMemcpyHostToDevice, st));
+  for (int e = 0; e < 2; ++e) {
+    const TEmbW& te = e == 0 ? w.te1 : w.te2;
+    float* out = e == 0 ? t1 : t2;
+    ck(tembed_run(d_t, te.freqs, emb, n, 1000.0f, st));
+    ck(gemv_f16w_run(te.w0, te.b0, emb, 256, hid, 512, 512, 256, n, 0, st));
+    ck(silu_run(hid, static_cast<size_t>(n) * 512, st));
+    ck(gemv_f16w_run(te.w2, te.b2, hid, 512, out, 512, 512, 512, n, 0, st));
+  }
+  for (int l = 0; l < kLayers; ++l) {
+    ck(gemv_f16w_run(w.L[l].proj_attn, w.L[l].projb_attn, t1, 512, tab + kTabAttn + l * 1024, kTcondPerStep, 1024,
+                     512, n, 0, st));
+    ck(gemv_f16w_run(w.L[l].proj_ffn, w.L[l].projb_ffn, t1, 512, tab + kTabFfn + l * 1024, kTcondPerStep, 1024, 512,
+                     n, 0, st));
+  }
+  ck(gemv_f16w_run(w.proj_norm, w.projb_norm, t1, 512, tab + kTabNorm, kTcondPerStep, 1024, 512, n, 0, st));
+  ck(gemv_f16w_run(w.ada_w, w.ada_b, t1, 512, tab + kTabFinal, kTcondPerStep, 1024, 512, n, 1, st));
+  ck(gemv_f32w_run(w.wcond, w.bcond, t2, 512, tab + kTabWn, kTcondPerStep, 8192, 512, n, 0, st));
+  ck(cudaStreamSynchronize(st));
+  cudaFree(d_t);
+  cudaFree(emb);
+  cudaFree(hid);
+  cudaFree(t1);
+  cudaFree(t2);
+  return tab;
+}
+
+const float* Engine::tables_for_steps(int steps) {
+  auto it = step_tables_.find(steps);
+  if (it != step_tables_.end()) return it->second;
+  std::vector<float> tv(steps);
+  float t = 0.0f;
+  const float dt = 1.0f / static_cast<float>(steps);
+  for (int i = 0; i < steps; ++i) {
+    tv[i] = t;
+    t += dt;
+  }
+  float* tab = build_tables(w_, tv, stream_);
+  step_tables_[steps] = tab;
+  return tab;
+}
+
+const float* Engine::tables_for_t(float t) {
+  const uint32_t key = fbits(t);
+  auto it = t_tables_.find(key);
+  if (it != t_tables_.end()) return it->second;
+  float* tab = build_tables(w_, std::vector<float>{t}, stream_);
+  t_tables_[key] = tab;
+  return tab;
+}
+
+Work* Engine::work(int B, int T, int branches) {
+  auto key = std::make_tuple(B, T, branches);
+  auto it = works_.find(key);
+  if (it != works_.end()) return it->second.get();
+  auto w = std::make_unique<Work>();
+  w->B = B;
+  w->T = T;
+  w->br = branches;
+  w->S = B * branches;
+  w->R = w->S * T;
+  w->Rp = w->S * (T + 4);
+  const size_t R = w->R, BT = static_cast<size_t>(B) * T;
+  // Size pass then carve.
+  size_t bytes = 0;
+  auto sz = [&](size_t n, size_t es) { bytes += (n * es + 255) & ~size_t(255); };
+  sz(BT * 80, 4); sz(BT * 80, 4); sz(R * 80, 2); sz(BT * 80, 4); sz(BT * 512, 4); sz(static_cast<size_t>(B) * 192, 4); sz(B, 4);
+  sz(R, 4); sz(BT * 512, 2); sz(BT * 512, 2); sz(R * 784, 2); sz(R * 512, 4);
+  sz(R * 512, 4); sz(R * 512, 2); for (int i = 0; i < 6; ++i) sz(R * 512, 2); sz(R * 512, 2); sz(R * 1536, 2);
+  sz(R * 512, 2); sz(R * 512, 4); sz(R * 1536, 2);
+  sz(R * 512, 2); sz(static_cast<size_t>(w->Rp) * 512, 2); sz(R * 512, 4); sz(R * 512, 2); sz(R * 512, 4);
+  sz(R * 512, 4); sz(R * 512, 2); sz(R * 512, 2); sz(R * 80, 4); sz(static_cast<size_t>(T) * 32, 8);
+  check(cudaMalloc(&w->arena, bytes), "workspace cudaMalloc");
+  w->arena_bytes = bytes;
+  check(cudaMemset(w->arena, 0, bytes), "workspace memset");
+  uint8_t* cur = static_cast<uint8_t*>(w->arena);
+  w->X0 = carve<float>(cur, BT * 80);
+  w->X = carve<float>(cur, BT * 80);
+  w->XD = carve<__half>(cur, R * 80);
+  w->prompt_x = carve<float>(cur, BT * 80);
+  w->cond = carve<float>(cur, BT * 512);
+  w->style = carve<float>(cur, static_cast<size_t>(B) * 192);
+  w->plen = carve<int>(cur, B);
+  w->mask = carve<float>(cur, R);
+  w->cond16 = carve<__half>(cur, BT * 512);
+  w->cp16 = carve<__half>(cur, BT * 512);
+  w->U = carve<__half>(cur, R * 784);
+  w->base = carve<float>(cur, R * 512);
+  w->xres = carve<float>(cur, R * 512);
+  w->x16 = carve<__half>(cur, R * 512);
+  for (int i = 0; i < 6; ++i) w->skip16[i] = carve<__half>(cur, R * 512);
+  w->xn16 = carve<__half>(cur, R * 512);
+  w->qkv16 = carve<__half>(cur, R * 1536);
+  w->attn16 = carve<__half>(cur, R * 512);
+  w->h = carve<float>(cur, R * 512);
+  w->g16 = carve<__half>(cur, R * 1536);
+  w->ls16 = carve<__half>(cur, R * 512);
+  w->xp16 = carve<__half>(cur, static_cast<size_t>(w->Rp) * 512);
+  w->res = carve<float>(cur, R * 512);
+  w->gate16 = carve<__half>(cur, R * 512);
+  w->wacc = carve<float>(cur, R * 512);
+  w->fin = carve<float>(cur, R * 512);
+  w->fn16 = carve<__half>(cur, R * 512);
+  w->fh16 = carve<__half>(cur, R * 512);
+  w->vel = carve<float>(cur, R * 80);
+  w->rope = carve<float2>(cur, static_cast<size_t>(T) * 32);
+  // RoPE table with the reference's float arithmetic (apply_rope_inplace,
+  // runtime/impl/tokenizer_tests.cpp:4266-4281).
+  std::vector<float2> rope(static_cast<size_t>(T) * 32);
+  for (int t = 0; t < T; ++t) {
+    for (int p = 0; p < 32; ++p) {
+      const float theta = static_cast<float>(t) / std::pow(10000.0f, static_cast<float>(p * 2) / 64.0f);
+      rope[static_cast<size_t>(t) * 32 + p] = make_float2(std::cos(theta), std::sin(theta));
+    }
+  }
+  check(cudaMemcpy(w->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope upload");
+  build_work_launches(w.get());
+  Work* raw = w.get();
+  works_[key] = std::move(w);
+  return raw;
+}
+
+void Engine::build_work_launches(Work* w) {
+  const int R = w->R, BT = w->B * w->T;
+  const Operand none{};
+  auto act = [](const __half* p, int cols, int rows) { return Operand{p, cols, rows, cols}; };
+  auto wt = [](const __half* p, int cols, int rows) { return Operand{p, cols, rows, cols}; };
+  auto common = [&](GemmLaunch& g) {
+    g.args.seq_T = w->T;
+    g.args.rope = w->rope;
+    g.args.row_mask = w->mask;
+    g.args.status = d_status_;
+  };
+  // Step-invariant: cond projection (conditional rows only) and merge base.
+  w->g_cp = make_gemm(act(w->cond16, 512, BT), none, wt(w_.wcp, 512, 512), BT, 512, 512, kAPlain, 0, 0, 128, kEpiF16);
+  w->g_cp.args.bias = w_.bcp;
+  w->g_cp.args.out16 = w->cp16;
+  w->g_cp.args.ld16 = 512;
+  w->g_base = make_gemm(act(w->U, 784, R), none, wt(w_.wrest, 784, 512), R, 512, 784, kAPlain, 0, 0, 128, kEpiF32);
+  w->g_base.args.bias = w_.bm;
+  w->g_base.args.out32 = w->base;
+  w->g_base.args.ld32 = 512;
+  // Per step: x slice of the merge + base.
+  w->g_merge = make_gemm(act(w->XD, 80, R), none, wt(w_.wx, 80, 512), R, 512, 80, kAPlain, 0, 0, 128, kEpiF32);
+  w->g_merge.args.resid32 = w->base;
+  w->g_merge.args.ldr = 512;
+  w->g_merge.args.out32 = w->xres;
+  w->g_merge.args.ld32 = 512;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerW& L = w_.L[l];
+    if (l > kLayers / 2) {
+      GemmLaunch& g = w->g_skip[l];
+      g = make_gemm(act(w->x16, 512, R), act(w->skip16[kLayers - 1 - l], 512, R), wt(L.wskip, 1024, 512), R, 512,
+                    1024, kASplit, 8, 0, 128, kEpiF32);
+      g.args.bias = L.bskip;
+      g.args.out32 = w->xres;
+      g.args.ld32 = 512;
+    }
+    w->g_qkv[l] = make_gemm(act(w->xn16, 512, R), none, wt(L.wqkv, 512, 1536), R, 1536, 512, kAPlain, 0, 0, 128, kEpiQKV);
+    w->g_qkv[l].args.out16 = w->qkv16;
+    w->g_qkv[l].args.ld16 = 1536;
+    w->g_wo[l] = make_gemm(act(w->attn16, 512, R), none, wt(L.wo, 512, 512), R, 512, 512, kAPlain, 0, 0, 128, kEpiF32);
+    w->g_wo[l].args.resid32 = w->xres;
+    w->g_wo[l].args.ldr = 512;
+    w->g_wo[l].args.out32 = w->h;
+    w->g_wo[l].args.ld32 = 512;
+    w->g_w13[l] = make_gemm(act(w->xn16, 512, R), none, wt(L.w13, 512, 3072), R, 3072, 512, kAPlain, 0, 0, 256, kEpiSwiGLU);
+    w->g_w13[l].args.out16 = w->g16;
+    w->g_w13[l].args.ld16 = 1536;
+    w->g_w2[l] = make_gemm(act(w->g16, 1536, R), none, wt(L.w2, 1536, 512), R, 512, 1536, kAPlain, 0, 0, 128, kEpiF32);
+    w->g_w2[l].args.resid32 = w->h;
+    w->g_w2[l].args.ldr = 512;
+    w->g_w2[l].args.out32 = w->xres;
+    w->g_w2[l].args.ld32 = 512;
+    if (l < kLayers / 2) {
+      w->g_w2[l].args.out16 = w->skip16[l];
+      w->g_w2[l].args.ld16 = 512;
+    } else if (l < kLayers - 1) {
+      w->g_w2[l].args.out16 = w->x16;
+      w->g_w2[l].args.ld16 = 512;
+    }
+  }
+  w->g_sl = make_gemm(act(w->xn16, 512, R), act(w->XD, 80, R), wt(w_.wsl, 592, 512), R, 512, 640, kASplit, 8, 0, 128,
+                      kEpiF16);
+  w->g_sl.args.bias = w_.bsl;
+  w->g_sl.args.out16 = w->ls16;
+  w->g_sl.args.ld16 = 512;
+  w->g_c1res = make_gemm(act(w->ls16, 512, R), none, wt(w_.wc1res, 512, 1024), R, 1024, 512, kAPlain, 0, 0, 128,
+                         kEpiConv1Res);
+  w->g_c1res.args.bias = w_.bc1res;
+  w->g_c1res.args.wn_xp = w->xp16;
+  w->g_c1res.args.out32 = w->res;
+  w->g_c1res.args.ld32 = 512;
+  for (int l = 0; l < kWnLayers; ++l) {
+    w->g_in[l] = make_gemm(act(w->xp16, 512, w->Rp), none, wt(w_.win[l], 2560, 1024), w->Rp, 1024, 2560, kAConv5, 0, 8,
+                           128, kEpiWnGate);
+    w->g_in[l].args.bias = w_.bin[l];
+    w->g_in[l].args.out16 = w->gate16;
+    w->g_in[l].args.ld16 = 512;
+    if (l < kWnLayers - 1) {
+      w->g_rs[l] = make_gemm(act(w->gate16, 512, R), none, wt(w_.wrs[l], 512, 1024), R, 1024, 512, kAPlain, 0, 0, 128,
+                             kEpiWnResSkip);
+      w->g_rs[l].args.wn_first = l == 0 ? 1 : 0;
+    } else {
+      w->g_rs[l] = make_gemm(act(w->gate16, 512, R), none, wt(w_.wrs[l], 512, 512), R, 512, 512, kAPlain, 0, 0, 128,
+                             kEpiWnLast);
+      w->g_rs[l].args.out32 = w->fin;
+      w->g_rs[l].args.ld32 = 512;
+      w->g_rs[l].args.wn_res = w->res;
+    }
+    w->g_rs[l].args.bias = w_.brs[l];
+    w->g_rs[l].args.wn_xp = w->xp16;
+    w->g_rs[l].args.wn_acc = w->wacc;
+  }
+  w->g_fin = make_gemm(act(w->fn16, 512, R), none, wt(w_.wfin, 512, 512), R, 512, 512, kAPlain, 0, 0, 128, kEpiF16);
+  w->g_fin.args.bias = w_.bfin;
+  w->g_fin.args.out16 = w->fh16;
+  w->g_fin.args.ld16 = 512;
+  w->g_c2 = make_gemm(act(w->fh16, 512, R), none, wt(w_.wc2, 512, 80), R, 80, 512, kAPlain, 0, 0, 80, kEpiF32);
+  w->g_c2.args.bias = w_.bc2;
+  w->g_c2.args.out32 = w->vel;
+  w->g_c2.args.ld32 = 80;
+  GemmLaunch* all[] = {&w->g_cp, &w->g_base, &w->g_merge, &w->g_sl, &w->g_c1res, &w->g_fin, &w->g_c2};
+  for (GemmLaunch* g : all) common(*g);
+  for (int l = 0; l < kLayers; ++l) {
+    common(w->g_qkv[l]);
+    common(w->g_wo[l]);
+    common(w->g_w13[l]);
+    common(w->g_w2[l]);
+    common(w->g_skip[l]);
+  }
+  for (int l = 0; l < kWnLayers; ++l) {
+    common(w->g_in[l]);
+    common(w->g_rs[l]);
+  }
+}
+
+void Engine::enqueue_prep(Work* w) {
+  const size_t BT = static_cast<size_t>(w->B) * w->T;
+  check(to_half_run(w->cond, w->cond16, BT * 512, stream_), "cond to f16");
+  check(gemm_run(w->g_cp, stream_), "cond_projection gemm");
+  check(merge_input_run(w->prompt_x, w->cp16, w_.bcp, w->style, w->U, w->B, w->T, w->br, stream_), "merge input");
+  check(gemm_run(w->g_base, stream_), "merge base gemm");
+}
+
+namespace {
+
+// Event-bracketed launch recorder used by profile_step.
+struct Prof {
+  std::vector<KernelTiming>* out;
+  cudaStream_t st;
+  std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> evs;
+  std::vector<std::pair<double, double>> work;  // flops, bytes
+  template <typename F>
+  void run(const std::string& name, double flops, double bytes, F&& f) {
+    if (!out) {
+      f();
+      return;
+    }
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, st);
+    f();
+    cudaEventRecord(b, st);
+    evs.push_back({name, {a, b}});
+    work.push_back({flops, bytes});
+  }
+  void finish() {
+    if (!out) return;
+    cudaStreamSynchronize(st);
+    for (size_t i = 0; i < evs.size(); ++i) {
+      float ms = 0.0f;
+      cudaEventElapsedTime(&ms, evs[i].second.first, evs[i].second.second);
+      KernelTiming* kt = nullptr;
+      for (auto& k : *out)
+        if (k.name == evs[i].first) kt = &k;
+      if (!kt) {
+        out->push_back(KernelTiming{evs[i].first});
+        kt = &out->back();
+      }
+      kt->launches += 1;
+      kt->ms += ms;
+      kt->flops += work[i].first;
+      kt->bytes += work[i].second;
+      cudaEventDestroy(evs[i].second.first);
+      cudaEventDestroy(evs[i].second.second);
+    }
+  }
+};
+
+}  // namespace
+
+void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool do_update,
+                          std::vector<KernelTiming>* prof) {
+  const double R = w->R, T = w->T, S = w->S;
+  Prof P{prof, stream_, {}, {}};
+  auto G = [&](const char* name, const GemmLaunch& g, double K) {
+    const double rows = g.args.a_mode == kAConv5 ? R : static_cast<double>(g.args.M);
+    const double flops = 2.0 * rows * g.args.N * K;
+    P.run(name, flops, 0.0, [&] { check(gemm_run(g, stream_), name); });
+  };
+  G("gemm", w->g_merge, 80);
+  for (int l = 0; l < kLayers; ++l) {
+    if (l > kLayers / 2) G("gemm", w->g_skip[l], 1024);
+    P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
+      check(adarms_run(w->xres, w->R, tab + kTabAttn + l * 1024, w_.L[l].g_attn, w->xn16, stream_), "adarms");
+    });
+    G("gemm", w->g_qkv[l], 512);
+    P.run("attention", S * 4.0 * T * T * 512.0, R * (1536 + 512) * 2.0,
+          [&] { check(attention_run(w->qkv16, w->mask, w->attn16, w->S, w->T, stream_), "attention"); });
+    G("gemm", w->g_wo[l], 512);
+    P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
+      check(adarms_run(w->h, w->R, tab + kTabFfn + l * 1024, w_.L[l].g_ffn, w->xn16, stream_), "adarms");
+    });
+    G("gemm", w->g_w13[l], 512);
+    G("gemm", w->g_w2[l], 1536);
+  }
+  P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
+    check(adarms_run(w->xres, w->R, tab + kTabNorm, w_.g_norm, w->xn16, stream_), "adarms");
+  });
+  G("gemm", w->g_sl, 592);
+  G("gemm", w->g_c1res, 512);
+  for (int l = 0; l < kWnLayers; ++l) {
+    GemmLaunch gi = w->g_in[l];
+    gi.args.wn_cond = tab + kTabWn + l * 1024;
+    G("gemm", gi, 2560);
+    G("gemm", w->g_rs[l], 512);
+  }
+  P.run("adaln", 0.0, R * 512 * (4 + 2),
+        [&] { check(adaln_run(w->fin, w->R, tab + kTabFinal, w->fn16, stream_), "adaln"); });
+  G("gemm", w->g_fin, 512);
+  G("gemm", w->g_c2, 512);
+  if (do_update) {
+    P.run("euler", 0.0, static_cast<double>(w->B) * T * 80 * 4.0 * (w->br + 2), [&] {
+      check(euler_run(w->X, w->vel, w->XD, w->plen, w->B, w->T, w->br, dt, cfg, stream_), "euler");
+    });
+  }
+  P.finish();
+}
+
+void Engine::enqueue_estimator(Work* w, const float* tab) { enqueue_step(w, tab, 0.0f, 0.0f, false, nullptr); }
+
+void Engine::enqueue_sampler(Work* w, int steps, float cfg, bool use_graph) {
+  const float* tab = tables_for_steps(steps);
+  const float dt = 1.0f / static_cast<float>(steps);
+  auto body = [&] {
+    enqueue_prep(w);
+    check(euler_init_run(w->X0, w->X, w->XD, w->plen, w->B, w->T, w->br, stream_), "euler init");
+    for (int i = 0; i < steps; ++i) enqueue_step(w, tab + static_cast<size_t>(i) * kTcondPerStep, dt, cfg, true, nullptr);
+  };
+  if (!use_graph) {
+    body();
+    return;
+  }
+  const auto key = std::make_pair(steps, fbits(cfg));
+  auto it = w->graphs.find(key);
+  if (it == w->graphs.end()) {
+    cudaGraph_t graph = nullptr;
+    check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      body();
+    } catch (...) {
+      cudaStreamEndCapture(stream_, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    check(cudaStreamEndCapture(stream_, &graph), "end capture");
+    size_t nn = 0;
+    cudaGraphGetNodes(graph, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    if (nn) cudaGraphGetNodes(graph, nodes.data(), &nn);
+    int kernels = 0;
+    for (auto nd : nodes) {
+      cudaGraphNodeType ty;
+      if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++kernels;
+    }
+    w->graph_kernels[key] = kernels;
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    check(e, "graph instantiate");
+    it = w->graphs.emplace(key, exec).first;
+  }
+  check(cudaGraphLaunch(it->second, stream_), "graph launch");
+}
+
+std::vector<KernelTiming> Engine::profile_step(Work* w, int steps, float cfg, int reps) {
+  const float* tab = tables_for_steps(steps);
+  const float dt = 1.0f / static_cast<float>(steps);
+  std::vector<KernelTiming> out;
+  enqueue_prep(w);
+  check(euler_init_run(w->X0, w->X, w->XD, w->plen, w->B, w->T, w->br, stream_), "euler init");
+  for (int r = 0; r < reps; ++r) enqueue_step(w, tab, dt, cfg, true, &out);
+  return out;
+}
+
+}  // namespace itts

@@ -1,0 +1,76 @@
+// tcgen05 GEMM for the DiT-CFM estimator: C[M,N] = A[M,K] * B[N,K]^T with f16
+// operands staged by TMA (128-byte swizzle, no multicast), fp32 accumulation
+// in TMEM and fused epilogues that read the accumulator with tcgen05.ld.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace itts {
+
+// How the A operand's k-blocks (64 columns each) are fetched.
+enum GemmAMode : int {
+  kAPlain = 0,  // every k-block from A0
+  kASplit = 1,  // k-blocks [0, kb_split) from A0, the rest from A1 (a concat without a buffer)
+  kAConv5 = 2,  // implicit k=5 conv over a reflect-padded row space: k-block kb reads A0 at
+                // column (kb % kb_per_tap)*64 and row (m0 + kb / kb_per_tap - 2)
+};
+
+// Fused epilogues. "Paired" epilogues expect B rows interleaved in 64-row
+// groups [a(64) | b(64)] so each 128-column slab holds matching a/b channels.
+enum GemmEpi : int {
+  kEpiF16 = 0,        // out16 = acc + bias
+  kEpiF32 = 1,        // out32 = acc + bias (+ resid32); optional f16 copy to out16
+  kEpiQKV = 2,        // RoPE on q,k columns, q scaled by 1/sqrt(64), -> out16
+  kEpiSwiGLU = 3,     // paired: silu(a) * b -> out16 (N/2 channels)
+  kEpiWnGate = 4,     // paired, padded row space: tanh(a + ca) * sigmoid(b + cb) -> out16 (compact rows)
+  kEpiWnResSkip = 5,  // paired: xp = (xp + a) * mask (with reflect halos); acc = (first ? 0 : acc) + b
+  kEpiWnLast = 6,     // out32 = (acc + a) * mask + res
+  kEpiConv1Res = 7,   // columns < 512 -> xp (f16, reflect halos); columns >= 512 -> out32 (res)
+};
+
+struct GemmArgs {
+  int M;        // rows of the A row space (compact R, or padded S*(T+4) in conv mode)
+  int N;        // columns of the product (rows of B)
+  int num_kb;   // k-blocks of 64
+  int a_mode;
+  int kb_split;
+  int kb_per_tap;
+  int epi;
+  const float* bias;      // [N] in B-row order, or null
+  float* out32;
+  int ld32;
+  __half* out16;
+  int ld16;
+  const float* resid32;
+  int ldr;
+  int seq_T;              // rows per sequence (T)
+  const float2* rope;     // [T][32] (cos, sin) of t / 10000^(2p/64)
+  const float* wn_cond;   // [1024] WaveNet global condition of this layer: a-part | b-part
+  const float* row_mask;  // [R] 0/1 per compact row
+  float* wn_acc;          // [R,512] skip accumulator
+  const float* wn_res;    // [R,512] residual projection
+  __half* wn_xp;          // [S*(T+4),512] reflect-padded WaveNet activations
+  int wn_first;
+  int pad_rows;           // kEpiF32 only: A rows are the padded S*(T+4) space; write compact rows
+  unsigned int* status;   // device status word
+};
+
+struct GemmLaunch {
+  CUtensorMap tmA0;
+  CUtensorMap tmA1;
+  CUtensorMap tmB;
+  GemmArgs args;
+  int bn;
+  int stages;
+};
+
+// Host helpers (gemm.cu).
+bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
+                   uint32_t box_rows);
+cudaError_t gemm_run(const GemmLaunch& g, cudaStream_t stream);
+size_t gemm_smem_bytes(int bn, int stages);
+
+}  // namespace itts

@@ -1,0 +1,242 @@
+"""ctypes binding of libitts_cfm.so (include/itts_cfm.h) for Python callers.
+
+The library is the product; this module only marshals numpy arrays and raises
+``IttsError`` for non-zero status codes. It never falls back to another
+implementation: if the library cannot be loaded, ``load()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "lib" / "libitts_cfm.so"
+
+ITTS_OK = 0
+ITTS_EINVAL_SHAPE = -1
+ITTS_EBUNDLE = -2
+ITTS_ECUDA = -3
+ITTS_ETIMEOUT = -4
+ITTS_ECAP = -5
+ITTS_ENODEV = -6
+ITTS_CREATE_VERIFY_SHA256 = 0x1
+
+EXPORTED = [
+    "itts_cfm_create", "itts_cfm_create_ex", "itts_cfm_destroy", "itts_cfm_last_error", "itts_cfm_create_error",
+    "itts_cfm_strerror", "itts_cfm_run", "itts_cfm_run_batch", "itts_cfm_bucket_len", "itts_cfm_run_padded",
+    "itts_cfm_estimator", "itts_cfm_stage_padded", "itts_cfm_launch", "itts_cfm_sync", "itts_cfm_fetch",
+    "itts_cfm_stream", "itts_cfm_launch_kernels", "itts_cfm_profile_step", "itts_cfm_step_flops", "itts_op_gemm", "itts_op_conv5",
+    "itts_op_attention", "itts_op_adarms",
+]
+
+
+class IttsError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"itts error {code}: {msg}")
+        self.code = code
+
+
+class Utt(C.Structure):
+    _fields_ = [
+        ("noise", C.c_void_p), ("prompt", C.c_void_p), ("cond", C.c_void_p), ("style", C.c_void_p),
+        ("T", C.c_uint32), ("P", C.c_uint32), ("out_mel", C.c_void_p),
+    ]
+
+
+class KernelStat(C.Structure):
+    _fields_ = [("name", C.c_char * 32), ("launches", C.c_int32), ("ms", C.c_double), ("flops", C.c_double),
+                ("bytes", C.c_double)]
+
+
+_lib = None
+
+
+def load(path: str | Path | None = None) -> C.CDLL:
+    """Load the C-ABI library (raises OSError if it is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    lib = C.CDLL(str(p))
+    vp, u32, i32, f32, f64 = C.c_void_p, C.c_uint32, C.c_int, C.c_float, C.c_double
+    sig = {
+        "itts_cfm_create": (i32, [C.c_char_p, i32, C.POINTER(vp)]),
+        "itts_cfm_create_ex": (i32, [C.c_char_p, i32, u32, C.POINTER(vp)]),
+        "itts_cfm_destroy": (None, [vp]),
+        "itts_cfm_last_error": (C.c_char_p, [vp]),
+        "itts_cfm_create_error": (C.c_char_p, []),
+        "itts_cfm_strerror": (C.c_char_p, [i32]),
+        "itts_cfm_run": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, f32, vp]),
+        "itts_cfm_run_batch": (i32, [vp, u32, vp, u32, f32]),
+        "itts_cfm_bucket_len": (u32, [u32]),
+        "itts_cfm_run_padded": (i32, [vp, u32, u32, vp, vp, vp, vp, vp, vp, u32, f32, vp]),
+        "itts_cfm_estimator": (i32, [vp, u32, u32, u32, vp, vp, vp, vp, vp, f32, vp]),
+        "itts_cfm_stage_padded": (i32, [vp, u32, u32, vp, vp, vp, vp, vp, vp, u32, f32]),
+        "itts_cfm_launch": (i32, [vp]),
+        "itts_cfm_sync": (i32, [vp]),
+        "itts_cfm_fetch": (i32, [vp, vp]),
+        "itts_cfm_stream": (vp, [vp]),
+        "itts_cfm_launch_kernels": (i32, [vp]),
+        "itts_cfm_profile_step": (i32, [vp, i32, vp, i32, C.POINTER(i32)]),
+        "itts_cfm_step_flops": (f64, [u32, u32]),
+        "itts_op_gemm": (i32, [vp, vp, u32, vp, u32, u32, vp, u32, vp, vp, u32, u32, u32, u32, u32]),
+        "itts_op_conv5": (i32, [vp, vp, u32, u32, vp, vp, vp, u32]),
+        "itts_op_attention": (i32, [vp, vp, vp, vp, u32, u32]),
+        "itts_op_adarms": (i32, [vp, vp, u32, vp, vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+class Context:
+    """One engine context bound to one GPU (itts_cfm_create)."""
+
+    def __init__(self, bundle_dir: str | Path, device: int = 0, verify_sha256: bool = False):
+        self.lib = load()
+        h = C.c_void_p()
+        flags = ITTS_CREATE_VERIFY_SHA256 if verify_sha256 else 0
+        rc = self.lib.itts_cfm_create_ex(str(bundle_dir).encode(), int(device), flags, C.byref(h))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_cfm_create_error().decode())
+        self.h = h
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.itts_cfm_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int) -> None:
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_cfm_last_error(self.h).decode())
+
+    # ---- sampler ----
+    def run(self, noise, prompt, cond, style, steps: int, cfg_rate: float) -> np.ndarray:
+        noise, cond, style = _f32(noise), _f32(cond), _f32(style)
+        T = noise.shape[0]
+        prompt = _f32(prompt) if prompt is not None and len(prompt) else None
+        P = 0 if prompt is None else prompt.shape[0]
+        out = np.empty((T, 80), np.float32)
+        self._check(self.lib.itts_cfm_run(self.h, _ptr(noise), _ptr(prompt), _ptr(cond), _ptr(style), T, P, steps,
+                                          float(cfg_rate), _ptr(out)))
+        return out
+
+    def run_padded(self, valid_len, prompt_len, noise, prompt_x, cond, style, steps: int, cfg_rate: float):
+        noise, prompt_x, cond, style = _f32(noise), _f32(prompt_x), _f32(cond), _f32(style)
+        B, T = noise.shape[0], noise.shape[1]
+        vl = np.ascontiguousarray(valid_len, dtype=np.uint32)
+        pl = np.ascontiguousarray(prompt_len, dtype=np.uint32)
+        out = np.empty((B, T, 80), np.float32)
+        self._check(self.lib.itts_cfm_run_padded(self.h, B, T, _ptr(vl), _ptr(pl), _ptr(noise), _ptr(prompt_x),
+                                                 _ptr(cond), _ptr(style), steps, float(cfg_rate), _ptr(out)))
+        return out
+
+    def run_batch(self, utts: list[dict], steps: int, cfg_rate: float) -> list[np.ndarray]:
+        keep = []
+        arr = (Utt * len(utts))()
+        outs = []
+        for i, u in enumerate(utts):
+            n, c, s = _f32(u["noise"]), _f32(u["cond"]), _f32(u["style"])
+            p = _f32(u["prompt"]) if u.get("prompt") is not None and len(u["prompt"]) else None
+            o = np.empty((n.shape[0], 80), np.float32)
+            keep += [n, c, s, p, o]
+            outs.append(o)
+            arr[i] = Utt(n.ctypes.data, None if p is None else p.ctypes.data, c.ctypes.data, s.ctypes.data,
+                         n.shape[0], 0 if p is None else p.shape[0], o.ctypes.data)
+        self._check(self.lib.itts_cfm_run_batch(self.h, len(utts), C.cast(arr, C.c_void_p), steps, float(cfg_rate)))
+        return outs
+
+    def estimator(self, x, prompt_x, cond, style, mask, t: float, branches: int = 2) -> np.ndarray:
+        """x, prompt_x [B,T,80]; cond [B,T,512]; style [B,192]; mask [B,T] -> vel [B,branches,T,80]."""
+        x, prompt_x, cond, style = _f32(x), _f32(prompt_x), _f32(cond), _f32(style)
+        mask = np.ascontiguousarray(mask, dtype=np.uint32)
+        B, T = x.shape[0], x.shape[1]
+        vel = np.empty((B, branches, T, 80), np.float32)
+        self._check(self.lib.itts_cfm_estimator(self.h, B, T, branches, _ptr(x), _ptr(prompt_x), _ptr(cond),
+                                                _ptr(style), _ptr(mask), float(t), _ptr(vel)))
+        return vel
+
+    # ---- staged (device-resident) ----
+    def stage_padded(self, valid_len, prompt_len, noise, prompt_x, cond, style, steps: int, cfg_rate: float):
+        noise, prompt_x, cond, style = _f32(noise), _f32(prompt_x), _f32(cond), _f32(style)
+        B, T = noise.shape[0], noise.shape[1]
+        vl = np.ascontiguousarray(valid_len, dtype=np.uint32)
+        pl = np.ascontiguousarray(prompt_len, dtype=np.uint32)
+        self._check(self.lib.itts_cfm_stage_padded(self.h, B, T, _ptr(vl), _ptr(pl), _ptr(noise), _ptr(prompt_x),
+                                                   _ptr(cond), _ptr(style), steps, float(cfg_rate)))
+        self._staged_shape = (B, T)
+
+    def launch(self) -> None:
+        self._check(self.lib.itts_cfm_launch(self.h))
+
+    def sync(self) -> None:
+        self._check(self.lib.itts_cfm_sync(self.h))
+
+    def fetch(self) -> np.ndarray:
+        B, T = self._staged_shape
+        out = np.empty((B, T, 80), np.float32)
+        self._check(self.lib.itts_cfm_fetch(self.h, _ptr(out)))
+        return out
+
+    def stream(self) -> int:
+        return int(self.lib.itts_cfm_stream(self.h) or 0)
+
+    def launch_kernels(self) -> int:
+        n = int(self.lib.itts_cfm_launch_kernels(self.h))
+        if n < 0:
+            raise IttsError(n, "no captured launch for the staged batch")
+        return n
+
+    def profile_step(self, reps: int = 1) -> list[dict]:
+        cap = 64
+        buf = (KernelStat * cap)()
+        n = C.c_int(0)
+        self._check(self.lib.itts_cfm_profile_step(self.h, reps, C.cast(buf, C.c_void_p), cap, C.byref(n)))
+        return [dict(name=buf[i].name.decode(), launches=buf[i].launches, ms=buf[i].ms, flops=buf[i].flops,
+                     bytes=buf[i].bytes) for i in range(n.value)]
+
+    # ---- kernel-level (device pointers as ints) ----
+    def op_gemm(self, a0, lda0, a1, lda1, k0, b, ldb, bias, c, ldc, M, N, K, bn=128) -> None:
+        self._check(self.lib.itts_op_gemm(self.h, a0, lda0, a1, lda1, k0, b, ldb, bias, c, ldc, M, N, K, bn))
+
+    def op_conv5(self, xp, S, T, w, bias, out, N) -> None:
+        self._check(self.lib.itts_op_conv5(self.h, xp, S, T, w, bias, out, N))
+
+    def op_attention(self, qkv, mask, out, S, T) -> None:
+        self._check(self.lib.itts_op_attention(self.h, qkv, mask, out, S, T))
+
+    def op_adarms(self, x, R, wb, gamma, y) -> None:
+        self._check(self.lib.itts_op_adarms(self.h, x, R, wb, gamma, y))
+
+
+def bucket_len(T: int) -> int:
+    return int(load().itts_cfm_bucket_len(T))
+
+
+def step_flops(S: int, T: int) -> float:
+    return float(load().itts_cfm_step_flops(S, T))

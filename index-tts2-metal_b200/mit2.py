@@ -1,0 +1,238 @@
+"""MIT2 weight bundles: writer, reader and the synthetic DiT estimator bundle.
+
+Format (the reference's native bundle, docs/native_bundle.md:1-80, writer
+metal_indextts2/bundle.py:98-144): ``weights.bin`` starts with b"MIT2", u32
+version 1, u32 alignment (4096); every tensor payload starts at an aligned
+offset. ``manifest.json`` lists name, shape, dtype, offset, nbytes and sha256
+per tensor.
+
+``make_dit_bundle`` writes every tensor the DiT-CFM estimator reads, under the
+reference's names (prefix ``s2mel.net.cfm.estimator.``), from a seeded
+``numpy.random.default_rng``:
+
+* ``init="baseline"`` — the benchmark configuration: f16 weights ~ N(0, 0.02),
+  RMSNorm gammas 1, timestep frequencies exp(-ln(10000) i / 128), weight-norm
+  pairs with g = ||v_row|| (so the folded weight equals v).
+* ``init="unit"`` — same tensors with fan-in scaled weights (std 1/sqrt(K))
+  and AdaRMS project_layer biases of 1 on the scale half, so every block
+  contributes O(1) to the output; used by parity tests so no sub-path hides
+  under rounding.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+import struct
+from pathlib import Path
+from typing import Iterable
+
+import numpy as np
+
+MAGIC = b"MIT2"
+VERSION = 1
+ALIGNMENT = 4096
+PREFIX = "s2mel.net.cfm.estimator."
+
+_DTYPES = {
+    np.dtype(np.float32): "f32",
+    np.dtype(np.float16): "f16",
+    np.dtype(np.int64): "i64",
+    np.dtype(np.int32): "i32",
+    np.dtype(np.uint32): "u32",
+    np.dtype(np.uint8): "u8",
+}
+_NP = {v: k for k, v in _DTYPES.items()}
+
+
+def write_bundle(out_dir: str | Path, tensors: Iterable[tuple[str, np.ndarray]], metadata: dict | None = None) -> dict:
+    """Write ``(name, array)`` pairs as an MIT2 bundle; returns the manifest."""
+    out = Path(out_dir)
+    out.mkdir(parents=True, exist_ok=True)
+    records = []
+    with (out / "weights.bin").open("wb") as fp:
+        fp.write(struct.pack("<4sII", MAGIC, VERSION, ALIGNMENT))
+        for name, arr in tensors:
+            arr = np.ascontiguousarray(arr)
+            if arr.dtype not in _DTYPES:
+                raise TypeError(f"unsupported dtype {arr.dtype} for {name}")
+            pos = fp.tell()
+            off = (pos + ALIGNMENT - 1) // ALIGNMENT * ALIGNMENT
+            fp.write(b"\0" * (off - pos))
+            payload = arr.tobytes()
+            fp.write(payload)
+            records.append(
+                {
+                    "name": name,
+                    "shape": [int(d) for d in arr.shape],
+                    "dtype": _DTYPES[arr.dtype],
+                    "offset": off,
+                    "nbytes": len(payload),
+                    "sha256": hashlib.sha256(payload).hexdigest(),
+                    "layout": "row_major",
+                    "component": "s2mel",
+                }
+            )
+    manifest = {
+        "format": "MIT2",
+        "version": VERSION,
+        "endianness": "little",
+        "alignment": ALIGNMENT,
+        "weights_file": "weights.bin",
+        "metadata": metadata or {},
+        "tensors": records,
+    }
+    (out / "manifest.json").write_text(json.dumps(manifest, indent=2, sort_keys=True), encoding="utf-8")
+    return manifest
+
+
+def read_bundle(bundle_dir: str | Path, names: Iterable[str] | None = None, verify: bool = False) -> dict[str, np.ndarray]:
+    """Read tensors (all, or ``names``) as numpy arrays in their stored dtype."""
+    d = Path(bundle_dir)
+    man = json.loads((d / "manifest.json").read_text(encoding="utf-8"))
+    want = set(names) if names is not None else None
+    out = {}
+    raw = np.memmap(d / man.get("weights_file", "weights.bin"), dtype=np.uint8, mode="r")
+    for rec in man["tensors"]:
+        if want is not None and rec["name"] not in want:
+            continue
+        buf = raw[rec["offset"] : rec["offset"] + rec["nbytes"]]
+        if verify and hashlib.sha256(buf.tobytes()).hexdigest() != rec["sha256"]:
+            raise ValueError(f"checksum mismatch for {rec['name']}")
+        out[rec["name"]] = np.frombuffer(buf.tobytes(), dtype=_NP[rec["dtype"]]).reshape(rec["shape"])
+    return out
+
+
+def dit_tensor_specs() -> list[tuple[str, tuple[int, ...], str]]:
+    """(name without prefix, shape, kind) of every estimator tensor.
+
+    kind: "w" weight (fan-in = last dims), "b" bias, "gamma" norm weight,
+    "freqs", "wg" weight-norm g, "wv" weight-norm v, "proj_b" AdaRMS project bias.
+    """
+    s: list[tuple[str, tuple[int, ...], str]] = []
+    s += [("cond_projection.weight", (512, 512), "w"), ("cond_projection.bias", (512,), "b")]
+    s += [("cond_x_merge_linear.weight", (512, 864), "w"), ("cond_x_merge_linear.bias", (512,), "b")]
+    for te in ("t_embedder", "t_embedder2"):
+        s += [
+            (f"{te}.freqs", (128,), "freqs"),
+            (f"{te}.mlp.0.weight", (512, 256), "w"),
+            (f"{te}.mlp.0.bias", (512,), "b"),
+            (f"{te}.mlp.2.weight", (512, 512), "w"),
+            (f"{te}.mlp.2.bias", (512,), "b"),
+        ]
+    for l in range(13):
+        p = f"transformer.layers.{l}."
+        for nm in ("attention_norm", "ffn_norm"):
+            s += [
+                (f"{p}{nm}.norm.weight", (512,), "gamma"),
+                (f"{p}{nm}.project_layer.weight", (1024, 512), "w"),
+                (f"{p}{nm}.project_layer.bias", (1024,), "proj_b"),
+            ]
+        s += [
+            (f"{p}attention.wqkv.weight", (1536, 512), "w"),
+            (f"{p}attention.wo.weight", (512, 512), "w"),
+            (f"{p}feed_forward.w1.weight", (1536, 512), "w"),
+            (f"{p}feed_forward.w2.weight", (512, 1536), "w"),
+            (f"{p}feed_forward.w3.weight", (1536, 512), "w"),
+        ]
+        if l > 6:
+            s += [(f"{p}skip_in_linear.weight", (512, 1024), "w"), (f"{p}skip_in_linear.bias", (512,), "b")]
+    s += [
+        ("transformer.norm.norm.weight", (512,), "gamma"),
+        ("transformer.norm.project_layer.weight", (1024, 512), "w"),
+        ("transformer.norm.project_layer.bias", (1024,), "proj_b"),
+        ("skip_linear.weight", (512, 592), "w"),
+        ("skip_linear.bias", (512,), "b"),
+        ("conv1.weight", (512, 512, 1), "w"),
+        ("conv1.bias", (512,), "b"),
+        ("res_projection.weight", (512, 512), "w"),
+        ("res_projection.bias", (512,), "b"),
+        ("wavenet.cond_layer.conv.conv.weight_g", (8192, 1, 1), "wg"),
+        ("wavenet.cond_layer.conv.conv.weight_v", (8192, 512, 1), "wv"),
+        ("wavenet.cond_layer.conv.conv.bias", (8192,), "b"),
+    ]
+    for l in range(8):
+        s += [
+            (f"wavenet.in_layers.{l}.conv.conv.weight_g", (1024, 1, 1), "wg"),
+            (f"wavenet.in_layers.{l}.conv.conv.weight_v", (1024, 512, 5), "wv"),
+            (f"wavenet.in_layers.{l}.conv.conv.bias", (1024,), "b"),
+        ]
+        rs = 1024 if l < 7 else 512
+        s += [
+            (f"wavenet.res_skip_layers.{l}.conv.conv.weight_g", (rs, 1, 1), "wg"),
+            (f"wavenet.res_skip_layers.{l}.conv.conv.weight_v", (rs, 512, 1), "wv"),
+            (f"wavenet.res_skip_layers.{l}.conv.conv.bias", (rs,), "b"),
+        ]
+    s += [
+        ("final_layer.adaLN_modulation.1.weight", (1024, 512), "w"),
+        ("final_layer.adaLN_modulation.1.bias", (1024,), "b"),
+        ("final_layer.linear.weight_g", (512, 1), "wg"),
+        ("final_layer.linear.weight_v", (512, 512), "wv"),
+        ("final_layer.linear.bias", (512,), "b"),
+        ("conv2.weight", (80, 512, 1), "w"),
+        ("conv2.bias", (80,), "b"),
+    ]
+    return s
+
+
+def make_dit_tensors(seed: int, init: str = "baseline") -> list[tuple[str, np.ndarray]]:
+    """Generate the estimator tensors (f16 except freqs, f32) deterministically."""
+    if init not in ("baseline", "unit"):
+        raise ValueError("init must be 'baseline' or 'unit'")
+    rng = np.random.default_rng(seed)
+    out: list[tuple[str, np.ndarray]] = []
+    pending_v: dict[str, np.ndarray] = {}
+    specs = dit_tensor_specs()
+    # Draw weight_v before weight_g so g can be set to ||v_row||.
+    for name, shape, kind in specs:
+        if kind == "wv":
+            fan_in = int(np.prod(shape[1:]))
+            std = 0.02 if init == "baseline" else 1.0 / math.sqrt(fan_in)
+            pending_v[name] = (rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float16)
+    for name, shape, kind in specs:
+        full = PREFIX + name
+        if kind == "w":
+            fan_in = int(np.prod(shape[1:]))
+            std = 0.02 if init == "baseline" else 1.0 / math.sqrt(fan_in)
+            arr = (rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float16)
+        elif kind == "b":
+            std = 0.02 if init == "baseline" else 0.1
+            arr = (rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float16)
+        elif kind == "proj_b":
+            std = 0.02 if init == "baseline" else 0.1
+            b = rng.standard_normal(shape, dtype=np.float32) * std
+            if init == "unit":
+                b[:512] += 1.0  # AdaRMS scale half centred on 1
+            arr = b.astype(np.float16)
+        elif kind == "gamma":
+            arr = np.ones(shape, dtype=np.float16)
+        elif kind == "freqs":
+            i = np.arange(128, dtype=np.float32)
+            arr = np.exp(-math.log(10000.0) * i / 128.0).astype(np.float32)
+        elif kind == "wv":
+            arr = pending_v[name]
+        elif kind == "wg":
+            v = pending_v[name[: -len("weight_g")] + "weight_v"].astype(np.float32)
+            norms = np.sqrt((v.reshape(v.shape[0], -1) ** 2).sum(axis=1))
+            arr = norms.reshape(shape).astype(np.float16)
+        else:
+            raise AssertionError(kind)
+        out.append((full, arr))
+    return out
+
+
+def make_dit_bundle(out_dir: str | Path, seed: int = 0, init: str = "baseline") -> Path:
+    """Write the synthetic estimator bundle; skips work when an identical one exists."""
+    out = Path(out_dir)
+    stamp = out / ".synthetic"
+    key = f"seed={seed} init={init} v1"
+    if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():
+        return out
+    write_bundle(out, make_dit_tensors(seed, init), metadata={"synthetic": True, "seed": seed, "init": init})
+    stamp.write_text(key)
+    return out
+
+
+def bundle_f32(bundle_dir: str | Path) -> dict[str, np.ndarray]:
+    """All estimator tensors decoded to contiguous float32 (f16 decoding is exact)."""
+    return {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in read_bundle(bundle_dir).items()}

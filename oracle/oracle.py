@@ -1,0 +1,214 @@
+"""TEST INFRASTRUCTURE — Python access to the CPU checkers.
+
+* ``PortOracle``: the C restatement in oracle/dit_oracle.c (always available;
+  built by oracle/build_ref.py into oracle/lib/).
+* ``RefOracle``: the reference's own CPU functions compiled into
+  oracle/_ref/libref_cfm.so (available where that library was built).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use
+this module, always as the checker or the timed CPU baseline.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+ORACLE = Path(__file__).resolve().parent
+PORT_LIB = ORACLE / "lib" / "libdit_oracle.so"
+REF_LIB = ORACLE / "_ref" / "libref_cfm.so"
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _u32(a):
+    return np.ascontiguousarray(a, dtype=np.uint32)
+
+
+def _p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class PortOracle:
+    """fp32 CPU restatement of the reference's estimator and Euler sampler."""
+
+    def __init__(self, tensors: dict[str, np.ndarray], lib_path: Path = PORT_LIB):
+        self.lib = C.CDLL(str(lib_path))
+        L = self.lib
+        L.orc_model_new.restype = C.c_void_p
+        L.orc_model_free.argtypes = [C.c_void_p]
+        L.orc_model_set.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]
+        L.orc_estimator.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
+                                    C.c_int, C.c_void_p]
+        L.orc_euler.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                C.c_int, C.c_int, C.c_float, C.c_void_p]
+        L.orc_attention_layer.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.orc_wavenet.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.orc_timestep_embed.argtypes = [C.c_void_p, C.c_float, C.c_char_p, C.c_void_p]
+        L.orc_noise.argtypes = [C.c_int, C.c_int, C.c_uint64, C.c_float, C.c_void_p]
+        L.orc_threads.restype = C.c_int
+        L.orc_set_threads.argtypes = [C.c_int]
+        self._keep = {k: _f32(v) for k, v in tensors.items()}
+        self.m = C.c_void_p(L.orc_model_new())
+        for k, v in self._keep.items():
+            L.orc_model_set(self.m, k.encode(), _p(v), v.size)
+
+    def __del__(self):
+        try:
+            self.lib.orc_model_free(self.m)
+        except Exception:
+            pass
+
+    def threads(self) -> int:
+        return int(self.lib.orc_threads())
+
+    def set_threads(self, n: int) -> None:
+        self.lib.orc_set_threads(int(n))
+
+    def estimator(self, x, prompt_x, cond, style, t, mask=None):
+        x, prompt_x, cond, style = _f32(x), _f32(prompt_x), _f32(cond), _f32(style)
+        T = x.shape[0]
+        mask = _u32(np.ones(T) if mask is None else mask)
+        v = np.empty((T, 80), np.float32)
+        rc = self.lib.orc_estimator(self.m, _p(x), _p(prompt_x), _p(cond), _p(style), float(t), _p(mask), T, _p(v))
+        if rc:
+            raise RuntimeError(f"oracle estimator failed (line {self.lib.orc_last_error()})")
+        return v
+
+    def euler(self, noise, prompt_x, cond, style, P, steps, cfg, mask=None, trace=False):
+        x = _f32(noise).copy()
+        prompt_x, cond, style = _f32(prompt_x), _f32(cond), _f32(style)
+        T = x.shape[0]
+        mask = _u32(np.ones(T) if mask is None else mask)
+        tr = np.empty((steps, T, 80), np.float32) if trace else None
+        rc = self.lib.orc_euler(self.m, _p(x), _p(prompt_x), _p(cond), _p(style), _p(mask), T, int(P), int(steps),
+                                float(cfg), None if tr is None else _p(tr))
+        if rc:
+            raise RuntimeError(f"oracle euler failed (line {self.lib.orc_last_error()})")
+        return (x, tr) if trace else x
+
+    def attention_layer(self, x, mask, layer):
+        x = _f32(x)
+        T = x.shape[0]
+        out = np.empty((T, 512), np.float32)
+        rc = self.lib.orc_attention_layer(self.m, _p(x), _p(_u32(mask)), T, layer, _p(out))
+        if rc:
+            raise RuntimeError("oracle attention failed")
+        return out
+
+    def wavenet(self, x, g, mask):
+        x, g = _f32(x), _f32(g)
+        T = x.shape[0]
+        out = np.empty((T, 512), np.float32)
+        rc = self.lib.orc_wavenet(self.m, _p(x), _p(g), _p(_u32(mask)), T, _p(out))
+        if rc:
+            raise RuntimeError("oracle wavenet failed")
+        return out
+
+    def timestep_embed(self, t, which=0):
+        out = np.empty(512, np.float32)
+        rc = self.lib.orc_timestep_embed(self.m, float(t), b"t_embedder" if which == 0 else b"t_embedder2", _p(out))
+        if rc:
+            raise RuntimeError("oracle timestep embed failed")
+        return out
+
+    def noise(self, T, C_, seed, temperature=1.0):
+        out = np.empty((T, C_), np.float32)
+        if self.lib.orc_noise(T, C_, seed, temperature, _p(out)):
+            raise RuntimeError("noise shape must be non-empty")
+        return out
+
+
+def ref_available() -> bool:
+    return REF_LIB.exists()
+
+
+class RefOracle:
+    """The reference's own compiled CPU functions (single-threaded, scalar)."""
+
+    def __init__(self, bundle_dir: str | Path, lib_path: Path = REF_LIB):
+        self.lib = C.CDLL(str(lib_path))
+        self.dir = str(bundle_dir).encode()
+        L = self.lib
+        L.ref_last_error.restype = C.c_char_p
+        L.ref_estimator_step.argtypes = [C.c_char_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
+                                         C.c_void_p, C.c_uint32, C.c_void_p]
+        L.ref_cfm_euler.argtypes = [C.c_char_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
+                                    C.c_uint32, C.c_float, C.c_void_p]
+        L.ref_cfm_euler_masked.argtypes = [C.c_char_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_void_p]
+        L.ref_attention_layer.argtypes = [C.c_char_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
+        L.ref_wavenet.argtypes = [C.c_char_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p]
+        L.ref_timestep_embed.argtypes = [C.c_char_p, C.c_float, C.c_int, C.c_void_p]
+        L.ref_noise.argtypes = [C.c_uint32, C.c_uint32, C.c_uint64, C.c_float, C.c_void_p]
+
+    def _ok(self, rc):
+        if rc:
+            raise RuntimeError("reference: " + self.lib.ref_last_error().decode())
+
+    def estimator(self, x, prompt_x, cond, style, t, mask=None):
+        x, prompt_x, cond, style = _f32(x), _f32(prompt_x), _f32(cond), _f32(style)
+        T = x.shape[0]
+        mask = _u32(np.ones(T) if mask is None else mask)
+        v = np.empty((T, 80), np.float32)
+        self._ok(self.lib.ref_estimator_step(self.dir, _p(x), _p(prompt_x), _p(cond), _p(style), float(t), _p(mask), T,
+                                             _p(v)))
+        return v
+
+    def euler(self, noise, prompt, cond, style, P, steps, cfg):
+        noise, cond, style = _f32(noise), _f32(cond), _f32(style)
+        T = noise.shape[0]
+        prompt = _f32(prompt if P else np.zeros((1, 80)))
+        out = np.empty((T, 80), np.float32)
+        self._ok(self.lib.ref_cfm_euler(self.dir, _p(noise), _p(prompt), _p(cond), _p(style), T, int(P), int(steps),
+                                        float(cfg), _p(out)))
+        return out
+
+    def euler_masked(self, noise, prompt_x, cond, style, mask, P, steps, cfg):
+        noise, prompt_x, cond, style = _f32(noise), _f32(prompt_x), _f32(cond), _f32(style)
+        T = noise.shape[0]
+        out = np.empty((T, 80), np.float32)
+        self._ok(self.lib.ref_cfm_euler_masked(self.dir, _p(noise), _p(prompt_x), _p(cond), _p(style), _p(_u32(mask)),
+                                               T, int(P), int(steps), float(cfg), _p(out)))
+        return out
+
+    def attention_layer(self, x, mask, layer):
+        x = _f32(x)
+        T = x.shape[0]
+        out = np.empty((T, 512), np.float32)
+        self._ok(self.lib.ref_attention_layer(self.dir, _p(x), _p(_u32(mask)), T, layer, _p(out)))
+        return out
+
+    def wavenet(self, x, g, mask):
+        x, g = _f32(x), _f32(g)
+        T = x.shape[0]
+        out = np.empty((T, 512), np.float32)
+        self._ok(self.lib.ref_wavenet(self.dir, _p(x), _p(g), _p(_u32(mask)), T, _p(out)))
+        return out
+
+    def timestep_embed(self, t, which=0):
+        out = np.empty(512, np.float32)
+        self._ok(self.lib.ref_timestep_embed(self.dir, float(t), which, _p(out)))
+        return out
+
+    def noise(self, T, C_, seed, temperature=1.0):
+        out = np.empty((T, C_), np.float32)
+        self._ok(self.lib.ref_noise(T, C_, seed, temperature, _p(out)))
+        return out
+
+
+def compare(ref, got) -> dict:
+    """max-abs, rel-L2 and cosine of got vs ref (compare_arrays semantics,
+    metal_indextts2/metrics.py:38-54)."""
+    r = np.asarray(ref, np.float64).ravel()
+    g = np.asarray(got, np.float64).ravel()
+    d = g - r
+    rn, gn = np.linalg.norm(r), np.linalg.norm(g)
+    return {
+        "max_abs": float(np.abs(d).max()) if d.size else 0.0,
+        "rel_l2": float(np.linalg.norm(d) / max(rn, 1e-30)),
+        "cosine": float(r @ g / max(rn * gn, 1e-30)),
+    }

@@ -1,0 +1,124 @@
+"""CPU-only tests: bundle format, host logic, the C-ABI library's exports, and
+input generators. No kernel is launched here."""
+from __future__ import annotations
+
+import json
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import mit2
+import workloads as W
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "itts_cfm.h"
+
+
+def test_bundle_round_trip(tmp_path):
+    man = mit2.write_bundle(tmp_path, [("a.weight", np.arange(12, dtype=np.float32).reshape(3, 4)),
+                                       ("b.codes", np.arange(5, dtype=np.int32)),
+                                       ("c.half", np.linspace(-1, 1, 7).astype(np.float16))])
+    assert man["format"] == "MIT2" and man["version"] == 1
+    assert all(t["offset"] % man["alignment"] == 0 for t in man["tensors"])
+    raw = (tmp_path / "weights.bin").read_bytes()
+    assert raw[:4] == b"MIT2" and int.from_bytes(raw[4:8], "little") == 1 and int.from_bytes(raw[8:12], "little") == 4096
+    got = mit2.read_bundle(tmp_path, verify=True)
+    np.testing.assert_array_equal(got["a.weight"], np.arange(12, dtype=np.float32).reshape(3, 4))
+    np.testing.assert_array_equal(got["b.codes"], np.arange(5, dtype=np.int32))
+    assert got["c.half"].dtype == np.float16
+
+
+def test_bundle_checksum_detects_corruption(tmp_path):
+    mit2.write_bundle(tmp_path, [("x", np.ones(8, np.float32))])
+    man = json.loads((tmp_path / "manifest.json").read_text())
+    off = man["tensors"][0]["offset"]
+    with (tmp_path / "weights.bin").open("r+b") as f:
+        f.seek(off)
+        f.write(b"\x00\x00\x80\x7f")
+    with pytest.raises(ValueError):
+        mit2.read_bundle(tmp_path, verify=True)
+
+
+def test_synthetic_bundle_is_deterministic_and_complete():
+    a = mit2.make_dit_tensors(3, "baseline")
+    b = mit2.make_dit_tensors(3, "baseline")
+    assert [n for n, _ in a] == [n for n, _ in b]
+    for (na, xa), (_, xb) in zip(a, b):
+        assert xa.dtype == xb.dtype and np.array_equal(xa, xb), na
+    names = {n for n, _ in a}
+    for spec_name, shape, _ in mit2.dit_tensor_specs():
+        assert mit2.PREFIX + spec_name in names
+    d = dict(a)
+    # weight-norm g equals ||v_row|| so the folded weight equals v
+    v = d[mit2.PREFIX + "final_layer.linear.weight_v"].astype(np.float32)
+    g = d[mit2.PREFIX + "final_layer.linear.weight_g"].astype(np.float32).ravel()
+    np.testing.assert_allclose(g, np.sqrt((v * v).sum(1)), rtol=1e-3)
+    w = d[mit2.PREFIX + "transformer.layers.0.attention.wqkv.weight"].astype(np.float32)
+    assert abs(w.std() - 0.02) < 1e-3
+
+
+def test_unit_init_scale():
+    d = dict(mit2.make_dit_tensors(0, "unit"))
+    w = d[mit2.PREFIX + "transformer.layers.3.feed_forward.w2.weight"].astype(np.float32)
+    assert abs(w.std() - 1 / np.sqrt(1536)) < 2e-3
+    pb = d[mit2.PREFIX + "transformer.layers.3.ffn_norm.project_layer.bias"].astype(np.float32)
+    assert abs(pb[:512].mean() - 1.0) < 0.05 and abs(pb[512:].mean()) < 0.05
+
+
+def test_header_exports_every_symbol():
+    """libitts_cfm.so loads on a CPU-only host and exports every declared entry point."""
+    import itts_cfm
+
+    decl = set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(itts_\w+)\s*\(", HEADER.read_text(), re.M))
+    assert decl, "no declarations parsed"
+    lib = itts_cfm.load()
+    for name in sorted(decl):
+        assert hasattr(lib, name), name
+    assert decl == set(itts_cfm.EXPORTED)
+
+
+def test_create_fails_loudly_without_gpu_or_bundle(tmp_path):
+    """No CPU fallback: creation without a usable GPU (or bundle) returns an error code."""
+    import itts_cfm
+
+    with pytest.raises(itts_cfm.IttsError) as e:
+        itts_cfm.Context(tmp_path / "missing", device=0)
+    assert e.value.code in (itts_cfm.ITTS_ECUDA, itts_cfm.ITTS_ENODEV, itts_cfm.ITTS_EBUNDLE)
+
+
+def test_bucket_len_policy():
+    import itts_cfm
+
+    assert itts_cfm.bucket_len(2) == 128
+    assert itts_cfm.bucket_len(128) == 128
+    assert itts_cfm.bucket_len(129) == 256
+    assert itts_cfm.bucket_len(1500) == 1536
+    assert itts_cfm.bucket_len(2049) == 2304
+    for t in range(2, 5000, 37):
+        b = itts_cfm.bucket_len(t)
+        assert b >= t and itts_cfm.bucket_len(b) == b
+
+
+def test_step_flops_matches_cost_model():
+    import itts_cfm
+
+    # 294.09e6 * T + 53,248 * T^2 per guided step (2 branches)
+    for T in (400, 800, 4096):
+        want = 2 * 2 * 73_523_200 * T + 2 * 13 * 4 * 512 * T * T
+        assert abs(itts_cfm.step_flops(2, T) - want) / want < 1e-12
+    assert abs(itts_cfm.step_flops(2, 800) - 269.35e9) / 269.35e9 < 1e-3
+
+
+def test_workloads_deterministic():
+    a = W.config_utterances(3, n=5)
+    b = W.config_utterances(3, n=5)
+    for x, y in zip(a, b):
+        assert x.T == y.T and x.P == y.P and np.array_equal(x.noise, y.noise)
+        assert 200 <= x.T <= 1500 and x.P <= x.T
+    u = W.config_utterances(2)[0]
+    assert u.T == 800 and u.P == 200 and u.cond.shape == (800, 512)
+    vl, pl, noise, px, cond, style = W.pad_batch(a[:2], 1536)
+    assert noise.shape == (2, 1536, 80) and np.all(noise[0, a[0].T:] == 0)
+    assert np.array_equal(px[1, : a[1].P], a[1].prompt) and np.all(px[1, a[1].P:] == 0)
