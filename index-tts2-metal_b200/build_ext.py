@@ -20,6 +20,7 @@ REPO = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "lib" / "libitts_cfm.so"
+CLI = PKG / "lib" / "mtts_cfm"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "-I", str(REPO / "include"),
@@ -59,6 +60,15 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    # C++ host driver over the C ABI (links the library with an $ORIGIN rpath).
+    cli_src = PKG / "cli" / "mtts_cfm.cpp"
+    if force or not CLI.exists() or CLI.stat().st_mtime < max(LIB.stat().st_mtime, cli_src.stat().st_mtime,
+                                                                (REPO / "include" / "itts_cfm.hpp").stat().st_mtime):
+        cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-I", str(REPO / "include"), str(cli_src), "-o",
+               str(CLI), "-L", str(LIB.parent), "-litts_cfm", "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"cli build failed:\n{r.stdout}\n{r.stderr}")
     return LIB
 
 

@@ -1,0 +1,136 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference.
+
+Runs the reference's own CPU functions (oracle/_ref/libref_cfm.so, compiled
+from the reference sources by oracle/build_ref.py) on small seeded cases and
+stores inputs + outputs as compressed .npz files next to this script. The
+synthetic bundles are regenerated from their seeds (index-tts2-metal_b200/mit2.py);
+each file records the sha256 of the bundle's weights.bin so generator drift
+is detected.
+
+    python tests/golden/make_golden.py
+
+Cases (inputs follow the reference's self-tests where it has them):
+  kat_tembed        t_embedder / t_embedder2 at t in {0, 0.37, 0.96}
+  kat_noise         make_deterministic_normal_noise(5, 80, 1234) and (3, 7, 0)
+  kat_estimator_t6  run_dit_estimator_step_test inputs (T=6, t=0.37, mask 111100),
+                    unit and baseline bundles
+  kat_estimator_t33 seeded N(0,1) inputs, T=33, t=0.5, 3 padded keys (unit)
+  kat_attention_t6  attention core of layers 0 and 12, masks 111100 / 101110
+  kat_wavenet_t6    WaveNet stack with a global condition, mask 111100
+  kat_euler_t5      run_cfm_euler_test inputs (T=5, P=2): 3 steps cfg 0 and 25 steps cfg 0.5
+  kat_euler_masked  T=8 (2 padded), P=2, 2 steps, cfg 0.7 (padded-batch semantics)
+"""
+from __future__ import annotations
+
+import hashlib
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO / "index-tts2-metal_b200"))
+sys.path.insert(0, str(REPO / "oracle"))
+
+import mit2  # noqa: E402
+import oracle  # noqa: E402
+import workloads  # noqa: E402
+
+ROOT = Path(tempfile.gettempdir()) / "itts_golden_bundles"
+
+
+def f32(a):
+    return np.asarray(a, dtype=np.float32)
+
+
+def weights_sha(d: Path) -> str:
+    h = hashlib.sha256()
+    with (d / "weights.bin").open("rb") as f:
+        for chunk in iter(lambda: f.read(1 << 22), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def estimator_selftest_inputs():
+    """run_dit_estimator_step_test inputs (runtime/impl/dit_cfm_bigvgan.cpp:2829-2848)."""
+    T = 6
+    i = np.arange(T * 80, dtype=np.float32)
+    m53 = (np.arange(T * 80) % 53).astype(np.float32)
+    m47 = (np.arange(T * 80) % 47).astype(np.float32)
+    x = np.sin(i * np.float32(0.021)) * np.float32(0.10) + np.cos(m53 * np.float32(0.017)) * np.float32(0.04)
+    px = np.cos(i * np.float32(0.019)) * np.float32(0.08) + np.sin(m47 * np.float32(0.023)) * np.float32(0.03)
+    ic = np.arange(T * 512, dtype=np.float32)
+    m127 = (np.arange(T * 512) % 127).astype(np.float32)
+    cond = np.sin(ic * np.float32(0.010)) * np.float32(0.09) + np.cos(m127 * np.float32(0.013)) * np.float32(0.05)
+    style = np.cos(np.arange(192, dtype=np.float32) * np.float32(0.016)) * np.float32(0.20)
+    return f32(x).reshape(T, 80), f32(px).reshape(T, 80), f32(cond).reshape(T, 512), f32(style)
+
+
+def main():
+    unit = mit2.make_dit_bundle(ROOT / "seed0_unit", seed=0, init="unit")
+    base = mit2.make_dit_bundle(ROOT / "seed0_baseline", seed=0, init="baseline")
+    ru, rb = oracle.RefOracle(unit), oracle.RefOracle(base)
+    meta = lambda d, init: dict(bundle_seed=0, bundle_init=init, weights_sha256=weights_sha(d))  # noqa: E731
+
+    ts = np.array([0.0, 0.37, 0.96], np.float32)
+    np.savez_compressed(HERE / "kat_tembed.npz", t=ts, t1=np.stack([ru.timestep_embed(t, 0) for t in ts]),
+                        t2=np.stack([ru.timestep_embed(t, 1) for t in ts]), **meta(unit, "unit"))
+
+    np.savez_compressed(HERE / "kat_noise.npz", a=ru.noise(5, 80, 1234), b=ru.noise(3, 7, 0))
+
+    x, px, cond, style = estimator_selftest_inputs()
+    mask = np.array([1, 1, 1, 1, 0, 0], np.uint32)
+    np.savez_compressed(HERE / "kat_estimator_t6.npz", x=x, prompt_x=px, cond=cond, style=style, mask=mask,
+                        t=np.float32(0.37), vel_unit=ru.estimator(x, px, cond, style, 0.37, mask),
+                        vel_baseline=rb.estimator(x, px, cond, style, 0.37, mask),
+                        baseline_weights_sha256=weights_sha(base), **meta(unit, "unit"))
+
+    rng = np.random.default_rng(33)
+    T = 33
+    x = f32(rng.standard_normal((T, 80)))
+    px = np.zeros((T, 80), np.float32)
+    px[:5] = rng.standard_normal((5, 80))
+    cond = f32(rng.standard_normal((T, 512)))
+    style = f32(rng.standard_normal(192))
+    mask = np.ones(T, np.uint32)
+    mask[-3:] = 0
+    np.savez_compressed(HERE / "kat_estimator_t33.npz", x=x, prompt_x=px, cond=cond, style=style, mask=mask,
+                        t=np.float32(0.5), vel=ru.estimator(x, px, cond, style, 0.5, mask), **meta(unit, "unit"))
+
+    rng = np.random.default_rng(6)
+    xa = f32(rng.standard_normal((6, 512)))
+    ma = np.array([1, 1, 1, 1, 0, 0], np.uint32)
+    mb = np.array([1, 0, 1, 1, 1, 0], np.uint32)
+    np.savez_compressed(HERE / "kat_attention_t6.npz", x=xa, mask_a=ma, mask_b=mb,
+                        l0_a=ru.attention_layer(xa, ma, 0), l0_b=ru.attention_layer(xa, mb, 0),
+                        l12_a=ru.attention_layer(xa, ma, 12), **meta(unit, "unit"))
+
+    i = np.arange(6 * 512, dtype=np.float32)
+    xw = f32(np.sin(i * np.float32(0.010)) * np.float32(0.08) +
+             np.cos((np.arange(6 * 512) % 181).astype(np.float32) * np.float32(0.013)) * np.float32(0.04)).reshape(6, 512)
+    gi = np.arange(512, dtype=np.float32)
+    g = f32(np.sin(gi * np.float32(0.019)) * np.float32(0.04) + np.cos((np.arange(512) % 71).astype(np.float32) * np.float32(0.023)) * np.float32(0.02))
+    np.savez_compressed(HERE / "kat_wavenet_t6.npz", x=xw, g=g, mask=ma, out=ru.wavenet(xw, g, ma), **meta(unit, "unit"))
+
+    x5, p5, c5, s5 = workloads.sincos_inputs(5, 2)
+    np.savez_compressed(HERE / "kat_euler_t5.npz", noise=x5, prompt=p5, cond=c5, style=s5,
+                        mel_3_cfg0=ru.euler(x5, p5, c5, s5, 2, 3, 0.0),
+                        mel_25_cfg05=ru.euler(x5, p5, c5, s5, 2, 25, 0.5), **meta(unit, "unit"))
+
+    rng = np.random.default_rng(8)
+    T = 8
+    n8 = f32(rng.standard_normal((T, 80)))
+    p8 = np.zeros((T, 80), np.float32)
+    p8[:2] = rng.standard_normal((2, 80))
+    c8 = f32(rng.standard_normal((T, 512)))
+    s8 = f32(rng.standard_normal(192))
+    m8 = np.array([1] * 6 + [0] * 2, np.uint32)
+    np.savez_compressed(HERE / "kat_euler_masked.npz", noise=n8, prompt_x=p8, cond=c8, style=s8, mask=m8,
+                        mel=ru.euler_masked(n8, p8, c8, s8, m8, 2, 2, 0.7), **meta(unit, "unit"))
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

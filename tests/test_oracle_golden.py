@@ -1,0 +1,106 @@
+"""Pin the CPU oracle (oracle/dit_oracle.c) to the reference's own CPU
+functions through the committed golden vectors (tests/golden/, made by
+tests/golden/make_golden.py from oracle/_ref). fp32 vs fp32 with a different
+summation order: the reference's own unit tolerance ladder applies (1e-4
+relative to the output scale)."""
+from __future__ import annotations
+
+import hashlib
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+GOLD = Path(__file__).resolve().parent / "golden"
+REL = 1e-4
+
+
+def _load(name):
+    return dict(np.load(GOLD / f"{name}.npz"))
+
+
+def _close(ref, got, rel=REL):
+    ref = np.asarray(ref, np.float64)
+    got = np.asarray(got, np.float64)
+    scale = max(1.0, float(np.abs(ref).max()))
+    err = float(np.abs(ref - got).max())
+    assert err <= rel * scale, (err, scale)
+
+
+def _sha(d: Path) -> str:
+    h = hashlib.sha256()
+    with (d / "weights.bin").open("rb") as f:
+        for chunk in iter(lambda: f.read(1 << 22), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def test_bundles_match_golden_generator(unit_bundle, baseline_bundle):
+    g = _load("kat_estimator_t6")
+    assert _sha(unit_bundle) == str(g["weights_sha256"])
+    assert _sha(baseline_bundle) == str(g["baseline_weights_sha256"])
+
+
+def test_noise_bit_exact(port_unit):
+    g = _load("kat_noise")
+    assert np.array_equal(port_unit.noise(5, 80, 1234), g["a"])
+    assert np.array_equal(port_unit.noise(3, 7, 0), g["b"])
+
+
+def test_timestep_embedders(port_unit):
+    g = _load("kat_tembed")
+    for i, t in enumerate(g["t"]):
+        _close(g["t1"][i], port_unit.timestep_embed(float(t), 0))
+        _close(g["t2"][i], port_unit.timestep_embed(float(t), 1))
+
+
+def test_estimator_selftest_inputs(port_unit, port_baseline):
+    g = _load("kat_estimator_t6")
+    args = (g["x"], g["prompt_x"], g["cond"], g["style"], float(g["t"]), g["mask"])
+    _close(g["vel_unit"], port_unit.estimator(*args))
+    _close(g["vel_baseline"], port_baseline.estimator(*args))
+
+
+def test_estimator_random_t33(port_unit):
+    g = _load("kat_estimator_t33")
+    _close(g["vel"], port_unit.estimator(g["x"], g["prompt_x"], g["cond"], g["style"], float(g["t"]), g["mask"]))
+
+
+def test_attention_core(port_unit):
+    g = _load("kat_attention_t6")
+    _close(g["l0_a"], port_unit.attention_layer(g["x"], g["mask_a"], 0))
+    _close(g["l0_b"], port_unit.attention_layer(g["x"], g["mask_b"], 0))
+    _close(g["l12_a"], port_unit.attention_layer(g["x"], g["mask_a"], 12))
+
+
+def test_wavenet_global_cond(port_unit):
+    g = _load("kat_wavenet_t6")
+    _close(g["out"], port_unit.wavenet(g["x"], g["g"], g["mask"]))
+
+
+def test_euler_sampler(port_unit):
+    g = _load("kat_euler_t5")
+    px = np.zeros((5, 80), np.float32)
+    px[:2] = g["prompt"]
+    _close(g["mel_3_cfg0"], port_unit.euler(g["noise"], px, g["cond"], g["style"], 2, 3, 0.0))
+    _close(g["mel_25_cfg05"], port_unit.euler(g["noise"], px, g["cond"], g["style"], 2, 25, 0.5))
+
+
+def test_euler_masked(port_unit):
+    g = _load("kat_euler_masked")
+    _close(g["mel"], port_unit.euler(g["noise"], g["prompt_x"], g["cond"], g["style"], 2, 2, 0.7, mask=g["mask"]))
+
+
+def test_oracle_detects_planted_error(port_unit, unit_tensors):
+    """A wrong weight in the oracle must break the pin (the check has teeth)."""
+    g = _load("kat_estimator_t6")
+    bad = dict(unit_tensors)
+    k = "s2mel.net.cfm.estimator.transformer.layers.5.feed_forward.w2.weight"
+    bad[k] = bad[k].copy()
+    bad[k][3, :] *= 1.5
+    wrong = O.PortOracle(bad)
+    args = (g["x"], g["prompt_x"], g["cond"], g["style"], float(g["t"]), g["mask"])
+    with pytest.raises(AssertionError):
+        _close(g["vel_unit"], wrong.estimator(*args))
