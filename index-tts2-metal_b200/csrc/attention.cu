@@ -16,6 +16,8 @@
 #include <stdint.h>
 
 #include "kernels.cuh"
+#include "launch.cuh"
+#include "ptx.cuh"
 
 namespace itts {
 
@@ -89,6 +91,8 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const __half* __restrict_
   __shared__ __align__(128) __half sV[2][kBKV * kHd];
   __shared__ float sBias[2][kBKV];
 
+  griddep_wait();
+  griddep_launch();
   const int qt = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t seq_base = static_cast<size_t>(s) * T;
@@ -252,8 +256,7 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const __half* __restrict_
 cudaError_t attention_run(const __half* qkv, const float* row_mask, __half* out, int S, int T, cudaStream_t st) {
   if (S <= 0 || T <= 0) return cudaErrorInvalidValue;
   dim3 grid((T + kBQ - 1) / kBQ, 8, S);
-  attn_fwd_kernel<<<grid, 128, 0, st>>>(qkv, row_mask, out, T);
-  return cudaGetLastError();
+  return launch_pdl(attn_fwd_kernel, grid, dim3(128), 0, st, qkv, row_mask, out, T);
 }
 
 }  // namespace itts

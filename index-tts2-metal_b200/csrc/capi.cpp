@@ -363,7 +363,7 @@ int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a
                  uint32_t K, uint32_t bn) {
   return guarded(ctx, [&] {
     need(a0 && b && c && M > 0 && N > 0 && K > 0, "bad gemm arguments");
-    need(bn == 80 || bn == 128 || bn == 256, "bn must be 80, 128 or 256");
+    need(bn == 64 || bn == 80 || bn == 128 || bn == 256, "bn must be 64, 80, 128 or 256");
     need(N % 16 == 0 && ldc % 4 == 0, "N must be a multiple of 16, ldc of 4");
     itts::GemmLaunch g;
     std::memset(&g, 0, sizeof(g));

@@ -32,6 +32,7 @@ GemmLaunch make_gemm(Operand a0, Operand a1, Operand b, int M, int N, int K, int
                      int kb_per_tap, int bn, int epi) {
   GemmLaunch g;
   std::memset(&g, 0, sizeof(g));
+  if (bn == 0) bn = gemm_pick_bn(M, N, epi == kEpiSwiGLU || epi == kEpiWnGate || epi == kEpiWnResSkip);
   if (!make_tmap_f16(&g.tmA0, a0.p, a0.cols, a0.rows, a0.ld, 128))
     throw std::runtime_error("gemm: tensor map for A0 rejected");
   if (a1.p) {
@@ -272,16 +273,16 @@ void Engine::build_work_launches(Work* w) {
     g.args.status = d_status_;
   };
   // Step-invariant: cond projection (conditional rows only) and merge base.
-  w->g_cp = make_gemm(act(w->cond16, 512, BT), none, wt(w_.wcp, 512, 512), BT, 512, 512, kAPlain, 0, 0, 128, kEpiF16);
+  w->g_cp = make_gemm(act(w->cond16, 512, BT), none, wt(w_.wcp, 512, 512), BT, 512, 512, kAPlain, 0, 0, 0, kEpiF16);
   w->g_cp.args.bias = w_.bcp;
   w->g_cp.args.out16 = w->cp16;
   w->g_cp.args.ld16 = 512;
-  w->g_base = make_gemm(act(w->U, 784, R), none, wt(w_.wrest, 784, 512), R, 512, 784, kAPlain, 0, 0, 128, kEpiF32);
+  w->g_base = make_gemm(act(w->U, 784, R), none, wt(w_.wrest, 784, 512), R, 512, 784, kAPlain, 0, 0, 0, kEpiF32);
   w->g_base.args.bias = w_.bm;
   w->g_base.args.out32 = w->base;
   w->g_base.args.ld32 = 512;
   // Per step: x slice of the merge + base.
-  w->g_merge = make_gemm(act(w->XD, 80, R), none, wt(w_.wx, 80, 512), R, 512, 80, kAPlain, 0, 0, 128, kEpiF32);
+  w->g_merge = make_gemm(act(w->XD, 80, R), none, wt(w_.wx, 80, 512), R, 512, 80, kAPlain, 0, 0, 0, kEpiF32);
   w->g_merge.args.resid32 = w->base;
   w->g_merge.args.ldr = 512;
   w->g_merge.args.out32 = w->xres;
@@ -291,23 +292,23 @@ void Engine::build_work_launches(Work* w) {
     if (l > kLayers / 2) {
       GemmLaunch& g = w->g_skip[l];
       g = make_gemm(act(w->x16, 512, R), act(w->skip16[kLayers - 1 - l], 512, R), wt(L.wskip, 1024, 512), R, 512,
-                    1024, kASplit, 8, 0, 128, kEpiF32);
+                    1024, kASplit, 8, 0, 0, kEpiF32);
       g.args.bias = L.bskip;
       g.args.out32 = w->xres;
       g.args.ld32 = 512;
     }
-    w->g_qkv[l] = make_gemm(act(w->xn16, 512, R), none, wt(L.wqkv, 512, 1536), R, 1536, 512, kAPlain, 0, 0, 128, kEpiQKV);
+    w->g_qkv[l] = make_gemm(act(w->xn16, 512, R), none, wt(L.wqkv, 512, 1536), R, 1536, 512, kAPlain, 0, 0, 0, kEpiQKV);
     w->g_qkv[l].args.out16 = w->qkv16;
     w->g_qkv[l].args.ld16 = 1536;
-    w->g_wo[l] = make_gemm(act(w->attn16, 512, R), none, wt(L.wo, 512, 512), R, 512, 512, kAPlain, 0, 0, 128, kEpiF32);
+    w->g_wo[l] = make_gemm(act(w->attn16, 512, R), none, wt(L.wo, 512, 512), R, 512, 512, kAPlain, 0, 0, 0, kEpiF32);
     w->g_wo[l].args.resid32 = w->xres;
     w->g_wo[l].args.ldr = 512;
     w->g_wo[l].args.out32 = w->h;
     w->g_wo[l].args.ld32 = 512;
-    w->g_w13[l] = make_gemm(act(w->xn16, 512, R), none, wt(L.w13, 512, 3072), R, 3072, 512, kAPlain, 0, 0, 256, kEpiSwiGLU);
+    w->g_w13[l] = make_gemm(act(w->xn16, 512, R), none, wt(L.w13, 512, 3072), R, 3072, 512, kAPlain, 0, 0, 0, kEpiSwiGLU);
     w->g_w13[l].args.out16 = w->g16;
     w->g_w13[l].args.ld16 = 1536;
-    w->g_w2[l] = make_gemm(act(w->g16, 1536, R), none, wt(L.w2, 1536, 512), R, 512, 1536, kAPlain, 0, 0, 128, kEpiF32);
+    w->g_w2[l] = make_gemm(act(w->g16, 1536, R), none, wt(L.w2, 1536, 512), R, 512, 1536, kAPlain, 0, 0, 0, kEpiF32);
     w->g_w2[l].args.resid32 = w->h;
     w->g_w2[l].args.ldr = 512;
     w->g_w2[l].args.out32 = w->xres;
@@ -320,12 +321,12 @@ void Engine::build_work_launches(Work* w) {
       w->g_w2[l].args.ld16 = 512;
     }
   }
-  w->g_sl = make_gemm(act(w->xn16, 512, R), act(w->XD, 80, R), wt(w_.wsl, 592, 512), R, 512, 640, kASplit, 8, 0, 128,
+  w->g_sl = make_gemm(act(w->xn16, 512, R), act(w->XD, 80, R), wt(w_.wsl, 592, 512), R, 512, 640, kASplit, 8, 0, 0,
                       kEpiF16);
   w->g_sl.args.bias = w_.bsl;
   w->g_sl.args.out16 = w->ls16;
   w->g_sl.args.ld16 = 512;
-  w->g_c1res = make_gemm(act(w->ls16, 512, R), none, wt(w_.wc1res, 512, 1024), R, 1024, 512, kAPlain, 0, 0, 128,
+  w->g_c1res = make_gemm(act(w->ls16, 512, R), none, wt(w_.wc1res, 512, 1024), R, 1024, 512, kAPlain, 0, 0, 0,
                          kEpiConv1Res);
   w->g_c1res.args.bias = w_.bc1res;
   w->g_c1res.args.wn_xp = w->xp16;
@@ -333,16 +334,16 @@ void Engine::build_work_launches(Work* w) {
   w->g_c1res.args.ld32 = 512;
   for (int l = 0; l < kWnLayers; ++l) {
     w->g_in[l] = make_gemm(act(w->xp16, 512, w->Rp), none, wt(w_.win[l], 2560, 1024), w->Rp, 1024, 2560, kAConv5, 0, 8,
-                           128, kEpiWnGate);
+                           0, kEpiWnGate);
     w->g_in[l].args.bias = w_.bin[l];
     w->g_in[l].args.out16 = w->gate16;
     w->g_in[l].args.ld16 = 512;
     if (l < kWnLayers - 1) {
-      w->g_rs[l] = make_gemm(act(w->gate16, 512, R), none, wt(w_.wrs[l], 512, 1024), R, 1024, 512, kAPlain, 0, 0, 128,
+      w->g_rs[l] = make_gemm(act(w->gate16, 512, R), none, wt(w_.wrs[l], 512, 1024), R, 1024, 512, kAPlain, 0, 0, 0,
                              kEpiWnResSkip);
       w->g_rs[l].args.wn_first = l == 0 ? 1 : 0;
     } else {
-      w->g_rs[l] = make_gemm(act(w->gate16, 512, R), none, wt(w_.wrs[l], 512, 512), R, 512, 512, kAPlain, 0, 0, 128,
+      w->g_rs[l] = make_gemm(act(w->gate16, 512, R), none, wt(w_.wrs[l], 512, 512), R, 512, 512, kAPlain, 0, 0, 0,
                              kEpiWnLast);
       w->g_rs[l].args.out32 = w->fin;
       w->g_rs[l].args.ld32 = 512;
@@ -352,7 +353,7 @@ void Engine::build_work_launches(Work* w) {
     w->g_rs[l].args.wn_xp = w->xp16;
     w->g_rs[l].args.wn_acc = w->wacc;
   }
-  w->g_fin = make_gemm(act(w->fn16, 512, R), none, wt(w_.wfin, 512, 512), R, 512, 512, kAPlain, 0, 0, 128, kEpiF16);
+  w->g_fin = make_gemm(act(w->fn16, 512, R), none, wt(w_.wfin, 512, 512), R, 512, 512, kAPlain, 0, 0, 0, kEpiF16);
   w->g_fin.args.bias = w_.bfin;
   w->g_fin.args.out16 = w->fh16;
   w->g_fin.args.ld16 = 512;

@@ -1,9 +1,13 @@
 // tcgen05/TMEM GEMM with fused DiT-CFM epilogues (sm_100a).
 //
-// One CTA computes a 128 x BN output tile. Warp roles (192 threads):
+// Persistent, warp-specialised: one CTA per SM walks the 128 x BN output
+// tiles (static round-robin over the grid). Warp roles (192 threads):
 //   warp 0 lane 0 : TMA producer (A and B k-blocks into a STAGES-deep ring)
-//   warp 1        : allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
-//   warps 2..5    : epilogue, one accumulator row per thread (TMEM lane quarter = warp % 4)
+//   warp 1        : allocates 2*BN TMEM columns; lane 0 issues tcgen05.mma
+//                   (M=128, N=BN, K=16) into accumulator buffer (tile & 1)
+//   warps 2..5    : epilogue, one accumulator row per thread (TMEM lane
+//                   quarter = warp % 4); drains buffer (tile & 1) while the
+//                   MMA warp fills the other one.
 // Replaces the reference's MPS GEMM calls and the elementwise kernels that
 // followed them (bias prefill, RoPE rotate, silu_mul_split, add, wavenet gate,
 // wavenet res/skip update, reflect pad, concat), metal/kernels.metal:131-239,
@@ -13,6 +17,7 @@
 #include <mutex>
 
 #include "gemm.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace itts {
@@ -21,9 +26,18 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 f16 = one 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each owning half of the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
-__host__ __device__ constexpr int tmem_cols_for(int bn) { return bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256; }
+// Phase timestamps for performance investigation: compiled out unless a
+// harness defines ITTS_GEMM_TRACE and provides itts_gemm_trace_point(slot).
+#ifdef ITTS_GEMM_TRACE
+#define GEMM_TRACE(slot) itts_gemm_trace_point(slot)
+#else
+#define GEMM_TRACE(slot) ((void)0)
+#endif
+
+__host__ __device__ constexpr int pow2_cols(int c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
 
 // Source row of the reflect padding used by the WaveNet k=5 convolution
 // (tokenizer_tests.cpp:3836-3854): halo position j in {-2,-1,T,T+1}.
@@ -37,16 +51,392 @@ __device__ __forceinline__ int reflect_src(int j, int T) {
   return src;
 }
 
-// Write 16 channels of one WaveNet activation row into the reflect-padded
-// buffer, including every halo slot that mirrors this row.
-__device__ __forceinline__ void write_xp16(__half* xp, int s, int t, int T, int col, const float* v) {
+__device__ __forceinline__ void u2f16(const uint32_t (&r)[16], float* v) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Epilogue helpers: the 128 epilogue threads (warps 2..5) share a named barrier.
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
+
+// Per-tile column constants staged in shared memory before the accumulator is
+// ready: bias[n0 .. n0+BN) and, for the WaveNet gate, the global condition of
+// the tile's channels (a-part then b-part, BN/2 each).
+template <int BN, int EPI>
+__device__ __forceinline__ void stage_tile_consts(const GemmArgs& args, int n0, float* sconst, int etid) {
+  for (int i = etid; i < BN; i += 128) {
+    const int n = n0 + i;
+    sconst[i] = (args.bias && n < args.N) ? args.bias[n] : 0.0f;
+  }
+  if constexpr (EPI == kEpiWnGate) {
+    for (int i = etid; i < BN / 2; i += 128) {
+      const int ch = (n0 >> 1) + i;
+      const bool in = 2 * ch < args.N;
+      sconst[BN + i] = in ? args.wn_cond[ch] : 0.0f;
+      sconst[BN + BN / 2 + i] = in ? args.wn_cond[512 + ch] : 0.0f;
+    }
+  }
+}
+
+__host__ __device__ constexpr int tile_const_floats(int bn) { return 2 * bn; }
+
+// ---- coalesced epilogue stores through a per-warp shared-memory stage ----
+// Each epilogue warp owns 32 accumulator rows (one per lane). Values of a
+// 32-column group are first written row-wise into a 32 x 32 fp32 stage (16-byte
+// chunks swizzled by row), then read column-wise so that 8 (fp32) or 4 (f16)
+// lanes cover one destination row segment and every store is a full 128 B / 64 B
+// line piece. Destination rows come from the owning lane by shuffle, so any
+// per-row remapping (padded WaveNet rows, compact rows) is supported.
+constexpr int kStageFloats = 32 * 32;  // per warp
+
+__device__ __forceinline__ void stage_put16(float4* stg, int r, int c16, const float* v) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int j = (c16 >> 2) + k;
+    stg[r * 8 + (j ^ (r & 7))] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  }
+}
+
+__device__ __forceinline__ const void* shfl_ptr(const void* p, int src) {
+  const unsigned long long u = reinterpret_cast<unsigned long long>(p);
+  const unsigned lo = __shfl_sync(0xffffffffu, static_cast<unsigned>(u), src);
+  const unsigned hi = __shfl_sync(0xffffffffu, static_cast<unsigned>(u >> 32), src);
+  return reinterpret_cast<const void*>((static_cast<unsigned long long>(hi) << 32) | lo);
+}
+
+// Store staged columns [0, ncols) of all 32 rows as fp32 at (row_ptr + col0).
+// `sj0` is the first 16-byte chunk (4 floats) of the staged columns.
+__device__ __forceinline__ void flush_f32(const float4* stg, const float* my_row, int col0, int ncols, int lane,
+                                          int sj0 = 0) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    const int j = lane & 7;
+    float* p = const_cast<float*>(static_cast<const float*>(shfl_ptr(my_row, r)));
+    if (p && j * 4 < ncols) *reinterpret_cast<float4*>(p + col0 + j * 4) = stg[r * 8 + ((sj0 + j) ^ (r & 7))];
+  }
+}
+
+// Store staged columns [0, ncols) of all 32 rows as f16 at (row_ptr + col0).
+__device__ __forceinline__ void flush_f16(const float4* stg, const __half* my_row, int col0, int ncols, int lane) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2);
+    const int j = lane & 3;
+    __half* p = const_cast<__half*>(static_cast<const __half*>(shfl_ptr(my_row, r)));
+    if (p && j * 8 < ncols) {
+      const float4 a = stg[r * 8 + ((2 * j) ^ (r & 7))];
+      const float4 b = stg[r * 8 + ((2 * j + 1) ^ (r & 7))];
+      union {
+        __half2 h[4];
+        uint4 u;
+      } pk;
+      pk.h[0] = __floats2half2_rn(a.x, a.y);
+      pk.h[1] = __floats2half2_rn(a.z, a.w);
+      pk.h[2] = __floats2half2_rn(b.x, b.y);
+      pk.h[3] = __floats2half2_rn(b.z, b.w);
+      *reinterpret_cast<uint4*>(p + col0 + j * 8) = pk.u;
+    }
+  }
+}
+
+// Reflect-halo copies of one WaveNet row (the interior row itself goes through
+// the coalesced path): rows t in {1, 2, T-2, T-3} (and more for tiny T) are
+// mirrored into the 2 halo rows on each side of their sequence. NV = 16 or 32 values.
+template <int NV>
+__device__ __forceinline__ void write_halos(__half* xp, int s, int t, int T, int col, const float* v) {
+  if (t > 2 && t < T - 3) return;
   __half* base = xp + static_cast<size_t>(s) * (T + 4) * 512;
-  store_h16(base + static_cast<size_t>(t + 2) * 512 + col, v);
   const int halo[4] = {-2, -1, T, T + 1};
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
-    if (reflect_src(halo[h], T) == t) store_h16(base + static_cast<size_t>(halo[h] + 2) * 512 + col, v);
+    if (reflect_src(halo[h], T) == t) {
+#pragma unroll
+      for (int k = 0; k < NV; k += 16) store_h16(base + static_cast<size_t>(halo[h] + 2) * 512 + col + k, v + k);
+    }
   }
+}
+
+// Epilogue of one 128 x BN tile for this thread's row and column half.
+// `taddr` addresses TMEM lane (quarter*32) at the tile's accumulator buffer.
+// Row-local operands (residual, RoPE pairs, WaveNet state) of the first chunk
+// are fetched before waiting for the accumulator and later ones one chunk
+// ahead; TMEM loads are double-buffered. Returns false if the accumulator
+// wait timed out.
+template <int BN, int EPI>
+__device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int n0, int row, int half, uint32_t taddr,
+                                              const float* sconst, float4* stg, uint64_t* acc_bar, uint32_t parity) {
+  const int lane = row & 31;
+  const int m = m0 + row;
+  const int T = args.seq_T;
+  if constexpr (EPI == kEpiSwiGLU || EPI == kEpiWnGate || EPI == kEpiWnResSkip) {
+    static_assert(BN % 128 == 0, "paired epilogues need 128-column slabs");
+    constexpr int NCH = (BN / 128) * 4;  // chunks of 16 a-columns (+16 b-columns)
+    const int q_begin = half * (NCH / 2), q_end = q_begin + NCH / 2;
+    bool row_ok = m < args.M;
+    int r = m;  // compact row
+    int s = 0, t = 0;
+    if constexpr (EPI == kEpiWnGate) {
+      s = m / (T + 4);
+      const int j = m - s * (T + 4) - 2;
+      row_ok = row_ok && j >= 0 && j < T;
+      r = s * T + j;
+    } else if constexpr (EPI == kEpiWnResSkip) {
+      s = m / T;
+      t = m - s * T;
+    }
+    float msk = 1.0f;
+    const __half* out16_row = nullptr;  // SwiGLU / gate output row
+    __half* xp_row = nullptr;           // res/skip: interior WaveNet row
+    float* acc_row = nullptr;           // res/skip: skip accumulator row
+    if (row_ok) {
+      if constexpr (EPI == kEpiWnResSkip) {
+        msk = args.row_mask[r];
+        xp_row = args.wn_xp + (static_cast<size_t>(s) * (T + 4) + t + 2) * 512;
+        acc_row = args.wn_acc + static_cast<size_t>(r) * 512;
+      } else {
+        out16_row = args.out16 + static_cast<size_t>(r) * args.ld16;
+      }
+    }
+    uint4 xo_cur[2], xo_nxt[2];
+    float ac_cur[16], ac_nxt[16];
+    auto fetch = [&](int q, uint4 (&xo)[2], float (&ac)[16]) {
+      if constexpr (EPI == kEpiWnResSkip) {
+        const int ch = (n0 >> 1) + (q >> 2) * 64 + (q & 3) * 16;
+        if (row_ok) {
+          const uint4* xs = reinterpret_cast<const uint4*>(xp_row + ch);
+          xo[0] = xs[0];
+          xo[1] = xs[1];
+          if (!args.wn_first) load_f32x16(acc_row + ch, ac);
+        }
+      }
+    };
+    auto tcol = [](int q) { return (q >> 2) * 128 + (q & 3) * 16; };  // tile column of the a-chunk
+    fetch(q_begin, xo_cur, ac_cur);
+    if (!mbar_wait(acc_bar, parity, args.status, kDevTimeoutAccum)) return false;
+    tc_fence_after();
+    uint32_t ta[16], tb[16], na_[16], nb_[16];
+    tmem_ld16_async(taddr + tcol(q_begin), ta);
+    tmem_ld16_async(taddr + tcol(q_begin) + 64, tb);
+    tmem_wait_ld();
+    reg_fence16(ta);
+    reg_fence16(tb);
+    // Chunks per store group: two for single-output epilogues, one for the
+    // res/skip update (x and skip values share the stage).
+    constexpr int G = EPI == kEpiWnResSkip ? 1 : 2;
+    float xg[16 * G], bg[16];
+#pragma unroll 1
+    for (int q2 = q_begin; q2 < q_end; q2 += G) {
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const int q = q2 + h;
+        const int ca = tcol(q);
+        const int ci = (q >> 2) * 64 + (q & 3) * 16;  // channel index inside the tile
+        const bool more = q + 1 < q_end;
+        if (more) {
+          tmem_ld16_async(taddr + tcol(q + 1), na_);
+          tmem_ld16_async(taddr + tcol(q + 1) + 64, nb_);
+          fetch(q + 1, xo_nxt, ac_nxt);
+        }
+        float a[16], b[16];
+        u2f16(ta, a);
+        u2f16(tb, b);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          a[e] += sconst[ca + e];
+          b[e] += sconst[ca + 64 + e];
+        }
+        if constexpr (EPI == kEpiSwiGLU) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) xg[h * 16 + e] = silu_f(a[e]) * b[e];
+        } else if constexpr (EPI == kEpiWnGate) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float ga = a[e] + sconst[BN + ci + e];
+            const float gb = b[e] + sconst[BN + BN / 2 + ci + e];
+            xg[h * 16 + e] = tanhf(ga) * sigmoid_f(gb);
+          }
+        } else {  // kEpiWnResSkip
+          union {
+            uint4 u[2];
+            __half2 hh[8];
+          } pk;
+          pk.u[0] = xo_cur[0];
+          pk.u[1] = xo_cur[1];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float2 f = __half22float2(pk.hh[e]);
+            xg[h * 16 + 2 * e] = (f.x + a[2 * e]) * msk;
+            xg[h * 16 + 2 * e + 1] = (f.y + a[2 * e + 1]) * msk;
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) bg[e] = args.wn_first ? b[e] : b[e] + ac_cur[e];
+          xo_cur[0] = xo_nxt[0];
+          xo_cur[1] = xo_nxt[1];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) ac_cur[e] = ac_nxt[e];
+        }
+        stage_put16(stg, lane, h * 16, xg + h * 16);
+        if constexpr (EPI == kEpiWnResSkip) stage_put16(stg, lane, 16, bg);
+        if (more) {
+          tmem_wait_ld();
+          reg_fence16(na_);
+          reg_fence16(nb_);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            ta[e] = na_[e];
+            tb[e] = nb_[e];
+          }
+        }
+      }
+      const int ch0 = (n0 >> 1) + (q2 >> 2) * 64 + (q2 & 3) * 16;
+      __syncwarp();
+      if constexpr (EPI == kEpiWnResSkip) {
+        flush_f16(stg, xp_row, ch0, 16, lane);
+        if (row_ok) write_halos<16>(args.wn_xp, s, t, T, ch0, xg);
+        flush_f32(stg, acc_row, ch0, 16, lane, 4);
+      } else {
+        flush_f16(stg, out16_row, ch0, 32, lane);
+      }
+      __syncwarp();
+    }
+  } else {
+    constexpr int NCH = BN / 16;
+    constexpr int SPLIT = (((NCH + 1) / 2) + 1) & ~1;  // even chunk count of the first half
+    const int c_begin = half ? SPLIT : 0;
+    const int c_end = half ? NCH : (SPLIT < NCH ? SPLIT : NCH);
+    bool row_ok = m < args.M;
+    int s = 0, t = 0;
+    if constexpr (EPI == kEpiQKV || EPI == kEpiConv1Res) {
+      s = m / T;
+      t = m - s * T;
+    }
+    int mo = m;  // output row
+    if constexpr (EPI == kEpiF32) {
+      if (args.pad_rows) {
+        const int sp = m / (T + 4);
+        const int j = m - sp * (T + 4) - 2;
+        row_ok = row_ok && j >= 0 && j < T;
+        mo = sp * T + j;
+      }
+    }
+    // Destination rows (null when the row is out of range).
+    const void* d0 = nullptr;  // primary
+    const void* d1 = nullptr;  // F32: f16 copy; Conv1Res: res projection row
+    if (row_ok) {
+      if constexpr (EPI == kEpiF16 || EPI == kEpiQKV) {
+        d0 = args.out16 + static_cast<size_t>(m) * args.ld16;
+      } else if constexpr (EPI == kEpiF32) {
+        d0 = args.out32 + static_cast<size_t>(mo) * args.ld32;
+        if (args.out16) d1 = args.out16 + static_cast<size_t>(mo) * args.ld16;
+      } else if constexpr (EPI == kEpiWnLast) {
+        d0 = args.out32 + static_cast<size_t>(m) * args.ld32;
+      } else if constexpr (EPI == kEpiConv1Res) {
+        d0 = args.wn_xp + (static_cast<size_t>(s) * (T + 4) + t + 2) * 512;
+        d1 = args.out32 + static_cast<size_t>(m) * args.ld32;
+      }
+    }
+    // Row-local operands: residual (F32), RoPE pairs (QKV), skip accumulator +
+    // res projection (WnLast).
+    float x0_cur[16], x1_cur[16], x0_nxt[16], x1_nxt[16];
+    auto fetch = [&](int c, float (&x0)[16], float (&x1)[16]) {
+      const int n = n0 + c * 16;
+      if (!row_ok || n >= args.N) return;
+      if constexpr (EPI == kEpiF32) {
+        if (args.resid32) load_f32x16(args.resid32 + static_cast<size_t>(mo) * args.ldr + n, x0);
+      } else if constexpr (EPI == kEpiQKV) {
+        if (n < 1024) load_f32x16(reinterpret_cast<const float*>(args.rope + static_cast<size_t>(t) * 32 + ((n & 63) >> 1)), x0);
+      } else if constexpr (EPI == kEpiWnLast) {
+        load_f32x16(args.wn_acc + static_cast<size_t>(m) * 512 + n, x0);
+        load_f32x16(args.wn_res + static_cast<size_t>(m) * 512 + n, x1);
+      }
+    };
+    float msk = 1.0f;
+    if constexpr (EPI == kEpiWnLast) msk = row_ok ? args.row_mask[m] : 0.0f;
+    fetch(c_begin, x0_cur, x1_cur);
+    if (!mbar_wait(acc_bar, parity, args.status, kDevTimeoutAccum)) return false;
+    tc_fence_after();
+    uint32_t tc[16], tn[16];
+    tmem_ld16_async(taddr + c_begin * 16, tc);
+    tmem_wait_ld();
+    reg_fence16(tc);
+    float vg[32];
+#pragma unroll 1
+    for (int cp = c_begin; cp < c_end; cp += 2) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = cp + h;
+        if (c < c_end) {
+          const int n = n0 + c * 16;
+          const bool more = c + 1 < c_end;
+          if (more) {
+            tmem_ld16_async(taddr + (c + 1) * 16, tn);
+            fetch(c + 1, x0_nxt, x1_nxt);
+          }
+          float* v = vg + h * 16;
+          u2f16(tc, v);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] += sconst[c * 16 + e];
+          if constexpr (EPI == kEpiF32) {
+            if (args.resid32) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) v[e] += x0_cur[e];
+            }
+          } else if constexpr (EPI == kEpiQKV) {
+            if (n < 1024) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float cs = x0_cur[2 * e], sn = x0_cur[2 * e + 1];
+                const float xa = v[2 * e], xb = v[2 * e + 1];
+                v[2 * e] = xa * cs - xb * sn;
+                v[2 * e + 1] = xb * cs + xa * sn;
+              }
+              if (n < 512) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] *= 0.125f;
+              }
+            }
+          } else if constexpr (EPI == kEpiWnLast) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = (x0_cur[e] + v[e]) * msk + x1_cur[e];
+          }
+          stage_put16(stg, lane, h * 16, v);
+          if (more) {
+            tmem_wait_ld();
+            reg_fence16(tn);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              tc[e] = tn[e];
+              x0_cur[e] = x0_nxt[e];
+              x1_cur[e] = x1_nxt[e];
+            }
+          }
+        }
+      }
+      // Flush the group (two chunks, or one at the end).
+      const int ng = n0 + cp * 16;
+      int ncols = (cp + 1 < c_end) ? 32 : 16;
+      if (ng + ncols > args.N) ncols = args.N > ng ? args.N - ng : 0;
+      __syncwarp();
+      if constexpr (EPI == kEpiF16 || EPI == kEpiQKV) {
+        flush_f16(stg, static_cast<const __half*>(d0), ng, ncols, lane);
+      } else if constexpr (EPI == kEpiF32) {
+        flush_f32(stg, static_cast<const float*>(d0), ng, ncols, lane);
+        if (args.out16) flush_f16(stg, static_cast<const __half*>(d1), ng, ncols, lane);
+      } else if constexpr (EPI == kEpiWnLast) {
+        flush_f32(stg, static_cast<const float*>(d0), ng, ncols, lane);
+      } else if constexpr (EPI == kEpiConv1Res) {
+        if (ng < 512) {
+          flush_f16(stg, static_cast<const __half*>(d0), ng, ncols, lane);
+          if (row_ok && ncols == 32) write_halos<32>(args.wn_xp, s, t, T, ng, vg);
+        } else {
+          flush_f32(stg, static_cast<const float*>(d1), ng - 512, ncols, lane);
+        }
+      }
+      __syncwarp();
+    }
+  }
+  return true;
 }
 
 template <int BN, int STAGES, int EPI>
@@ -56,28 +446,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int A_BYTES = kBM * kBK * 2;
   constexpr int B_BYTES = BN * kBK * 2;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr int ACC_STRIDE = pow2_cols(BN);  // columns between the two accumulator buffers
+  constexpr uint32_t TMEM_COLS = pow2_cols(2 * ACC_STRIDE);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(2 * ACC_STRIDE <= 512, "two accumulator buffers must fit TMEM");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* accum_bar = empty_bar + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+  uint64_t* acc_full = empty_bar + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* sconst = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);  // [tile_const_floats(BN)]
+  float4* stage_all = reinterpret_cast<float4*>(sconst + tile_const_floats(BN));  // kEpiWarps x 32 x 32 fp32
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM;
-  const int n0 = blockIdx.y * BN;
   const int num_kb = args.num_kb;
+  const int n_tiles = (args.N + BN - 1) / BN;
+  const int num_tiles = ((args.M + kBM - 1) / kBM) * n_tiles;
 
+  if (threadIdx.x == 0) GEMM_TRACE(0);
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kEpiWarps);  // one arrival per epilogue warp
+    }
     fence_barrier_init();
     fence_proxy_async_shared();
     prefetch_tmap(&tmA0);
@@ -92,27 +491,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything below reads or writes memory of the previous kernel in the stream.
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x == 0) GEMM_TRACE(1);
 
   if (warp == 0) {
     if (lane == 0) {
       // ---- TMA producer ----
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&empty_bar[s], ph ^ 1, args.status, kDevTimeoutEmpty)) break;
-        uint8_t* sa = smem + s * STAGE_BYTES;
-        uint8_t* sb = sa + A_BYTES;
-        mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
-        if (args.a_mode == kAConv5) {
-          const int tap = kb / args.kb_per_tap;
-          const int kc = kb - tap * args.kb_per_tap;
-          tma_load_2d(sa, &tmA0, &full_bar[s], kc * kBK, m0 + tap - 2);
-        } else if (args.a_mode == kASplit && kb >= args.kb_split) {
-          tma_load_2d(sa, &tmA1, &full_bar[s], (kb - args.kb_split) * kBK, m0);
-        } else {
-          tma_load_2d(sa, &tmA0, &full_bar[s], kb * kBK, m0);
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * kBM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, args.status, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+          if (args.a_mode == kAConv5) {
+            const int tap = kb / args.kb_per_tap;
+            const int kc = kb - tap * args.kb_per_tap;
+            tma_load_2d(sa, &tmA0, &full_bar[s], kc * kBK, m0 + tap - 2);
+          } else if (args.a_mode == kASplit && kb >= args.kb_split) {
+            tma_load_2d(sa, &tmA1, &full_bar[s], (kb - args.kb_split) * kBK, m0);
+          } else {
+            tma_load_2d(sa, &tmA0, &full_bar[s], kb * kBK, m0);
+          }
+          tma_load_2d(sb, &tmB, &full_bar[s], kb * kBK, n0);
+          if (it == 0) GEMM_TRACE(2);
         }
-        tma_load_2d(sb, &tmB, &full_bar[s], kb * kBK, n0);
       }
     }
     __syncwarp();
@@ -120,175 +533,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---- MMA issuer ----
       constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&full_bar[s], ph, args.status, kDevTimeoutFull)) break;
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int a = local & 1;
+        if (!mbar_wait(&acc_empty[a], ((local >> 1) & 1) ^ 1, args.status, kDevTimeoutAccum)) break;
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t sb = sa + A_BYTES;
+        const uint32_t d = tmem_base + static_cast<uint32_t>(a * ACC_STRIDE);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full_bar[s], ph, args.status, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (it == 0) GEMM_TRACE(3);
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          umma_f16_ss(tmem_base, sdesc_k_sw128(sa + k * 32), sdesc_k_sw128(sb + k * 32), idesc,
-                      (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_f16_ss(d, sdesc_k_sw128(sa + k * 32), sdesc_k_sw128(sb + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[s]);
         }
-        umma_commit(&empty_bar[s]);
+        umma_commit(&acc_full[a]);
+        if (local == 0) GEMM_TRACE(4);
       }
-      umma_commit(accum_bar);
     }
     __syncwarp();
   } else {
-    // ---- epilogue: warps 2..5 ----
+    // ---- epilogue: warps 2..(2 + kEpiWarps) ----
     const int quarter = warp & 3;
+    const int half = (warp - 2) / 4;
     const int row = quarter * 32 + lane;
-    const int m = m0 + row;
-    const bool ok = mbar_wait(accum_bar, 0, args.status, kDevTimeoutAccum);
-    tc_fence_after();
-    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-    if (ok) {
-      const int T = args.seq_T;
-      if constexpr (EPI == kEpiSwiGLU || EPI == kEpiWnGate || EPI == kEpiWnResSkip) {
-        static_assert(BN % 128 == 0, "paired epilogues need 128-column slabs");
-        // Row-space bookkeeping.
-        bool row_ok = m < args.M;
-        int r = m;  // compact row
-        int s = 0, t = 0;
-        if constexpr (EPI == kEpiWnGate) {
-          s = m / (T + 4);
-          const int j = m - s * (T + 4) - 2;
-          row_ok = row_ok && j >= 0 && j < T;
-          r = s * T + j;
-        } else if constexpr (EPI == kEpiWnResSkip) {
-          s = m / T;
-          t = m - s * T;
-        }
-        float msk = 1.0f;
-        if constexpr (EPI == kEpiWnResSkip) msk = row_ok ? args.row_mask[r] : 0.0f;
-#pragma unroll 1
-        for (int slab = 0; slab < BN / 128; ++slab) {
-#pragma unroll 1
-          for (int i = 0; i < 4; ++i) {
-            const int ca = slab * 128 + i * 16;
-            const int na = n0 + ca;
-            float a[16], b[16];
-            tmem_ld16(taddr + ca, a);
-            tmem_ld16(taddr + ca + 64, b);
-            if (row_ok && na < args.N) {
-            const int ch = (n0 >> 1) + slab * 64 + i * 16;
-            if (args.bias) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                a[e] += args.bias[na + e];
-                b[e] += args.bias[na + 64 + e];
-              }
-            }
-            if constexpr (EPI == kEpiSwiGLU) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) a[e] = silu_f(a[e]) * b[e];
-              store_h16(args.out16 + static_cast<size_t>(r) * args.ld16 + ch, a);
-            } else if constexpr (EPI == kEpiWnGate) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                const float ga = a[e] + args.wn_cond[ch + e];
-                const float gb = b[e] + args.wn_cond[512 + ch + e];
-                a[e] = tanhf(ga) * sigmoid_f(gb);
-              }
-              store_h16(args.out16 + static_cast<size_t>(r) * args.ld16 + ch, a);
-            } else {  // kEpiWnResSkip
-              float x[16];
-              __half* xrow = args.wn_xp + (static_cast<size_t>(s) * (T + 4) + t + 2) * 512 + ch;
-              load_h16(xrow, x);
-#pragma unroll
-              for (int e = 0; e < 16; ++e) x[e] = (x[e] + a[e]) * msk;
-              write_xp16(args.wn_xp, s, t, T, ch, x);
-              float* acc = args.wn_acc + static_cast<size_t>(r) * 512 + ch;
-              if (!args.wn_first) {
-                float o[16];
-                load_f32x16(acc, o);
-#pragma unroll
-                for (int e = 0; e < 16; ++e) b[e] += o[e];
-              }
-              store_f32x16(acc, b);
-            }
-            }
-          }
-        }
-      } else {
-        bool row_ok = m < args.M;
-        int s = 0, t = 0;
-        if constexpr (EPI == kEpiQKV || EPI == kEpiConv1Res) {
-          s = m / T;
-          t = m - s * T;
-        }
-        int mo = m;  // output row
-        if constexpr (EPI == kEpiF32) {
-          if (args.pad_rows) {
-            const int sp = m / (T + 4);
-            const int j = m - sp * (T + 4) - 2;
-            row_ok = row_ok && j >= 0 && j < T;
-            mo = sp * T + j;
-          }
-        }
-        float msk = 1.0f;
-        if constexpr (EPI == kEpiWnLast) msk = row_ok ? args.row_mask[m] : 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          const int n = n0 + c;
-          float v[16];
-          tmem_ld16(taddr + c, v);
-          if (row_ok && n < args.N) {
-          if (args.bias) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] += args.bias[n + e];
-          }
-          if constexpr (EPI == kEpiF16) {
-            store_h16(args.out16 + static_cast<size_t>(m) * args.ld16 + n, v);
-          } else if constexpr (EPI == kEpiF32) {
-            if (args.resid32) {
-              float rr[16];
-              load_f32x16(args.resid32 + static_cast<size_t>(mo) * args.ldr + n, rr);
-#pragma unroll
-              for (int e = 0; e < 16; ++e) v[e] += rr[e];
-            }
-            store_f32x16(args.out32 + static_cast<size_t>(mo) * args.ld32 + n, v);
-            if (args.out16) store_h16(args.out16 + static_cast<size_t>(mo) * args.ld16 + n, v);
-          } else if constexpr (EPI == kEpiQKV) {
-            if (n < 1024) {
-              const int d0 = n & 63;  // column inside the head
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float2 cs = args.rope[static_cast<size_t>(t) * 32 + (d0 >> 1) + e];
-                const float x0 = v[2 * e], x1 = v[2 * e + 1];
-                v[2 * e] = x0 * cs.x - x1 * cs.y;
-                v[2 * e + 1] = x1 * cs.x + x0 * cs.y;
-              }
-              if (n < 512) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] *= 0.125f;
-              }
-            }
-            store_h16(args.out16 + static_cast<size_t>(m) * args.ld16 + n, v);
-          } else if constexpr (EPI == kEpiWnLast) {
-            float o[16], rr[16];
-            load_f32x16(args.wn_acc + static_cast<size_t>(m) * 512 + n, o);
-            load_f32x16(args.wn_res + static_cast<size_t>(m) * 512 + n, rr);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = (o[e] + v[e]) * msk + rr[e];
-            store_f32x16(args.out32 + static_cast<size_t>(m) * args.ld32 + n, v);
-          } else if constexpr (EPI == kEpiConv1Res) {
-            if (n < 512) {
-              write_xp16(args.wn_xp, s, t, T, n, v);
-            } else {
-              store_f32x16(args.out32 + static_cast<size_t>(m) * args.ld32 + (n - 512), v);
-            }
-          }
-          }
-        }
-      }
+    const int etid = threadIdx.x - 64;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int a = local & 1;
+      const int m0 = (tile / n_tiles) * kBM;
+      const int n0 = (tile % n_tiles) * BN;
+      epi_bar();  // every epilogue thread is done with the previous tile's constants
+      stage_tile_consts<BN, EPI>(args, n0, sconst, etid);
+      epi_bar();
+      const bool ok = epilogue_tile<BN, EPI>(args, m0, n0, row, half,
+                                             tmem_base + lane_off + static_cast<uint32_t>(a * ACC_STRIDE), sconst,
+                                             stage_all + (warp - 2) * (kStageFloats / 4), &acc_full[a],
+                                             (local >> 1) & 1);
+      if (!ok) break;
+      if (local == 0 && warp == 2 && lane == 0) GEMM_TRACE(5);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (local == 0 && warp == 2 && lane == 0) GEMM_TRACE(6);
     }
-    tc_fence_before();
   }
   __syncthreads();
+  if (threadIdx.x == 0) GEMM_TRACE(7);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
@@ -312,8 +614,19 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int BN, int STAGES, int EPI>
+int sm_count() {
+  static int n = [] {
+    int dev = 0, v = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v > 0 ? v : 148;
+  }();
+  return n;
+}
+
+template <int BN, int EPI>
 cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
+  constexpr int STAGES = gemm_stages(BN);
   auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
   const size_t smem = gemm_smem_bytes(BN, STAGES);
   // The shared-memory opt-in is set once per device for each instantiation.
@@ -326,26 +639,26 @@ cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit);
   }
-  dim3 grid((g.args.M + kBM - 1) / kBM, (g.args.N + BN - 1) / BN);
-  kern<<<grid, kThreads, smem, stream>>>(g.tmA0, g.tmA1, g.tmB, g.args);
-  return cudaGetLastError();
+  const int tiles = ((g.args.M + kBM - 1) / kBM) * ((g.args.N + BN - 1) / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  return launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, g.tmA0, g.tmA1, g.tmB, g.args);
 }
 
-template <int BN, int STAGES>
+template <int BN>
 cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream) {
   switch (g.args.epi) {
-    case kEpiF16: return launch_t<BN, STAGES, kEpiF16>(g, stream);
-    case kEpiF32: return launch_t<BN, STAGES, kEpiF32>(g, stream);
-    case kEpiQKV: return launch_t<BN, STAGES, kEpiQKV>(g, stream);
-    case kEpiWnLast: return launch_t<BN, STAGES, kEpiWnLast>(g, stream);
-    case kEpiConv1Res: return launch_t<BN, STAGES, kEpiConv1Res>(g, stream);
+    case kEpiF16: return launch_t<BN, kEpiF16>(g, stream);
+    case kEpiF32: return launch_t<BN, kEpiF32>(g, stream);
+    case kEpiQKV: return launch_t<BN, kEpiQKV>(g, stream);
+    case kEpiWnLast: return launch_t<BN, kEpiWnLast>(g, stream);
+    case kEpiConv1Res: return launch_t<BN, kEpiConv1Res>(g, stream);
     default: break;
   }
   if constexpr (BN % 128 == 0) {
     switch (g.args.epi) {
-      case kEpiSwiGLU: return launch_t<BN, STAGES, kEpiSwiGLU>(g, stream);
-      case kEpiWnGate: return launch_t<BN, STAGES, kEpiWnGate>(g, stream);
-      case kEpiWnResSkip: return launch_t<BN, STAGES, kEpiWnResSkip>(g, stream);
+      case kEpiSwiGLU: return launch_t<BN, kEpiSwiGLU>(g, stream);
+      case kEpiWnGate: return launch_t<BN, kEpiWnGate>(g, stream);
+      case kEpiWnResSkip: return launch_t<BN, kEpiWnResSkip>(g, stream);
       default: break;
     }
   }
@@ -355,7 +668,27 @@ cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 size_t gemm_smem_bytes(int bn, int stages) {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * (kBM * kBK * 2 + bn * kBK * 2) + 256;
+  return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * (kBM * kBK * 2 + bn * kBK * 2) + 256 /*barriers*/ +
+         static_cast<size_t>(tile_const_floats(bn)) * 4 + kEpiWarps * kStageFloats * 4 /*epilogue stages*/;
+}
+
+int gemm_pick_bn(int M, int N, bool paired) {
+  const int sms = sm_count();
+  const int m_tiles = (M + kBM - 1) / kBM;
+  int best = 0;
+  double best_cost = 0.0;
+  for (int bn : {256, 128, 64}) {
+    if (paired && bn % 128) continue;
+    if (N % bn && bn > N) continue;
+    const int tiles = m_tiles * ((N + bn - 1) / bn);
+    const int waves = (tiles + sms - 1) / sms;
+    const double cost = static_cast<double>(waves) * (bn + 64);
+    if (best == 0 || cost < best_cost - 1e-9) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
@@ -376,9 +709,10 @@ bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t ro
 cudaError_t gemm_run(const GemmLaunch& g, cudaStream_t stream) {
   if (g.args.M <= 0 || g.args.N <= 0 || g.args.num_kb <= 0) return cudaErrorInvalidValue;
   switch (g.bn) {
-    case 80: return launch_epi<80, 4>(g, stream);
-    case 128: return g.stages <= 3 ? launch_epi<128, 3>(g, stream) : launch_epi<128, 4>(g, stream);
-    case 256: return launch_epi<256, 4>(g, stream);
+    case 64: return launch_epi<64>(g, stream);
+    case 80: return launch_epi<80>(g, stream);
+    case 128: return launch_epi<128>(g, stream);
+    case 256: return launch_epi<256>(g, stream);
     default: return cudaErrorInvalidValue;
   }
 }

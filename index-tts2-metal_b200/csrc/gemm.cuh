@@ -67,10 +67,22 @@ struct GemmLaunch {
   int stages;
 };
 
+// Pipeline depth for a tile width: as many 64-deep k-blocks as fit next to the
+// epilogue's shared memory (constants, 8 x 4 KB store stages, barriers) in
+// the 227 KB a CTA may use.
+constexpr int gemm_stages(int bn) {
+  return ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / (128 * 64 * 2 + bn * 64 * 2)) > 8
+             ? 8
+             : ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / (128 * 64 * 2 + bn * 64 * 2));
+}
+
 // Host helpers (gemm.cu).
 bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
                    uint32_t box_rows);
 cudaError_t gemm_run(const GemmLaunch& g, cudaStream_t stream);
 size_t gemm_smem_bytes(int bn, int stages);
+// Tile width (64, 128 or 256; paired epilogues need a multiple of 128) that
+// minimises waves x per-tile cost for an M x N output on this GPU.
+int gemm_pick_bn(int M, int N, bool paired);
 
 }  // namespace itts

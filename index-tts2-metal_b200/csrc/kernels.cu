@@ -7,12 +7,21 @@
 #include <stdint.h>
 
 #include "kernels.cuh"
+#include "launch.cuh"
+#include "ptx.cuh"
 
 namespace itts {
 
 namespace {
 
 constexpr int kC = 512;
+
+// Kernels of the sampler graph are launched with programmatic dependent
+// launch; each starts by waiting for its predecessor's memory.
+__device__ __forceinline__ void pdl_entry() {
+  griddep_wait();
+  griddep_launch();
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -34,6 +43,7 @@ __device__ __forceinline__ void store_h4(__half* dst, float a, float b, float c,
 // with cpu_rmsnorm (runtime/impl/tokenizer_tests.cpp:3012-3024), eps 1e-5.
 __global__ void __launch_bounds__(256) adarms_kernel(const float* __restrict__ x, int R, const float* __restrict__ wb,
                                                      const float* __restrict__ gamma, __half* __restrict__ out) {
+  pdl_entry();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
@@ -64,6 +74,7 @@ __global__ void __launch_bounds__(256) adarms_kernel(const float* __restrict__ x
 // with cpu_layernorm (runtime/impl/tokenizer_tests.cpp:2992-3010), eps 1e-6.
 __global__ void __launch_bounds__(256) adaln_kernel(const float* __restrict__ x, int R, const float* __restrict__ ss,
                                                     __half* __restrict__ out) {
+  pdl_entry();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
@@ -101,6 +112,7 @@ __global__ void __launch_bounds__(256) adaln_kernel(const float* __restrict__ x,
 // Sequence order in the velocity buffer: s = u * branches + branch.
 __global__ void euler_kernel(float* __restrict__ X, const float* __restrict__ V, __half* __restrict__ XD,
                              const int* __restrict__ prompt_len, int B, int T, int branches, float dt, float cfg) {
+  pdl_entry();
   const size_t total = static_cast<size_t>(B) * T * 80;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -124,6 +136,7 @@ __global__ void euler_kernel(float* __restrict__ X, const float* __restrict__ V,
 
 __global__ void euler_init_kernel(const float* X0, float* X, __half* __restrict__ XD,
                                   const int* __restrict__ prompt_len, int B, int T, int branches) {
+  pdl_entry();
   const size_t total = static_cast<size_t>(B) * T * 80;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -141,6 +154,7 @@ __global__ void euler_init_kernel(const float* X0, float* X, __half* __restrict_
 }
 
 __global__ void to_half_kernel(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+  pdl_entry();
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     y[i] = __float2half_rn(x[i]);
@@ -151,6 +165,7 @@ __global__ void to_half_kernel(const float* __restrict__ x, __half* __restrict__
 __global__ void merge_input_kernel(const float* __restrict__ prompt_x, const __half* __restrict__ cp16,
                                    const float* __restrict__ bcp, const float* __restrict__ style,
                                    __half* __restrict__ U, int B, int T, int branches) {
+  pdl_entry();
   constexpr int W = 784;
   const size_t total = static_cast<size_t>(B) * branches * T * W;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
@@ -226,39 +241,35 @@ inline unsigned grid_for(size_t n, int threads) {
 }  // namespace
 
 cudaError_t adarms_run(const float* x, int R, const float* wb, const float* gamma, __half* out, cudaStream_t st) {
-  adarms_kernel<<<(R + 7) / 8, 256, 0, st>>>(x, R, wb, gamma, out);
-  return cudaGetLastError();
+  return launch_pdl(adarms_kernel, dim3((R + 7) / 8), dim3(256), 0, st, x, R, wb, gamma, out);
 }
 
 cudaError_t adaln_run(const float* x, int R, const float* ss, __half* out, cudaStream_t st) {
-  adaln_kernel<<<(R + 7) / 8, 256, 0, st>>>(x, R, ss, out);
-  return cudaGetLastError();
+  return launch_pdl(adaln_kernel, dim3((R + 7) / 8), dim3(256), 0, st, x, R, ss, out);
 }
 
 cudaError_t euler_run(float* X, const float* V, __half* XD, const int* prompt_len, int B, int T, int branches,
                       float dt, float cfg, cudaStream_t st) {
   const size_t n = static_cast<size_t>(B) * T * 80;
-  euler_kernel<<<grid_for(n, 256), 256, 0, st>>>(X, V, XD, prompt_len, B, T, branches, dt, cfg);
-  return cudaGetLastError();
+  return launch_pdl(euler_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, X, V, XD, prompt_len, B, T, branches, dt,
+                    cfg);
 }
 
 cudaError_t euler_init_run(const float* X0, float* X, __half* XD, const int* prompt_len, int B, int T, int branches,
                            cudaStream_t st) {
   const size_t n = static_cast<size_t>(B) * T * 80;
-  euler_init_kernel<<<grid_for(n, 256), 256, 0, st>>>(X0, X, XD, prompt_len, B, T, branches);
-  return cudaGetLastError();
+  return launch_pdl(euler_init_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, X0, X, XD, prompt_len, B, T, branches);
 }
 
 cudaError_t to_half_run(const float* x, __half* y, size_t n, cudaStream_t st) {
-  to_half_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
-  return cudaGetLastError();
+  return launch_pdl(to_half_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, x, y, n);
 }
 
 cudaError_t merge_input_run(const float* prompt_x, const __half* cp16, const float* bcp, const float* style,
                             __half* U, int B, int T, int branches, cudaStream_t st) {
   const size_t n = static_cast<size_t>(B) * branches * T * 784;
-  merge_input_kernel<<<grid_for(n, 256), 256, 0, st>>>(prompt_x, cp16, bcp, style, U, B, T, branches);
-  return cudaGetLastError();
+  return launch_pdl(merge_input_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, prompt_x, cp16, bcp, style, U, B, T,
+                    branches);
 }
 
 cudaError_t gemv_f16w_run(const __half* W, const float* bias, const float* x, int ldx, float* y, int ldy, int N,

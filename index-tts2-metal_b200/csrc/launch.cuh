@@ -1,0 +1,38 @@
+// Kernel launch with programmatic dependent launch (PDL): the next kernel in
+// the stream may start its prologue while this one drains. Every kernel
+// launched through here calls griddep_wait() before it touches memory written
+// by its predecessor, so ordering is preserved. ITTS_PDL=0 in the environment
+// turns the attribute off (plain stream order).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <utility>
+
+namespace itts {
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("ITTS_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+}  // namespace itts
