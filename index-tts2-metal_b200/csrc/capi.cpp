@@ -368,14 +368,16 @@ int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a
     itts::GemmLaunch g;
     std::memset(&g, 0, sizeof(g));
     const uint32_t ka = a1 ? k0 : K;
-    need(!a1 || (k0 % 64 == 0 && k0 < K), "k0 must be a multiple of 64 below K");
-    if (!itts::make_tmap_f16(&g.tmA0, a0, ka, M, lda0, 128)) throw ShapeError("A0 layout rejected by TMA");
+    need(!a1 || (k0 % 128 == 0 && k0 < K), "k0 must be a multiple of 128 below K");
+    need(K % 64 == 0, "K must be a multiple of 64 (zero-pad the operands)");
+    const uint32_t kbox = static_cast<uint32_t>(itts::gemm_kbox(static_cast<int>(bn)));
+    if (!itts::make_tmap_f16(&g.tmA0, a0, ka, M, lda0, 128, kbox)) throw ShapeError("A0 layout rejected by TMA");
     if (a1) {
-      if (!itts::make_tmap_f16(&g.tmA1, a1, K - k0, M, lda1, 128)) throw ShapeError("A1 layout rejected by TMA");
+      if (!itts::make_tmap_f16(&g.tmA1, a1, K - k0, M, lda1, 128, kbox)) throw ShapeError("A1 layout rejected by TMA");
     } else {
       g.tmA1 = g.tmA0;
     }
-    if (!itts::make_tmap_f16(&g.tmB, b, K, N, ldb, bn)) throw ShapeError("B layout rejected by TMA");
+    if (!itts::make_tmap_f16(&g.tmB, b, K, N, ldb, bn, kbox)) throw ShapeError("B layout rejected by TMA");
     g.args.M = static_cast<int>(M);
     g.args.N = static_cast<int>(N);
     g.args.a_mode = a1 ? itts::kASplit : itts::kAPlain;
@@ -403,9 +405,9 @@ int itts_op_conv5(itts_cfm_ctx* ctx, const void* xp, uint32_t S, uint32_t T, con
     itts::GemmLaunch g;
     std::memset(&g, 0, sizeof(g));
     const uint32_t Rp = S * (T + 4);
-    if (!itts::make_tmap_f16(&g.tmA0, xp, 512, Rp, 512, 128)) throw ShapeError("xp layout rejected by TMA");
+    if (!itts::make_tmap_f16(&g.tmA0, xp, 512, Rp, 512, 128, 2)) throw ShapeError("xp layout rejected by TMA");
     g.tmA1 = g.tmA0;
-    if (!itts::make_tmap_f16(&g.tmB, w, 2560, N, 2560, 128)) throw ShapeError("w layout rejected by TMA");
+    if (!itts::make_tmap_f16(&g.tmB, w, 2560, N, 2560, 128, 2)) throw ShapeError("w layout rejected by TMA");
     g.args.M = static_cast<int>(Rp);
     g.args.N = static_cast<int>(N);
     g.args.a_mode = itts::kAConv5;

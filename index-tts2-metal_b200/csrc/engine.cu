@@ -33,15 +33,16 @@ GemmLaunch make_gemm(Operand a0, Operand a1, Operand b, int M, int N, int K, int
   GemmLaunch g;
   std::memset(&g, 0, sizeof(g));
   if (bn == 0) bn = gemm_pick_bn(M, N, epi == kEpiSwiGLU || epi == kEpiWnGate || epi == kEpiWnResSkip);
-  if (!make_tmap_f16(&g.tmA0, a0.p, a0.cols, a0.rows, a0.ld, 128))
+  const uint32_t kbox = static_cast<uint32_t>(gemm_kbox(bn));
+  if (!make_tmap_f16(&g.tmA0, a0.p, a0.cols, a0.rows, a0.ld, 128, kbox))
     throw std::runtime_error("gemm: tensor map for A0 rejected");
   if (a1.p) {
-    if (!make_tmap_f16(&g.tmA1, a1.p, a1.cols, a1.rows, a1.ld, 128))
+    if (!make_tmap_f16(&g.tmA1, a1.p, a1.cols, a1.rows, a1.ld, 128, kbox))
       throw std::runtime_error("gemm: tensor map for A1 rejected");
   } else {
     g.tmA1 = g.tmA0;
   }
-  if (!make_tmap_f16(&g.tmB, b.p, b.cols, b.rows, b.ld, static_cast<uint32_t>(bn)))
+  if (!make_tmap_f16(&g.tmB, b.p, b.cols, b.rows, b.ld, static_cast<uint32_t>(bn), kbox))
     throw std::runtime_error("gemm: tensor map for B rejected");
   g.args.M = M;
   g.args.N = N;
@@ -202,49 +203,46 @@ Work* Engine::work(int B, int T, int branches) {
   w->R = w->S * T;
   w->Rp = w->S * (T + 4);
   const size_t R = w->R, BT = static_cast<size_t>(B) * T;
-  // Size pass then carve.
-  size_t bytes = 0;
-  auto sz = [&](size_t n, size_t es) { bytes += (n * es + 255) & ~size_t(255); };
-  sz(BT * 80, 4); sz(BT * 80, 4); sz(R * 80, 2); sz(BT * 80, 4); sz(BT * 512, 4); sz(static_cast<size_t>(B) * 192, 4); sz(B, 4);
-  sz(R, 4); sz(BT * 512, 2); sz(BT * 512, 2); sz(R * 784, 2); sz(R * 512, 4);
-  sz(R * 512, 4); sz(R * 512, 2); for (int i = 0; i < 6; ++i) sz(R * 512, 2); sz(R * 512, 2); sz(R * 1536, 2);
-  sz(R * 512, 2); sz(R * 512, 4); sz(R * 1536, 2);
-  sz(R * 512, 2); sz(static_cast<size_t>(w->Rp) * 512, 2); sz(R * 512, 4); sz(R * 512, 2); sz(R * 512, 4);
-  sz(R * 512, 4); sz(R * 512, 2); sz(R * 512, 2); sz(R * 80, 4); sz(static_cast<size_t>(T) * 32, 8);
+  // One carve sequence, run twice: first from address 0 to measure the arena,
+  // then over the allocation (so sizes and offsets can never disagree).
+  auto layout = [&](uint8_t* cur) {
+    w->X0 = carve<float>(cur, BT * 80);
+    w->X = carve<float>(cur, BT * 80);
+    w->XD = carve<__half>(cur, R * kXdLd);
+    w->prompt_x = carve<float>(cur, BT * 80);
+    w->cond = carve<float>(cur, BT * 512);
+    w->style = carve<float>(cur, static_cast<size_t>(B) * 192);
+    w->plen = carve<int>(cur, B);
+    w->mask = carve<float>(cur, R);
+    w->cond16 = carve<__half>(cur, BT * 512);
+    w->cp16 = carve<__half>(cur, BT * 512);
+    w->U = carve<__half>(cur, R * kUld);
+    w->base = carve<float>(cur, R * 512);
+    w->xres = carve<float>(cur, R * 512);
+    w->x16 = carve<__half>(cur, R * 512);
+    for (int i = 0; i < 6; ++i) w->skip16[i] = carve<__half>(cur, R * 512);
+    w->xn16 = carve<__half>(cur, R * 512);
+    w->qkv16 = carve<__half>(cur, R * 1536);
+    w->attn16 = carve<__half>(cur, R * 512);
+    w->h = carve<float>(cur, R * 512);
+    w->g16 = carve<__half>(cur, R * 1536);
+    w->ls16 = carve<__half>(cur, R * 512);
+    w->xp16 = carve<__half>(cur, static_cast<size_t>(w->Rp) * 512);
+    w->res = carve<float>(cur, R * 512);
+    w->gate16 = carve<__half>(cur, R * 512);
+    w->wacc = carve<float>(cur, R * 512);
+    w->fin = carve<float>(cur, R * 512);
+    w->fn16 = carve<__half>(cur, R * 512);
+    w->fh16 = carve<__half>(cur, R * 512);
+    w->vel = carve<float>(cur, R * 80);
+    w->rope = carve<float2>(cur, static_cast<size_t>(T) * 32);
+    return cur;
+  };
+  const size_t bytes = static_cast<size_t>(layout(nullptr) - static_cast<uint8_t*>(nullptr));
   check(cudaMalloc(&w->arena, bytes), "workspace cudaMalloc");
   w->arena_bytes = bytes;
   check(cudaMemset(w->arena, 0, bytes), "workspace memset");
-  uint8_t* cur = static_cast<uint8_t*>(w->arena);
-  w->X0 = carve<float>(cur, BT * 80);
-  w->X = carve<float>(cur, BT * 80);
-  w->XD = carve<__half>(cur, R * 80);
-  w->prompt_x = carve<float>(cur, BT * 80);
-  w->cond = carve<float>(cur, BT * 512);
-  w->style = carve<float>(cur, static_cast<size_t>(B) * 192);
-  w->plen = carve<int>(cur, B);
-  w->mask = carve<float>(cur, R);
-  w->cond16 = carve<__half>(cur, BT * 512);
-  w->cp16 = carve<__half>(cur, BT * 512);
-  w->U = carve<__half>(cur, R * 784);
-  w->base = carve<float>(cur, R * 512);
-  w->xres = carve<float>(cur, R * 512);
-  w->x16 = carve<__half>(cur, R * 512);
-  for (int i = 0; i < 6; ++i) w->skip16[i] = carve<__half>(cur, R * 512);
-  w->xn16 = carve<__half>(cur, R * 512);
-  w->qkv16 = carve<__half>(cur, R * 1536);
-  w->attn16 = carve<__half>(cur, R * 512);
-  w->h = carve<float>(cur, R * 512);
-  w->g16 = carve<__half>(cur, R * 1536);
-  w->ls16 = carve<__half>(cur, R * 512);
-  w->xp16 = carve<__half>(cur, static_cast<size_t>(w->Rp) * 512);
-  w->res = carve<float>(cur, R * 512);
-  w->gate16 = carve<__half>(cur, R * 512);
-  w->wacc = carve<float>(cur, R * 512);
-  w->fin = carve<float>(cur, R * 512);
-  w->fn16 = carve<__half>(cur, R * 512);
-  w->fh16 = carve<__half>(cur, R * 512);
-  w->vel = carve<float>(cur, R * 80);
-  w->rope = carve<float2>(cur, static_cast<size_t>(T) * 32);
+  layout(static_cast<uint8_t*>(w->arena));
   // RoPE table with the reference's float arithmetic (apply_rope_inplace,
   // runtime/impl/tokenizer_tests.cpp:4266-4281).
   std::vector<float2> rope(static_cast<size_t>(T) * 32);
@@ -277,12 +275,12 @@ void Engine::build_work_launches(Work* w) {
   w->g_cp.args.bias = w_.bcp;
   w->g_cp.args.out16 = w->cp16;
   w->g_cp.args.ld16 = 512;
-  w->g_base = make_gemm(act(w->U, 784, R), none, wt(w_.wrest, 784, 512), R, 512, 784, kAPlain, 0, 0, 0, kEpiF32);
+  w->g_base = make_gemm(act(w->U, kUld, R), none, wt(w_.wrest, kUld, 512), R, 512, kUld, kAPlain, 0, 0, 0, kEpiF32);
   w->g_base.args.bias = w_.bm;
   w->g_base.args.out32 = w->base;
   w->g_base.args.ld32 = 512;
   // Per step: x slice of the merge + base.
-  w->g_merge = make_gemm(act(w->XD, 80, R), none, wt(w_.wx, 80, 512), R, 512, 80, kAPlain, 0, 0, 0, kEpiF32);
+  w->g_merge = make_gemm(act(w->XD, kXdLd, R), none, wt(w_.wx, kXdLd, 512), R, 512, kXdLd, kAPlain, 0, 0, 0, kEpiF32);
   w->g_merge.args.resid32 = w->base;
   w->g_merge.args.ldr = 512;
   w->g_merge.args.out32 = w->xres;
@@ -321,7 +319,8 @@ void Engine::build_work_launches(Work* w) {
       w->g_w2[l].args.ld16 = 512;
     }
   }
-  w->g_sl = make_gemm(act(w->xn16, 512, R), act(w->XD, 80, R), wt(w_.wsl, 592, 512), R, 512, 640, kASplit, 8, 0, 0,
+  w->g_sl = make_gemm(act(w->xn16, 512, R), act(w->XD, kXdLd, R), wt(w_.wsl, 512 + kXdLd, 512), R, 512, 512 + kXdLd,
+                      kASplit, 8, 0, 0,
                       kEpiF16);
   w->g_sl.args.bias = w_.bsl;
   w->g_sl.args.out16 = w->ls16;

@@ -34,7 +34,7 @@ struct Work {
   // inputs / state
   float* X0 = nullptr;        // [B*T, 80] initial noise (kept for replays)
   float* X = nullptr;         // [B*T, 80] mel state (fp32)
-  __half* XD = nullptr;       // [S*T, 80] f16 copy per branch (GEMM operand)
+  __half* XD = nullptr;       // [S*T, kXdLd] f16 copy per branch (GEMM operand; columns >= 80 stay 0)
   float* prompt_x = nullptr;  // [B*T, 80]
   float* cond = nullptr;      // [B*T, 512]
   float* style = nullptr;     // [B, 192]
@@ -43,7 +43,7 @@ struct Work {
   // step-invariant merge
   __half* cond16 = nullptr;
   __half* cp16 = nullptr;
-  __half* U = nullptr;    // [R, 784]
+  __half* U = nullptr;    // [R, kUld] (columns >= 784 stay 0)
   float* base = nullptr;  // [R, 512]
   // transformer
   float* xres = nullptr;

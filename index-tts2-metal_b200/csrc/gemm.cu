@@ -443,8 +443,11 @@ template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
-  constexpr int A_BYTES = kBM * kBK * 2;
-  constexpr int B_BYTES = BN * kBK * 2;
+  constexpr int KBOX = gemm_kbox(BN);      // k-blocks per stage (one TMA box per operand)
+  constexpr int A_KB = kBM * kBK * 2;       // one 128 x 64 k-block of A
+  constexpr int B_KB = BN * kBK * 2;        // one BN x 64 k-block of B
+  constexpr int A_BYTES = KBOX * A_KB;
+  constexpr int B_BYTES = KBOX * B_KB;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr int ACC_STRIDE = pow2_cols(BN);  // columns between the two accumulator buffers
   constexpr uint32_t TMEM_COLS = pow2_cols(2 * ACC_STRIDE);
@@ -463,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_kb = args.num_kb;
+  const int num_sb = (args.num_kb + KBOX - 1) / KBOX;  // stages per tile (a missing k-block reads zeros)
   const int n_tiles = (args.N + BN - 1) / BN;
   const int num_tiles = ((args.M + kBM - 1) / kBM) * n_tiles;
 
@@ -504,7 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * kBM;
         const int n0 = (tile % n_tiles) * BN;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int sbk = 0; sbk < num_sb; ++sbk, ++it) {
+          const int kb = sbk * KBOX;  // first k-block of the stage (kb_split and kb_per_tap are multiples of KBOX)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty_bar[s], ph ^ 1, args.status, kDevTimeoutEmpty)) {
@@ -517,13 +521,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (args.a_mode == kAConv5) {
             const int tap = kb / args.kb_per_tap;
             const int kc = kb - tap * args.kb_per_tap;
-            tma_load_2d(sa, &tmA0, &full_bar[s], kc * kBK, m0 + tap - 2);
+            tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0 + tap - 2, kc);
           } else if (args.a_mode == kASplit && kb >= args.kb_split) {
-            tma_load_2d(sa, &tmA1, &full_bar[s], (kb - args.kb_split) * kBK, m0);
+            tma_load_3d(sa, &tmA1, &full_bar[s], 0, m0, kb - args.kb_split);
           } else {
-            tma_load_2d(sa, &tmA0, &full_bar[s], kb * kBK, m0);
+            tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0, kb);
           }
-          tma_load_2d(sb, &tmB, &full_bar[s], kb * kBK, n0);
+          tma_load_3d(sb, &tmB, &full_bar[s], 0, n0, kb);
           if (it == 0) GEMM_TRACE(2);
         }
       }
@@ -540,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&acc_empty[a], ((local >> 1) & 1) ^ 1, args.status, kDevTimeoutAccum)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(a * ACC_STRIDE);
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int sbk = 0; sbk < num_sb; ++sbk, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full_bar[s], ph, args.status, kDevTimeoutFull)) {
@@ -552,8 +556,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            umma_f16_ss(d, sdesc_k_sw128(sa + k * 32), sdesc_k_sw128(sb + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int j = 0; j < KBOX; ++j) {
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              umma_f16_ss(d, sdesc_k_sw128(sa + j * A_KB + k * 32), sdesc_k_sw128(sb + j * B_KB + k * 32), idesc,
+                          (sbk | j | k) != 0 ? 1u : 0u);
+            }
           }
           umma_commit(&empty_bar[s]);
         }
@@ -668,7 +676,8 @@ cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 size_t gemm_smem_bytes(int bn, int stages) {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * (kBM * kBK * 2 + bn * kBK * 2) + 256 /*barriers*/ +
+  return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * gemm_kbox(bn) * (kBM * kBK * 2 + bn * kBK * 2) +
+         256 /*barriers*/ +
          static_cast<size_t>(tile_const_floats(bn)) * 4 + kEpiWarps * kStageFloats * 4 /*epilogue stages*/;
 }
 
@@ -692,15 +701,17 @@ int gemm_pick_bn(int M, int N, bool paired) {
 }
 
 bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
-                   uint32_t box_rows) {
+                   uint32_t box_rows, uint32_t kbox) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn || !base) return false;
+  if (!fn || !base || cols % kBK != 0 || cols > ld_elems || kbox < 1) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld_elems * 2) % 16 != 0) return false;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {ld_elems * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  // {64 columns of a k-block, rows, k-blocks}; the k-block stride (128 B) is
+  // smaller than the row stride, so one box gathers kbox k-blocks of box_rows rows.
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kBK), rows, cols / kBK};
+  cuuint64_t strides[2] = {ld_elems * 2, static_cast<cuuint64_t>(kBK) * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), box_rows, kbox};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;

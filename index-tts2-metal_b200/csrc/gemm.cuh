@@ -67,18 +67,25 @@ struct GemmLaunch {
   int stages;
 };
 
-// Pipeline depth for a tile width: as many 64-deep k-blocks as fit next to the
-// epilogue's shared memory (constants, 8 x 4 KB store stages, barriers) in
-// the 227 KB a CTA may use.
-constexpr int gemm_stages(int bn) {
-  return ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / (128 * 64 * 2 + bn * 64 * 2)) > 8
+// k-blocks (64 columns each) fetched per TMA instruction: one TMA box moves
+// kbox x rows x 128 B, and larger boxes raise the per-SM ingest rate.
+__host__ __device__ constexpr int gemm_kbox(int bn) { return bn <= 128 ? 2 : 1; }
+
+// Pipeline depth for a tile width: as many stages (kbox k-blocks of A and B)
+// as fit next to the epilogue's shared memory (constants, 8 x 4 KB store
+// stages, barriers) in the 227 KB a CTA may use.
+__host__ __device__ constexpr int gemm_stages(int bn) {
+  return ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / (gemm_kbox(bn) * (128 * 64 * 2 + bn * 64 * 2))) > 8
              ? 8
-             : ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / (128 * 64 * 2 + bn * 64 * 2));
+             : ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / (gemm_kbox(bn) * (128 * 64 * 2 + bn * 64 * 2)));
 }
 
 // Host helpers (gemm.cu).
+// Tensor map of a row-major f16 matrix [rows][cols] (row stride ld_elems)
+// viewed as {64, rows, cols/64}; the box is {64, box_rows, kbox}. cols must be
+// a multiple of 64 (pad the matrix with zero columns).
 bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
-                   uint32_t box_rows);
+                   uint32_t box_rows, uint32_t kbox);
 cudaError_t gemm_run(const GemmLaunch& g, cudaStream_t stream);
 size_t gemm_smem_bytes(int bn, int stages);
 // Tile width (64, 128 or 256; paired epilogues need a multiple of 128) that

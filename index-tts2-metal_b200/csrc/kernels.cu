@@ -130,7 +130,7 @@ __global__ void euler_kernel(float* __restrict__ X, const float* __restrict__ V,
     if (t < prompt_len[u]) x = 0.0f;
     X[i] = x;
     const __half xh = __float2half_rn(x);
-    for (int b = 0; b < branches; ++b) XD[(cond_row + static_cast<size_t>(b) * T) * 80 + c] = xh;
+    for (int b = 0; b < branches; ++b) XD[(cond_row + static_cast<size_t>(b) * T) * kXdLd + c] = xh;
   }
 }
 
@@ -149,7 +149,7 @@ __global__ void euler_init_kernel(const float* X0, float* X, __half* __restrict_
     X[i] = x;
     const size_t cond_row = (static_cast<size_t>(u) * branches) * T + t;
     const __half xh = __float2half_rn(x);
-    for (int b = 0; b < branches; ++b) XD[(cond_row + static_cast<size_t>(b) * T) * 80 + c] = xh;
+    for (int b = 0; b < branches; ++b) XD[(cond_row + static_cast<size_t>(b) * T) * kXdLd + c] = xh;
   }
 }
 
@@ -166,7 +166,7 @@ __global__ void merge_input_kernel(const float* __restrict__ prompt_x, const __h
                                    const float* __restrict__ bcp, const float* __restrict__ style,
                                    __half* __restrict__ U, int B, int T, int branches) {
   pdl_entry();
-  constexpr int W = 784;
+  constexpr int W = kUld;
   const size_t total = static_cast<size_t>(B) * branches * T * W;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -180,7 +180,8 @@ __global__ void merge_input_kernel(const float* __restrict__ prompt_x, const __h
     if (br == 0) {
       if (c < 80) v = prompt_x[(static_cast<size_t>(u) * T + t) * 80 + c];
       else if (c < 592) v = __half2float(cp16[(static_cast<size_t>(u) * T + t) * 512 + (c - 80)]);
-      else v = style[static_cast<size_t>(u) * 192 + (c - 592)];
+      else if (c < 784) v = style[static_cast<size_t>(u) * 192 + (c - 592)];
+      else v = 0.0f;
     } else {
       v = (c >= 80 && c < 592) ? bcp[c - 80] : 0.0f;
     }
@@ -267,7 +268,7 @@ cudaError_t to_half_run(const float* x, __half* y, size_t n, cudaStream_t st) {
 
 cudaError_t merge_input_run(const float* prompt_x, const __half* cp16, const float* bcp, const float* style,
                             __half* U, int B, int T, int branches, cudaStream_t st) {
-  const size_t n = static_cast<size_t>(B) * branches * T * 784;
+  const size_t n = static_cast<size_t>(B) * branches * T * kUld;
   return launch_pdl(merge_input_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, prompt_x, cp16, bcp, style, U, B, T,
                     branches);
 }

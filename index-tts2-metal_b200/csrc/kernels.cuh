@@ -7,6 +7,11 @@
 
 namespace itts {
 
+// Row strides of the zero-padded GEMM operands: 80 mel columns padded to two
+// 64-column k-blocks, 784 merge columns padded to 13 k-blocks.
+constexpr int kXdLd = 128;
+constexpr int kUld = 832;
+
 // Masked MHA over packed QKV (attention.cu).
 cudaError_t attention_run(const __half* qkv, const float* row_mask, __half* out, int S, int T, cudaStream_t st);
 
@@ -32,7 +37,7 @@ cudaError_t euler_init_run(const float* X0, float* X, __half* XD, const int* pro
 // f32 -> f16 conversion.
 cudaError_t to_half_run(const float* x, __half* y, size_t n, cudaStream_t st);
 
-// Build the 784-wide step-invariant merge input per sequence row:
+// Build the 784-wide (row stride kUld, zero tail) step-invariant merge input per sequence row:
 //   cond branch: [prompt_x(80) | CP(512) | style(192)], null branch: [0 | bcp | 0].
 cudaError_t merge_input_run(const float* prompt_x, const __half* cp16, const float* bcp, const float* style,
                             __half* U, int B, int T, int branches, cudaStream_t st);

@@ -1,6 +1,8 @@
 // Estimator weight preparation and upload (host C++, fp32 math).
 #include "model.hpp"
 
+#include "kernels.cuh"
+
 #include <cmath>
 #include <cstring>
 #include <functional>
@@ -181,10 +183,11 @@ void load_weights(const Mit2Bundle& b, DevWeights* w) {
   pk.add(f32(b, P("cond_projection.bias"), 512), &w->bcp);
   {
     auto m = h16(b, P("cond_x_merge_linear.weight"), 512 * 864);
-    std::vector<uint16_t> wx(512 * 80), wr(512 * 784);
+    // Zero-padded to whole 64-column k-blocks (x slice 80 -> kXdLd, rest 784 -> kUld).
+    std::vector<uint16_t> wx(512 * kXdLd, 0), wr(512 * kUld, 0);
     for (int r = 0; r < 512; ++r) {
-      std::memcpy(&wx[r * 80], &m[r * 864], 80 * 2);
-      std::memcpy(&wr[r * 784], &m[r * 864 + 80], 784 * 2);
+      std::memcpy(&wx[r * kXdLd], &m[r * 864], 80 * 2);
+      std::memcpy(&wr[r * kUld], &m[r * 864 + 80], 784 * 2);
     }
     pk.add(std::move(wx), reinterpret_cast<uint16_t**>(&w->wx));
     pk.add(std::move(wr), reinterpret_cast<uint16_t**>(&w->wrest));
@@ -229,7 +232,13 @@ void load_weights(const Mit2Bundle& b, DevWeights* w) {
   pk.add(h16(b, P("transformer.norm.project_layer.weight"), 1024 * 512), reinterpret_cast<uint16_t**>(&w->proj_norm));
   pk.add(f32(b, P("transformer.norm.project_layer.bias"), 1024), &w->projb_norm);
   // Post-transformer projections.
-  pk.add(h16(b, P("skip_linear.weight"), 512 * 592), reinterpret_cast<uint16_t**>(&w->wsl));
+  {
+    // [x_normed (512) | x_mel (80 -> kXdLd, zero-padded)]
+    auto sl = h16(b, P("skip_linear.weight"), 512 * 592);
+    std::vector<uint16_t> slp(512 * (512 + kXdLd), 0);
+    for (int r = 0; r < 512; ++r) std::memcpy(&slp[r * (512 + kXdLd)], &sl[r * 592], 592 * 2);
+    pk.add(std::move(slp), reinterpret_cast<uint16_t**>(&w->wsl));
+  }
   pk.add(f32(b, P("skip_linear.bias"), 512), &w->bsl);
   {
     auto c1 = h16(b, P("conv1.weight"), 512 * 512);

@@ -60,10 +60,10 @@ struct DevWeights {
   float* projb_norm = nullptr;
   __half* wcp = nullptr;  // cond_projection [512][512]
   float* bcp = nullptr;
-  __half* wx = nullptr;     // cond_x_merge_linear x slice [512][80]
-  __half* wrest = nullptr;  // remaining merge columns [512][784]
+  __half* wx = nullptr;     // cond_x_merge_linear x slice [512][kXdLd] (zero-padded)
+  __half* wrest = nullptr;  // remaining merge columns [512][kUld] (zero-padded)
   float* bm = nullptr;
-  __half* wsl = nullptr;  // skip_linear [512][592]
+  __half* wsl = nullptr;  // skip_linear [512][512 + kXdLd] (zero-padded)
   float* bsl = nullptr;
   __half* wc1res = nullptr;  // [conv1 ; res_projection] [1024][512]
   float* bc1res = nullptr;

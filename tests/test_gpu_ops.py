@@ -32,8 +32,9 @@ def _rel_err(ref, got):
         (300, 3072, 512, 256),
         (1600, 512, 1536, 128),
         (1600, 80, 512, 80),
-        (513, 512, 80, 128),
-        (257, 512, 784, 128),
+        (513, 512, 128, 128),
+        (257, 512, 832, 128),
+        (129, 512, 704, 64),
         (1000, 1024, 2560, 256),
     ],
 )
@@ -57,12 +58,17 @@ def test_gemm_split_two_sources(ctx_unit):
     M = 333
     g = torch.Generator(device="cpu").manual_seed(5)
     a0 = torch.randn(M, 512, generator=g).half().to(dev)
-    a1 = torch.randn(M, 80, generator=g).half().to(dev)
-    w = (torch.randn(512, 592, generator=g) / 592**0.5).half().to(dev)
+    a1 = torch.zeros(M, 128).half()
+    a1[:, :80] = torch.randn(M, 80, generator=g).half()
+    a1 = a1.to(dev)
+    w = torch.zeros(512, 640).half()
+    w[:, :592] = (torch.randn(512, 592, generator=g) / 592**0.5).half()
+    w = w.to(dev)
     bias = torch.randn(512, generator=g).float().to(dev)
     c = torch.empty(M, 512, device=dev)
-    ctx_unit.op_gemm(a0.data_ptr(), 512, a1.data_ptr(), 80, 512, w.data_ptr(), 592, bias.data_ptr(), c.data_ptr(), 512,
-                     M, 512, 592, 128)
+    # columns 80..127 of a1 and 592..639 of w are the zero padding of the 64-column k-blocks
+    ctx_unit.op_gemm(a0.data_ptr(), 512, a1.data_ptr(), 128, 512, w.data_ptr(), 640, bias.data_ptr(), c.data_ptr(), 512,
+                     M, 512, 640, 128)
     ref = torch.cat([a0, a1], 1).float() @ w.float().T + bias
     rel, mx = _rel_err(ref, c)
     assert rel < 1e-5 and mx < 1e-3, (rel, mx)
