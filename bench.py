@@ -45,6 +45,14 @@ BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_seed0_baseline"
 REF_SAMPLE_FRAMES = 32
 
 
+def step_flops_total(B: int, T: int, cfg: dict) -> float:
+    """Algorithmic FLOPs of one guided CFM step for B utterances of T frames."""
+    import itts_cfm
+
+    branches = 2 if cfg["cfg"] > 0 else 1
+    return itts_cfm.step_flops(B * branches, T)
+
+
 def _env_int(k, d):
     try:
         return int(os.environ.get(k, d))
@@ -209,6 +217,8 @@ def main():
     ap.add_argument("--workload", type=int, choices=[2, 5], default=2)
     ap.add_argument("--utts", type=int, default=None, help="utterances per GPU (default: 1 for config 2)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batched", type=int, default=64,
+                    help="also time a padded batch of this many utterances per GPU (0 = skip)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -330,6 +340,35 @@ def main():
                 "time_share": gemm["ms"] / total_prof_ms if total_prof_ms else None,
                 "kernels": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in d.items()} for d in prof]}
 
+    # Batched serving throughput on the same utterance shape (supplementary):
+    # utterances per GPU share one padded batch, so the GEMMs see large M.
+    batched = None
+    if args.batched > 0:
+        Bb = args.batched
+        butts = workloads.config_utterances(args.workload, n=Bb, seed_offset=rank * 1000 + 500)
+        bvl, bpl, bno, bpx, bco, bst = workloads.pad_batch(butts, T)
+        ctx.stage_padded(bvl, bpl, bno, bpx, bco, bst, cfg["steps"], cfg["cfg"])
+        ctx.launch()
+        ctx.sync()
+        bev0 = torch.cuda.Event(enable_timing=True)
+        bev1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        bev0.record(stream)
+        nb = 3
+        for _ in range(nb):
+            ctx.launch()
+        bev1.record(stream)
+        bev1.synchronize()
+        barrier()
+        bms = max_over_ranks(bev0.elapsed_time(bev1)) / nb
+        bprof = ctx.profile_step(reps=2)
+        bg = next(d for d in bprof if d["name"] == "gemm")
+        b_ach = bg["flops"] / (bg["ms"] / 1e3) / 1e12
+        batched = {"utterances_per_gpu": Bb, "value": Bb * T * world / (bms / 1e3), "unit": UNIT,
+                   "ms_per_run": bms, "ms_per_cfm_step": bms / cfg["steps"],
+                   "tflops": step_flops_total(Bb, T, cfg) * cfg["steps"] / (bms / 1e3) / 1e12,
+                   "gemm_tflops": b_ach, "gemm_frac": b_ach / peak}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
@@ -360,6 +399,7 @@ def main():
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clk,
+            "batched": batched,
         }
         print(json.dumps(line))
     if dist is not None:
