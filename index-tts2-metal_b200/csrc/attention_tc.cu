@@ -1,0 +1,412 @@
+// tcgen05 flash attention for the DiT blocks (sm_100a): one CTA computes 128
+// queries of one (sequence, head) against all keys of its sequence in blocks
+// of 128 keys.
+//
+//   warp 0      : TMA producer (Q once; K and V blocks into a 2-deep ring) and
+//                 the per-block key-mask bias row
+//   warp 1 (l0) : tcgen05.mma issuer: S_j = Q K_j^T (M=128, N=128, K=64) and
+//                 O_j = P_j V_j (M=128, N=64, K=128; V is read MN-major)
+//   warps 2..9  : online softmax, two warps per query row quarter (64 keys
+//                 each): S_j from TMEM, P_j (f16) into shared memory in the
+//                 UMMA operand layout, O_j from TMEM accumulated in registers
+//                 with the running rescale, normalised output to global memory.
+// TMEM: S double buffer (2 x 128 columns) and O double buffer (2 x 64).
+//
+// Semantics follow cpu_attention_single_head_masked
+// (runtime/impl/tokenizer_tests.cpp:3960-3997): keys with mask 0 get
+// probability 0; q arrives RoPE'd and scaled by 1/8 from the QKV epilogue.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math_constants.h>
+#include <stdint.h>
+
+#include <atomic>
+
+#include "kernels.cuh"
+#include "launch.cuh"
+#include "ptx.cuh"
+
+namespace itts {
+
+namespace {
+
+constexpr int kQ = 128;    // queries per CTA
+constexpr int kKB = 128;   // keys per block
+constexpr int kThreadsA = 64 + 8 * 32;  // producer, MMA, 8 softmax warps
+constexpr int kKV = 4;     // K/V ring depth (blocks in flight)
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = 16384;                      // kKV stages x 16 KB
+constexpr int OFF_V = OFF_K + kKV * 16384;        // kKV stages x 16 KB
+constexpr int OFF_P = OFF_V + kKV * 16384;        // 2 buffers x 32 KB
+constexpr int OFF_BIAS = OFF_P + 2 * 32768;       // kKV x 128 floats
+constexpr int OFF_FLAG = OFF_BIAS + kKV * kKB * 4;  // kKV ints: block has no masked key
+constexpr int OFF_XCH = OFF_FLAG + 16;               // row-max / row-sum exchange: 6 x 128 floats
+constexpr int OFF_XTAG = OFF_XCH + 6 * 128 * 4;      // exchange tags: 2 halves x 128 rows
+constexpr int OFF_BAR = OFF_XTAG + 2 * 128 * 4;
+constexpr int SMEM_A = 1024 + OFF_BAR + 256;
+constexpr uint32_t TMEM_S = 0;    // + 128 * stage
+constexpr uint32_t TMEM_O = 256;  // + 64 * stage
+
+enum : unsigned int { kDevTimeoutAttn = 16 };
+
+// Timeline hooks for performance investigation: compiled out unless a harness
+// defines ITTS_ATTN_TRACE and provides itts_attn_trace_point(slot).
+#ifdef ITTS_ATTN_TRACE
+#define ATTN_TRACE(slot) itts_attn_trace_point(slot)
+#else
+#define ATTN_TRACE(slot) ((void)0)
+#endif
+
+// 2^x on the special-function unit (|rel err| < 2^-22; inputs here are <= 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x on the FMA/ALU pipes, for x <= 0: x = i + f with i = round(x) (via the
+// 1.5*2^23 rounding constant) and f in [-0.5, 0.5]; 2^f from a degree-4
+// polynomial fitted to relative error 2.7e-6 on that interval; 2^i added to
+// the exponent bits. x is clamped at -125 so the result stays a normal
+// number (2^-125 rounds to 0 in the f16 P operand).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float t = x + kRound;
+  const int i = __float_as_int(t) - __float_as_int(kRound);
+  const float f = x - (t - kRound);
+  float p = 0.00956052f;
+  p = fmaf(p, f, 0.05591704f);
+  p = fmaf(p, f, 0.24024981f);
+  p = fmaf(p, f, 0.69312197f);
+  p = fmaf(p, f, 0.99999917f);
+  return __int_as_float(__float_as_int(p) + (i << 23));
+}
+
+__global__ void __launch_bounds__(kThreadsA, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const float* __restrict__ row_mask, __half* __restrict__ out,
+                   int T, unsigned int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* q_full = bars;               // 1
+  uint64_t* kv_full = bars + 1;          // kKV
+  uint64_t* kv_empty = kv_full + kKV;    // kKV
+  uint64_t* s_full = kv_empty + kKV;     // 2
+  uint64_t* s_free = s_full + 2;         // 2
+  uint64_t* p_full = s_free + 2;         // 2
+  uint64_t* o_full = p_full + 2;         // 2
+  uint64_t* o_free = o_full + 2;         // 2
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+  float* bias = reinterpret_cast<float*>(sm + OFF_BIAS);
+  int* full_block = reinterpret_cast<int*>(sm + OFF_FLAG);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int q0 = qt * kQ;
+  const int seq0 = s * T;
+  const int nkb = (T + kKB - 1) / kKB;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kKV; ++i) {
+      mbar_init(&kv_full[i], 1 + 32);  // producer expect_tx + 32 lanes writing the mask row
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 8);  // one arrival per softmax warp
+      mbar_init(&p_full[i], 8);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 8);
+    }
+    fence_barrier_init();
+    fence_proxy_async_shared();
+    prefetch_tmap(&tm);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  // Exchange tags start at 0 for every row and half (shared memory is not
+  // cleared between CTAs); the barrier below publishes them.
+  if (threadIdx.x < 2 * 128) reinterpret_cast<int*>(sm + OFF_XTAG)[threadIdx.x] = 0;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x == 0) ATTN_TRACE(0);
+
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kQ * 128);
+      tma_load_3d(sm + OFF_Q, &tm, q_full, 0, seq0 + q0, h);
+    }
+    for (int j = 0; j < nkb; ++j) {
+      const int st = j % kKV;
+      const uint32_t ph = (j / kKV) & 1;
+      if (!mbar_wait(&kv_empty[st], ph ^ 1, status, kDevTimeoutAttn)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kKB * 128);
+        tma_load_3d(sm + OFF_K + st * 16384, &tm, &kv_full[st], 0, seq0 + j * kKB, 8 + h);
+        tma_load_3d(sm + OFF_V + st * 16384, &tm, &kv_full[st], 0, seq0 + j * kKB, 16 + h);
+      }
+      bool valid4 = true;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = lane * 4 + i;
+        const int key = j * kKB + k;
+        const bool valid = key < T && row_mask[seq0 + key] != 0.0f;
+        valid4 = valid4 && valid;
+        bias[st * kKB + k] = valid ? 0.0f : -CUDART_INF_F;
+      }
+      const bool all_valid = __all_sync(0xffffffffu, valid4);
+      if (lane == 0) full_block[st] = all_valid ? 1 : 0;
+      __syncwarp();
+      mbar_arrive(&kv_full[st]);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, kKB);
+      constexpr uint32_t idesc_o = idesc_f16_f32(128, 64) | (1u << 16);  // B (V) MN-major
+      const uint32_t sq = smem_u32(sm + OFF_Q);
+      bool ok = mbar_wait(q_full, 0, status, kDevTimeoutAttn);
+      auto issue_s = [&](int j) -> bool {
+        const int kst = j % kKV;           // K/V stage
+        const int st = j & 1;              // S buffer
+        if (!mbar_wait(&kv_full[kst], (j / kKV) & 1, status, kDevTimeoutAttn)) return false;
+        if (!mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, status, kDevTimeoutAttn)) return false;
+        tc_fence_after();
+        if (j < 8) ATTN_TRACE(2 + j);  // slots 2..9: S_j waits done
+        const uint32_t sk = smem_u32(sm + OFF_K + kst * 16384);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f16_ss(tmem + TMEM_S + st * 128, sdesc_k_sw128(sq + k * 32), sdesc_k_sw128(sk + k * 32), idesc_s,
+                      k != 0 ? 1u : 0u);
+        umma_commit(&s_full[st]);
+        if (j < 8) ATTN_TRACE(10 + j);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (j + 1 < nkb && !issue_s(j + 1)) break;
+        if (!mbar_wait(&p_full[st], ph, status, kDevTimeoutAttn)) break;
+        if (!mbar_wait(&o_free[st], ph ^ 1, status, kDevTimeoutAttn)) break;
+        tc_fence_after();
+        if (j < 4) ATTN_TRACE(56 + j);  // slots 56..59: O_j waits done
+        const uint32_t sp = smem_u32(sm + OFF_P + st * 32768);
+        const uint32_t sv = smem_u32(sm + OFF_V + (j % kKV) * 16384);
+#pragma unroll
+        for (int kk = 0; kk < kKB / 16; ++kk)
+          umma_f16_ss(tmem + TMEM_O + st * 64, sdesc_k_sw128(sp + (kk >> 2) * 16384 + (kk & 3) * 32),
+                      sdesc_mn_sw128(sv + kk * 2048), idesc_o, kk != 0 ? 1u : 0u);
+        umma_commit(&o_full[st]);
+        umma_commit(&kv_empty[j % kKV]);
+        if (j < 8) ATTN_TRACE(40 + j);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- softmax: warps 2..9; the two warps of a TMEM lane quarter share 32
+    // query rows, each owning 64 of the 128 keys of a block and 32 of the 64
+    // output dims. The row maximum is exchanged through shared memory.
+    const int quarter = warp & 3;
+    const int hh = (warp - 2) >> 2;  // key half / output-dim half
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const float kLog2e = 1.4426950408889634f;
+    float* xval = reinterpret_cast<float*>(sm + OFF_XCH);          // [3 slots][2 halves][128 rows]
+    volatile int* xtag = reinterpret_cast<volatile int*>(sm + OFF_XTAG);  // [2 halves][128 rows]
+    float o[32];
+#pragma unroll
+    for (int d = 0; d < 32; ++d) o[d] = 0.0f;
+    float m = -CUDART_INF_F, l = 0.0f, alpha_prev = 0.0f;
+    bool ok = true;
+    // Hand `val` to the partner warp (same row, other half) and return the
+    // partner's value for the same tag. Tags grow monotonically; the wait is
+    // bounded and records kDevTimeoutAttn instead of hanging.
+    auto exchange = [&](float val, int slot, int tag, bool& good) -> float {
+      xval[(slot * 2 + hh) * 128 + row] = val;
+      __threadfence_block();
+      xtag[hh * 128 + row] = tag;
+      const long long t0 = clock64();
+      while (xtag[(hh ^ 1) * 128 + row] < tag) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+          if (status) atomicCAS(status, 0u, static_cast<unsigned int>(kDevTimeoutAttn));
+          good = false;
+          return 0.0f;
+        }
+      }
+      __threadfence_block();
+      return xval[(slot * 2 + (hh ^ 1)) * 128 + row];
+    };
+    auto accumulate_o = [&](int jp) -> bool {
+      const int st = jp & 1;
+      if (!mbar_wait(&o_full[st], (jp >> 1) & 1, status, kDevTimeoutAttn)) return false;
+      tc_fence_after();
+      uint32_t r0[32];
+      tmem_ld32_async(tmem + lane_off + TMEM_O + st * 64 + hh * 32, r0);
+      tmem_wait_ld();
+      reg_fence32(r0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[st]);
+      if (warp == 2 && lane == 0 && jp < 8) ATTN_TRACE(50 + jp);
+#pragma unroll
+      for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha_prev + __uint_as_float(r0[d]);
+      return true;
+    };
+    for (int j = 0; j < nkb && ok; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!mbar_wait(&s_full[st], ph, status, kDevTimeoutAttn)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[64];
+      tmem_ld32_async(tmem + lane_off + TMEM_S + st * 128 + hh * 64, sr);
+      tmem_ld32_async(tmem + lane_off + TMEM_S + st * 128 + hh * 64 + 32, sr + 32);
+      tmem_wait_ld();
+      reg_fence32(sr);
+      reg_fence32(sr + 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[st]);
+      if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(20 + j);
+      // The mask row of this block was published with kv_full (already complete).
+      const int kst = j % kKV;
+      if (!mbar_wait(&kv_full[kst], (j / kKV) & 1, status, kDevTimeoutAttn)) {
+        ok = false;
+        break;
+      }
+      if (!full_block[kst]) {
+        const float* brow = bias + kst * kKB + hh * 64;
+#pragma unroll
+        for (int k = 0; k < 64; ++k) sr[k] = __float_as_uint(__uint_as_float(sr[k]) + brow[k]);
+      }
+      // Row max: 8 partial maxima over this warp's 64 keys, then the partner's.
+      float mp[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mp[e] = __uint_as_float(sr[e]);
+#pragma unroll
+      for (int k = 8; k < 64; ++k) mp[k & 7] = fmaxf(mp[k & 7], __uint_as_float(sr[k]));
+      float mine = mp[0];
+#pragma unroll
+      for (int e = 1; e < 8; ++e) mine = fmaxf(mine, mp[e]);
+      const float other = exchange(mine, st, j + 1, ok);
+      if (!ok) break;
+      const float mx = fmaxf(m, fmaxf(mine, other));
+      const float ref = (mx == -CUDART_INF_F) ? 0.0f : mx;
+      const float alpha = ex2_approx((m - ref) * kLog2e);
+      const float nref = -ref * kLog2e;
+      m = mx;
+      float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      uint8_t* ptile = sm + OFF_P + st * 32768 + hh * 16384 + row * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 keys = this warp's 64-key k-block of P
+        float p[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          // One in four on the FMA pipe, the rest on the SFU (the units run in parallel).
+          const float xe = fmaf(__uint_as_float(sr[c * 8 + e]), kLog2e, nref);
+          p[e] = (e & 3) == 3 ? ex2_poly(xe) : ex2_approx(xe);
+          sp[e] += p[e];
+        }
+        union {
+          __half2 h2[4];
+          uint4 u;
+        } pk;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pk.h2[e] = __floats2half2_rn(p[2 * e], p[2 * e + 1]);
+        *reinterpret_cast<uint4*>(ptile + ((c ^ (row & 7)) << 4)) = pk.u;
+      }
+      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+      l = l * alpha + sum;  // this warp's partial row sum
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[st]);
+      if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(30 + j);
+      if (j >= 1 && !accumulate_o(j - 1)) {
+        ok = false;
+        break;
+      }
+      alpha_prev = alpha;
+    }
+    if (ok) ok = accumulate_o(nkb - 1);
+    // Combine the two partial row sums.
+    float l_all = l;
+    if (ok) l_all += exchange(l, 2, nkb + 1, ok);
+    if (ok && q0 + row < T) {
+      const float inv = l_all > 0.0f ? 1.0f / l_all : 0.0f;
+      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(seq0 + q0 + row) * 512 + h * 64 + hh * 32);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        union {
+          __half2 h2[4];
+          uint4 u;
+        } pk;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pk.h2[e] = __floats2half2_rn(o[c * 8 + 2 * e] * inv, o[c * 8 + 2 * e + 1] * inv);
+        dst[c] = pk.u;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) ATTN_TRACE(60);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace
+
+bool make_attn_tmap(CUtensorMap* tm, const __half* qkv, int R) {
+  // qkv [R][1536] viewed as {64, R, 24 k-blocks}: block h = q head h, 8+h = k, 16+h = v.
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(R), 24};
+  cuuint64_t strides[2] = {1536 * 2, 128};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(qkv), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t attention_tc_run(const CUtensorMap& tm, const float* row_mask, __half* out, int S, int T,
+                             unsigned int* status, cudaStream_t st) {
+  if (S <= 0 || T <= 0) return cudaErrorInvalidValue;
+  static std::atomic<uint32_t> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint32_t bit = 1u << (dev & 31);
+  if ((configured.load() & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_A);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit);
+  }
+  dim3 grid((T + kQ - 1) / kQ, 8, S);
+  return launch_pdl(attn_tc_kernel, grid, dim3(kThreadsA), SMEM_A, st, tm, row_mask, out, T, status);
+}
+
+}  // namespace itts

@@ -433,10 +433,15 @@ int itts_op_attention(itts_cfm_ctx* ctx, const void* qkv, const float* row_mask,
   return guarded(ctx, [&] {
     need(qkv && row_mask && out && S > 0 && T > 0, "bad attention arguments");
     itts::Engine& e = *ctx->eng;
-    cuda_ok(itts::attention_run(static_cast<const __half*>(qkv), row_mask, static_cast<__half*>(out),
-                                static_cast<int>(S), static_cast<int>(T), e.stream()),
+    CUtensorMap tm;
+    if (!itts::make_attn_tmap(&tm, static_cast<const __half*>(qkv), static_cast<int>(S * T)))
+      throw ShapeError("qkv layout rejected by TMA");
+    e.clear_status();
+    cuda_ok(itts::attention_tc_run(tm, row_mask, static_cast<__half*>(out), static_cast<int>(S), static_cast<int>(T),
+                                   e.status_ptr(), e.stream()),
             "attention launch");
     cuda_ok(cudaStreamSynchronize(e.stream()), "attention sync");
+    check_status(e);
   });
 }
 

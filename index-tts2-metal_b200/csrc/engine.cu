@@ -243,6 +243,7 @@ Work* Engine::work(int B, int T, int branches) {
   w->arena_bytes = bytes;
   check(cudaMemset(w->arena, 0, bytes), "workspace memset");
   layout(static_cast<uint8_t*>(w->arena));
+  if (!make_attn_tmap(&w->tm_attn, w->qkv16, w->R)) throw std::runtime_error("cuda: attention tensor map rejected");
   // RoPE table with the reference's float arithmetic (apply_rope_inplace,
   // runtime/impl/tokenizer_tests.cpp:4266-4281).
   std::vector<float2> rope(static_cast<size_t>(T) * 32);
@@ -448,7 +449,7 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
     });
     G("gemm", w->g_qkv[l], 512);
     P.run("attention", S * 4.0 * T * T * 512.0, R * (1536 + 512) * 2.0,
-          [&] { check(attention_run(w->qkv16, w->mask, w->attn16, w->S, w->T, stream_), "attention"); });
+          [&] { check(attention_tc_run(w->tm_attn, w->mask, w->attn16, w->S, w->T, d_status_, stream_), "attention"); });
     G("gemm", w->g_wo[l], 512);
     P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
       check(adarms_run(w->h, w->R, tab + kTabFfn + l * 1024, w_.L[l].g_ffn, w->xn16, stream_), "adarms");

@@ -65,6 +65,7 @@ struct Work {
   __half* fh16 = nullptr;
   float* vel = nullptr;  // [R, 80]
   float2* rope = nullptr;
+  CUtensorMap tm_attn;  // qkv16 viewed for the attention kernel
   void* arena = nullptr;
   size_t arena_bytes = 0;
   // prebuilt GEMM launches
@@ -103,6 +104,7 @@ class Engine {
 
   // Device status word (non-zero after a kernel abandoned a bounded wait).
   unsigned int read_status();
+  unsigned int* status_ptr() const { return d_status_; }
   void clear_status();
 
  private:

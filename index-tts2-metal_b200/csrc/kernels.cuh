@@ -1,6 +1,7 @@
 // Launchers for the non-GEMM kernels of the DiT-CFM sampler.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -12,8 +13,12 @@ namespace itts {
 constexpr int kXdLd = 128;
 constexpr int kUld = 832;
 
-// Masked MHA over packed QKV (attention.cu).
-cudaError_t attention_run(const __half* qkv, const float* row_mask, __half* out, int S, int T, cudaStream_t st);
+// Masked MHA over packed QKV on tcgen05 (attention_tc.cu). make_attn_tmap builds
+// the tensor map of qkv [R][1536]; attention_tc_run launches S x 8 heads x
+// ceil(T/128) CTAs.
+bool make_attn_tmap(CUtensorMap* tm, const __half* qkv, int R);
+cudaError_t attention_tc_run(const CUtensorMap& tm, const float* row_mask, __half* out, int S, int T,
+                             unsigned int* status, cudaStream_t st);
 
 // y = w (.) (x * rsqrt(mean(x^2) + 1e-5) (.) gamma) + b per 512-wide row;
 // wb = [w(512) | b(512)]. f32 in, f16 out.
