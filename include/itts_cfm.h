@@ -183,6 +183,31 @@ int itts_op_attention(itts_cfm_ctx* ctx, const void* qkv, const float* row_mask,
  */
 int itts_op_adarms(itts_cfm_ctx* ctx, const float* x, uint32_t R, const float* wb, const float* gamma, void* y);
 
+/*
+ * itts_op_conv5_noalloc: the k=5 reflect-padded conv of itts_op_conv5 for
+ * callers that cannot allocate device memory. Examples are a serving process
+ * whose own memory pool already holds the GPU's memory, and a real-time audio
+ * thread that must not take cudaMalloc's implicit device-wide synchronisation.
+ * It needs no context: nothing here calls cudaMalloc, cudaFree or an
+ * allocating library routine. No counterpart in the reference.
+ *
+ * x: [S*T, 512] f16 UNPADDED rows (16-byte aligned); w, bias, out as for
+ * itts_op_conv5. The reflect-padded staging copy the conv reads lives in one
+ * static device array of ITTS_NOALLOC_CONV5_MAX_ROWS x 512 f16 (16 MiB) per
+ * GPU, held from the first call on that GPU until the process exits;
+ * S*(T+4) above that limit returns ITTS_ECAP. Runs on the calling thread's
+ * current device and on `stream` (a cudaStream_t of that device; NULL = the
+ * legacy default stream), and synchronises that stream before returning.
+ * The first call on each device looks up the array's device address; make
+ * that call before any stream capture. Every call shares the array, so calls
+ * that overlap on the GPU (several host threads, or streams that are not
+ * ordered) race on it. On failure a message goes to err (err_cap bytes,
+ * may be NULL).
+ */
+#define ITTS_NOALLOC_CONV5_MAX_ROWS 16384u
+int itts_op_conv5_noalloc(const void* x, uint32_t S, uint32_t T, const void* w, const float* bias, float* out,
+                          uint32_t N, void* stream, char* err, uint32_t err_cap);
+
 #ifdef __cplusplus
 }
 #endif

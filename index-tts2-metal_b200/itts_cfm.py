@@ -28,7 +28,7 @@ EXPORTED = [
     "itts_cfm_strerror", "itts_cfm_run", "itts_cfm_run_batch", "itts_cfm_bucket_len", "itts_cfm_run_padded",
     "itts_cfm_estimator", "itts_cfm_stage_padded", "itts_cfm_launch", "itts_cfm_sync", "itts_cfm_fetch",
     "itts_cfm_stream", "itts_cfm_launch_kernels", "itts_cfm_profile_step", "itts_cfm_step_flops", "itts_op_gemm", "itts_op_conv5",
-    "itts_op_attention", "itts_op_adarms",
+    "itts_op_attention", "itts_op_adarms", "itts_op_conv5_noalloc",
 ]
 
 
@@ -85,6 +85,7 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_op_conv5": (i32, [vp, vp, u32, u32, vp, vp, vp, u32]),
         "itts_op_attention": (i32, [vp, vp, vp, vp, u32, u32]),
         "itts_op_adarms": (i32, [vp, vp, u32, vp, vp, vp]),
+        "itts_op_conv5_noalloc": (i32, [vp, u32, u32, vp, vp, vp, u32, vp, C.c_char_p, u32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -232,6 +233,21 @@ class Context:
 
     def op_adarms(self, x, R, wb, gamma, y) -> None:
         self._check(self.lib.itts_op_adarms(self.h, x, R, wb, gamma, y))
+
+
+NOALLOC_CONV5_MAX_ROWS = 16384
+
+
+def conv5_noalloc(x, S: int, T: int, w, bias, out, N: int, stream=None) -> None:
+    """itts_op_conv5_noalloc on device pointers: the k=5 reflect conv from
+    UNPADDED rows x [S*T, 512] f16, for callers that cannot allocate device
+    memory. It needs no Context; the padded staging copy lives in a static
+    device array of NOALLOC_CONV5_MAX_ROWS rows that every call shares."""
+    lib = load()
+    err = C.create_string_buffer(256)
+    rc = lib.itts_op_conv5_noalloc(x, S, T, w, bias, out, N, stream, err, len(err))
+    if rc != ITTS_OK:
+        raise IttsError(rc, err.value.decode())
 
 
 def bucket_len(T: int) -> int:
