@@ -158,6 +158,13 @@ static float* build_tables(const DevWeights& w, const std::vector<float>& tv, cu
   ck(gemv_f16w_run(w.proj_norm, w.projb_norm, t1, 512, tab + kTabNorm, kTcondPerStep, 1024, 512, n, 0, st));
   ck(gemv_f16w_run(w.ada_w, w.ada_b, t1, 512, tab + kTabFinal, kTcondPerStep, 1024, 512, n, 1, st));
   ck(gemv_f32w_run(w.wcond, w.bcond, t2, 512, tab + kTabWn, kTcondPerStep, 8192, 512, n, 0, st));
+  // Folded AdaRMS column terms: the norm shift b through the next GEMM's weights.
+  for (int l = 0; l < kLayers; ++l) {
+    ck(gemv_f16w_run(w.L[l].wqkv, nullptr, tab + kTabAttn + l * 1024 + 512, kTcondPerStep, tab + kTabQkvC + l * 1536,
+                     kTcondPerStep, 1536, 512, n, 0, st));
+    ck(gemv_f16w_run(w.L[l].w13, nullptr, tab + kTabFfn + l * 1024 + 512, kTcondPerStep, tab + kTabW13C + l * 3072,
+                     kTcondPerStep, 3072, 512, n, 0, st));
+  }
   ck(cudaStreamSynchronize(st));
   cudaFree(d_t);
   cudaFree(emb);
@@ -222,6 +229,7 @@ Work* Engine::work(int B, int T, int branches) {
     w->x16 = carve<__half>(cur, R * 512);
     for (int i = 0; i < 6; ++i) w->skip16[i] = carve<__half>(cur, R * 512);
     w->xn16 = carve<__half>(cur, R * 512);
+    w->ss = carve<float>(cur, R * 16);
     w->qkv16 = carve<__half>(cur, R * 1536);
     w->attn16 = carve<__half>(cur, R * 512);
     w->h = carve<float>(cur, R * 512);
@@ -319,6 +327,31 @@ void Engine::build_work_launches(Work* w) {
       w->g_w2[l].args.out16 = w->x16;
       w->g_w2[l].args.ld16 = 512;
     }
+  }
+  // Folded AdaRMS: every norm input inside the transformer stack is produced by
+  // an F32 GEMM (merge, w2 of layers 0..5, skip of layers 7..12, wo) that also
+  // writes the scaled operand xn16 and the row partial sums; QKV / w13 apply the
+  // row scale. The per-step w (nrm_w) and b . W^T (bias) are set per launch.
+  auto producer = [&](GemmLaunch& g, const float* gamma) {
+    g.args.nrm16 = w->xn16;
+    g.args.ldn = 512;
+    g.args.nrm_g = gamma;
+    g.args.ss_out = w->ss;
+    g.args.ss_ld = R;
+  };
+  auto consumer = [&](GemmLaunch& g) {
+    g.args.ss_in = w->ss;
+    g.args.ss_parts = 16;
+    g.args.ss_n = 512;
+    g.args.ss_ld = R;
+  };
+  producer(w->g_merge, w_.L[0].g_attn);
+  for (int l = 0; l < kLayers; ++l) {
+    if (l >= 1 && l <= kLayers / 2) producer(w->g_w2[l - 1], w_.L[l].g_attn);
+    if (l > kLayers / 2) producer(w->g_skip[l], w_.L[l].g_attn);
+    producer(w->g_wo[l], w_.L[l].g_ffn);
+    consumer(w->g_qkv[l]);
+    consumer(w->g_w13[l]);
   }
   w->g_sl = make_gemm(act(w->xn16, 512, R), act(w->XD, kXdLd, R), wt(w_.wsl, 512 + kXdLd, 512), R, 512, 512 + kXdLd,
                       kASplit, 8, 0, 0,
@@ -441,21 +474,26 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
     const double flops = 2.0 * rows * g.args.N * K;
     P.run(name, flops, 0.0, [&] { check(gemm_run(g, stream_), name); });
   };
-  G("gemm", w->g_merge, 80);
+  // Launch copies carrying this step's folded-norm constants (nrm_w: the
+  // norm's w row; bias of QKV / w13: the norm's b through the weights).
+  auto with_w = [](GemmLaunch g, const float* nw) {
+    g.args.nrm_w = nw;
+    return g;
+  };
+  auto with_bias = [](GemmLaunch g, const float* b) {
+    g.args.bias = b;
+    return g;
+  };
+  G("gemm", with_w(w->g_merge, tab + kTabAttn), 80);
   for (int l = 0; l < kLayers; ++l) {
-    if (l > kLayers / 2) G("gemm", w->g_skip[l], 1024);
-    P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
-      check(adarms_run(w->xres, w->R, tab + kTabAttn + l * 1024, w_.L[l].g_attn, w->xn16, stream_), "adarms");
-    });
-    G("gemm", w->g_qkv[l], 512);
+    if (l > kLayers / 2) G("gemm", with_w(w->g_skip[l], tab + kTabAttn + l * 1024), 1024);
+    G("gemm", with_bias(w->g_qkv[l], tab + kTabQkvC + l * 1536), 512);
     P.run("attention", S * 4.0 * T * T * 512.0, R * (1536 + 512) * 2.0,
           [&] { check(attention_tc_run(w->tm_attn, w->mask, w->attn16, w->S, w->T, d_status_, stream_), "attention"); });
-    G("gemm", w->g_wo[l], 512);
-    P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
-      check(adarms_run(w->h, w->R, tab + kTabFfn + l * 1024, w_.L[l].g_ffn, w->xn16, stream_), "adarms");
-    });
-    G("gemm", w->g_w13[l], 512);
-    G("gemm", w->g_w2[l], 1536);
+    G("gemm", with_w(w->g_wo[l], tab + kTabFfn + l * 1024), 512);
+    G("gemm", with_bias(w->g_w13[l], tab + kTabW13C + l * 3072), 512);
+    if (l + 1 <= kLayers / 2) G("gemm", with_w(w->g_w2[l], tab + kTabAttn + (l + 1) * 1024), 1536);
+    else G("gemm", w->g_w2[l], 1536);
   }
   P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
     check(adarms_run(w->xres, w->R, tab + kTabNorm, w_.g_norm, w->xn16, stream_), "adarms");

@@ -49,7 +49,8 @@ struct Work {
   float* xres = nullptr;
   __half* x16 = nullptr;
   __half* skip16[6] = {};
-  __half* xn16 = nullptr;
+  __half* xn16 = nullptr;  // normalised GEMM operand (folded AdaRMS: x * w * g)
+  float* ss = nullptr;     // [16][R] per-32-column partial sums of squares of the normalised x
   __half* qkv16 = nullptr;
   __half* attn16 = nullptr;
   float* h = nullptr;
@@ -86,9 +87,9 @@ class Engine {
   const DevWeights& weights() const { return w_; }
 
   Work* work(int B, int T, int branches);
-  // Device table [steps][36864] for the Euler schedule t_i = i/steps (fp32 accumulation).
+  // Device table [steps][kTcondPerStep] for the Euler schedule t_i = i/steps (fp32 accumulation).
   const float* tables_for_steps(int steps);
-  // Device table [1][36864] for one timestep value.
+  // Device table [1][kTcondPerStep] for one timestep value.
   const float* tables_for_t(float t);
 
   // Enqueue the whole sampler on stream(): inputs must already be in the

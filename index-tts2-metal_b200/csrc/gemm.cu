@@ -56,17 +56,26 @@ __device__ __forceinline__ void u2f16(const uint32_t (&r)[16], float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Epilogue helpers: the 128 epilogue threads (warps 2..5) share a named barrier.
+// Epilogue helpers: the 256 epilogue threads (warps 2..9) share a named barrier.
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
 
 // Per-tile column constants staged in shared memory before the accumulator is
 // ready: bias[n0 .. n0+BN) and, for the WaveNet gate, the global condition of
-// the tile's channels (a-part then b-part, BN/2 each).
+// the tile's channels (a-part then b-part, BN/2 each); for a folded-norm
+// producer the column scale nrm_w * nrm_g.
 template <int BN, int EPI>
 __device__ __forceinline__ void stage_tile_consts(const GemmArgs& args, int n0, float* sconst, int etid) {
   for (int i = etid; i < BN; i += 128) {
     const int n = n0 + i;
     sconst[i] = (args.bias && n < args.N) ? args.bias[n] : 0.0f;
+  }
+  if constexpr (EPI == kEpiF32) {
+    if (args.nrm16) {
+      for (int i = etid; i < BN; i += 128) {
+        const int n = n0 + i;
+        sconst[BN + i] = n < args.N ? args.nrm_w[n] * args.nrm_g[n] : 0.0f;
+      }
+    }
   }
   if constexpr (EPI == kEpiWnGate) {
     for (int i = etid; i < BN / 2; i += 128) {
@@ -138,6 +147,40 @@ __device__ __forceinline__ void flush_f16(const float4* stg, const __half* my_ro
       *reinterpret_cast<uint4*>(p + col0 + j * 8) = pk.u;
     }
   }
+}
+
+// As flush_f16, with staged column c multiplied by scale[c] first.
+__device__ __forceinline__ void flush_f16_scaled(const float4* stg, const __half* my_row, int col0, int ncols,
+                                                 int lane, const float* scale) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2);
+    const int j = lane & 3;
+    __half* p = const_cast<__half*>(static_cast<const __half*>(shfl_ptr(my_row, r)));
+    if (p && j * 8 < ncols) {
+      const float4 a = stg[r * 8 + ((2 * j) ^ (r & 7))];
+      const float4 b = stg[r * 8 + ((2 * j + 1) ^ (r & 7))];
+      const float* sc = scale + j * 8;
+      union {
+        __half2 h[4];
+        uint4 u;
+      } pk;
+      pk.h[0] = __floats2half2_rn(a.x * sc[0], a.y * sc[1]);
+      pk.h[1] = __floats2half2_rn(a.z * sc[2], a.w * sc[3]);
+      pk.h[2] = __floats2half2_rn(b.x * sc[4], b.y * sc[5]);
+      pk.h[3] = __floats2half2_rn(b.z * sc[6], b.w * sc[7]);
+      *reinterpret_cast<uint4*>(p + col0 + j * 8) = pk.u;
+    }
+  }
+}
+
+// Row scale of a folded-norm consumer: 1/sqrt(mean of squares + 1e-5) from the
+// producer's per-group partial sums (summed in group order), or 1.
+__device__ __forceinline__ float folded_row_scale(const GemmArgs& args, int m, bool row_ok) {
+  if (!args.ss_in || !row_ok) return 1.0f;
+  float t = 0.0f;
+  for (int p = 0; p < args.ss_parts; ++p) t += args.ss_in[static_cast<size_t>(p) * args.ss_ld + m];
+  return 1.0f / sqrtf(t / static_cast<float>(args.ss_n) + 1e-5f);
 }
 
 // Reflect-halo copies of one WaveNet row (the interior row itself goes through
@@ -213,6 +256,8 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
     };
     auto tcol = [](int q) { return (q >> 2) * 128 + (q & 3) * 16; };  // tile column of the a-chunk
     fetch(q_begin, xo_cur, ac_cur);
+    float rs = 1.0f;
+    if constexpr (EPI == kEpiSwiGLU) rs = folded_row_scale(args, m, row_ok);
     if (!mbar_wait(acc_bar, parity, args.status, kDevTimeoutAccum)) return false;
     tc_fence_after();
     uint32_t ta[16], tb[16], na_[16], nb_[16];
@@ -243,8 +288,8 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
         u2f16(tb, b);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          a[e] += sconst[ca + e];
-          b[e] += sconst[ca + 64 + e];
+          a[e] = fmaf(a[e], rs, sconst[ca + e]);
+          b[e] = fmaf(b[e], rs, sconst[ca + 64 + e]);
         }
         if constexpr (EPI == kEpiSwiGLU) {
 #pragma unroll
@@ -323,12 +368,14 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
     // Destination rows (null when the row is out of range).
     const void* d0 = nullptr;  // primary
     const void* d1 = nullptr;  // F32: f16 copy; Conv1Res: res projection row
+    const void* d2 = nullptr;  // F32: folded-norm f16 operand row
     if (row_ok) {
       if constexpr (EPI == kEpiF16 || EPI == kEpiQKV) {
         d0 = args.out16 + static_cast<size_t>(m) * args.ld16;
       } else if constexpr (EPI == kEpiF32) {
         d0 = args.out32 + static_cast<size_t>(mo) * args.ld32;
         if (args.out16) d1 = args.out16 + static_cast<size_t>(mo) * args.ld16;
+        if (args.nrm16) d2 = args.nrm16 + static_cast<size_t>(mo) * args.ldn;
       } else if constexpr (EPI == kEpiWnLast) {
         d0 = args.out32 + static_cast<size_t>(m) * args.ld32;
       } else if constexpr (EPI == kEpiConv1Res) {
@@ -354,6 +401,13 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
     float msk = 1.0f;
     if constexpr (EPI == kEpiWnLast) msk = row_ok ? args.row_mask[m] : 0.0f;
     fetch(c_begin, x0_cur, x1_cur);
+    // With two chunks per thread (F32, BN = 64) both residual chunks are in
+    // flight before the accumulator wait.
+    constexpr bool kPre2 = EPI == kEpiF32 && BN == 64;
+    if constexpr (kPre2) fetch(c_begin + 1, x0_nxt, x1_nxt);
+    float rs = 1.0f;
+    if constexpr (EPI == kEpiQKV) rs = folded_row_scale(args, m, row_ok);
+    float ssg = 0.0f;  // F32 producer: sum of squares of the current 32-column group
     if (!mbar_wait(acc_bar, parity, args.status, kDevTimeoutAccum)) return false;
     tc_fence_after();
     uint32_t tc[16], tn[16];
@@ -371,16 +425,20 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
           const bool more = c + 1 < c_end;
           if (more) {
             tmem_ld16_async(taddr + (c + 1) * 16, tn);
-            fetch(c + 1, x0_nxt, x1_nxt);
+            if constexpr (!kPre2) fetch(c + 1, x0_nxt, x1_nxt);
           }
           float* v = vg + h * 16;
           u2f16(tc, v);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] += sconst[c * 16 + e];
+          for (int e = 0; e < 16; ++e) v[e] = fmaf(v[e], rs, sconst[c * 16 + e]);
           if constexpr (EPI == kEpiF32) {
             if (args.resid32) {
 #pragma unroll
               for (int e = 0; e < 16; ++e) v[e] += x0_cur[e];
+            }
+            if (args.ss_out) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) ssg = fmaf(v[e], v[e], ssg);
             }
           } else if constexpr (EPI == kEpiQKV) {
             if (n < 1024) {
@@ -423,6 +481,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
       } else if constexpr (EPI == kEpiF32) {
         flush_f32(stg, static_cast<const float*>(d0), ng, ncols, lane);
         if (args.out16) flush_f16(stg, static_cast<const __half*>(d1), ng, ncols, lane);
+        if (args.nrm16) flush_f16_scaled(stg, static_cast<const __half*>(d2), ng, ncols, lane, sconst + BN + (ng - n0));
+        if (args.ss_out) {
+          if (row_ok) args.ss_out[static_cast<size_t>(ng >> 5) * args.ss_ld + mo] = ssg;
+          ssg = 0.0f;
+        }
       } else if constexpr (EPI == kEpiWnLast) {
         flush_f32(stg, static_cast<const float*>(d0), ng, ncols, lane);
       } else if constexpr (EPI == kEpiConv1Res) {
@@ -511,12 +574,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int kb = sbk * KBOX;  // first k-block of the stage (kb_split and kb_per_tap are multiples of KBOX)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          if (it == 0) GEMM_TRACE(18);
           if (!mbar_wait(&empty_bar[s], ph ^ 1, args.status, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
+          if (it == 0) GEMM_TRACE(19);
           uint8_t* sa = smem + s * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
+          if (it == 0) GEMM_TRACE(8);
           mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
           if (args.a_mode == kAConv5) {
             const int tap = kb / args.kb_per_tap;
@@ -598,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) GEMM_TRACE(7);
+  if (lane == 0) GEMM_TRACE(warp == 0 ? 7 : 8 + warp);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);

@@ -56,6 +56,24 @@ struct GemmArgs {
   int wn_first;
   int pad_rows;           // kEpiF32 only: A rows are the padded S*(T+4) space; write compact rows
   unsigned int* status;   // device status word
+  // AdaRMSNorm folded across a producer/consumer GEMM pair:
+  //   y = w*g*(x*inv) + b,  inv = 1/sqrt(mean_k x^2 + 1e-5)
+  //   y . W^T = inv * ((x*w*g) . W^T) + (b . W^T)
+  // Producer (kEpiF32): nrm16 = f16(v * nrm_w * nrm_g) and, per 32-column
+  // group p of the output, ss_out[p * ss_ld + row] = sum of v^2 over the group
+  // (the partial count never depends on the tile width).
+  // Consumer (kEpiQKV, kEpiSwiGLU): the accumulator of row m is multiplied by
+  // 1/sqrt(sum_p ss_in[p * ss_ld + m] / ss_n + 1e-5) before `bias` (which then
+  // holds b . W^T) is added.
+  __half* nrm16;
+  int ldn;
+  const float* nrm_w;
+  const float* nrm_g;
+  float* ss_out;
+  const float* ss_in;
+  int ss_parts;
+  int ss_n;
+  int ss_ld;
 };
 
 struct GemmLaunch {

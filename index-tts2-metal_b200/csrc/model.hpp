@@ -22,13 +22,17 @@ namespace itts {
 
 constexpr int kLayers = 13;
 constexpr int kWnLayers = 8;
-constexpr int kTcondPerStep = 36864;  // floats per step in the t-conditioning table
 // Offsets (floats) inside one step's table row.
 constexpr int kTabAttn = 0;           // + L*1024: [w | b] of attention_norm
 constexpr int kTabFfn = 13 * 1024;    // + L*1024: [w | b] of ffn_norm
 constexpr int kTabNorm = 26 * 1024;   // [w | b] of transformer.norm
 constexpr int kTabFinal = 27 * 1024;  // [shift | scale] of final_layer.adaLN_modulation
 constexpr int kTabWn = 28 * 1024;     // + l*1024: WaveNet global condition [a | b]
+// Folded AdaRMS: the shift b of each norm pushed through the following GEMM
+// (b . W^T, in the GEMM's B-row order), added in that GEMM's epilogue.
+constexpr int kTabQkvC = 36 * 1024;                // + L*1536: b_attn . Wqkv^T
+constexpr int kTabW13C = kTabQkvC + 13 * 1536;     // + L*3072: b_ffn . W13^T (interleaved rows)
+constexpr int kTcondPerStep = kTabW13C + 13 * 3072;  // floats per step in the t-conditioning table
 
 struct LayerW {
   __half* wqkv = nullptr;   // [1536][512]
