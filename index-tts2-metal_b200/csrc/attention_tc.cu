@@ -5,12 +5,14 @@
 //   warp 0      : TMA producer (Q once; K and V blocks into a 2-deep ring) and
 //                 the per-block key-mask bias row
 //   warp 1 (l0) : tcgen05.mma issuer: S_j = Q K_j^T (M=128, N=128, K=64) and
-//                 O_j = P_j V_j (M=128, N=64, K=128; V is read MN-major)
-//   warps 2..9  : online softmax, two warps per query row quarter (64 keys
-//                 each): S_j from TMEM, P_j (f16) into shared memory in the
-//                 UMMA operand layout, O_j from TMEM accumulated in registers
-//                 with the running rescale, normalised output to global memory.
-// TMEM: S double buffer (2 x 128 columns) and O double buffer (2 x 64).
+//                 O_h += P_j,h V_j,h per 64-key half h (M=128, N=64, K=64; V
+//                 is read MN-major)
+//   warps 2..9  : online softmax, two warps per query row quarter, each over
+//                 its own 64-key half of every block: S_j from TMEM, P_j (f16)
+//                 into shared memory in the UMMA operand layout; O stays in
+//                 TMEM (rescaled lazily there); the halves merge at the end.
+// TMEM: S double buffer (2 x 128 columns) and one O accumulator per key half
+// (2 x 64 columns).
 //
 // Semantics follow cpu_attention_single_head_masked
 // (runtime/impl/tokenizer_tests.cpp:3960-3997): keys with mask 0 get
@@ -58,18 +60,19 @@ enum : unsigned int { kDevTimeoutAttn = 16 };
 #define ATTN_TRACE(slot) ((void)0)
 #endif
 
-// 2^x on the special-function unit (|rel err| < 2^-22; inputs here are <= 0).
+// 2^x on the special-function unit (|rel err| < 2^-22; inputs here are <= 8).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-// 2^x on the FMA/ALU pipes, for x <= 0: x = i + f with i = round(x) (via the
-// 1.5*2^23 rounding constant) and f in [-0.5, 0.5]; 2^f from a degree-4
-// polynomial fitted to relative error 2.7e-6 on that interval; 2^i added to
-// the exponent bits. x is clamped at -125 so the result stays a normal
-// number (2^-125 rounds to 0 in the f16 P operand).
+// 2^x on the FMA/ALU pipes, for x <= 8 (the lazily rescaled softmax keeps
+// exponents there): x = i + f with i = round(x) (via the 1.5*2^23 rounding
+// constant) and f in [-0.5, 0.5]; 2^f from a degree-4 polynomial fitted to
+// relative error 2.7e-6 on that interval; 2^i added to the exponent bits. x is
+// clamped at -125 so the result stays a normal number (2^-125 rounds to 0 in
+// the f16 P operand).
 __device__ __forceinline__ float ex2_poly(float x) {
   x = fmaxf(x, -125.0f);
   const float kRound = 12582912.0f;  // 1.5 * 2^23
@@ -96,9 +99,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   uint64_t* s_full = kv_empty + kKV;     // 2
   uint64_t* s_free = s_full + 2;         // 2
   uint64_t* p_full = s_free + 2;         // 2
-  uint64_t* o_full = p_full + 2;         // 2
-  uint64_t* o_free = o_full + 2;         // 2
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+  uint64_t* o_full = p_full + 2;         // 2: O MMAs of the blocks using P buffer 0 / 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
   float* bias = reinterpret_cast<float*>(sm + OFF_BIAS);
   int* full_block = reinterpret_cast<int*>(sm + OFF_FLAG);
 
@@ -119,7 +121,6 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       mbar_init(&s_free[i], 8);  // one arrival per softmax warp
       mbar_init(&p_full[i], 8);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 8);
     }
     fence_barrier_init();
     fence_proxy_async_shared();
@@ -182,91 +183,59 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         if (!mbar_wait(&kv_full[kst], (j / kKV) & 1, status, kDevTimeoutAttn)) return false;
         if (!mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, status, kDevTimeoutAttn)) return false;
         tc_fence_after();
-        if (j < 8) ATTN_TRACE(2 + j);  // slots 2..9: S_j waits done
         const uint32_t sk = smem_u32(sm + OFF_K + kst * 16384);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_f16_ss(tmem + TMEM_S + st * 128, sdesc_k_sw128(sq + k * 32), sdesc_k_sw128(sk + k * 32), idesc_s,
                       k != 0 ? 1u : 0u);
         umma_commit(&s_full[st]);
-        if (j < 8) ATTN_TRACE(10 + j);
         return true;
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < nkb && ok; ++j) {
         const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
         if (j + 1 < nkb && !issue_s(j + 1)) break;
-        if (!mbar_wait(&p_full[st], ph, status, kDevTimeoutAttn)) break;
-        if (!mbar_wait(&o_free[st], ph ^ 1, status, kDevTimeoutAttn)) break;
+        if (!mbar_wait(&p_full[st], (j >> 1) & 1, status, kDevTimeoutAttn)) break;
         tc_fence_after();
         if (j < 4) ATTN_TRACE(56 + j);  // slots 56..59: O_j waits done
         const uint32_t sp = smem_u32(sm + OFF_P + st * 32768);
         const uint32_t sv = smem_u32(sm + OFF_V + (j % kKV) * 16384);
+        // O_h += P_h V_h for the two 64-key halves; each half accumulates
+        // into its own TMEM columns across all key blocks.
 #pragma unroll
-        for (int kk = 0; kk < kKB / 16; ++kk)
-          umma_f16_ss(tmem + TMEM_O + st * 64, sdesc_k_sw128(sp + (kk >> 2) * 16384 + (kk & 3) * 32),
-                      sdesc_mn_sw128(sv + kk * 2048), idesc_o, kk != 0 ? 1u : 0u);
+        for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_ss(tmem + TMEM_O + hh * 64, sdesc_k_sw128(sp + hh * 16384 + kk * 32),
+                        sdesc_mn_sw128(sv + (hh * 4 + kk) * 2048), idesc_o, (j | kk) != 0 ? 1u : 0u);
+        }
         umma_commit(&o_full[st]);
         umma_commit(&kv_empty[j % kKV]);
-        if (j < 8) ATTN_TRACE(40 + j);
       }
     }
     __syncwarp();
   } else {
-    // ---- softmax: warps 2..9; the two warps of a TMEM lane quarter share 32
-    // query rows, each owning 64 of the 128 keys of a block and 32 of the 64
-    // output dims. The row maximum is exchanged through shared memory.
+    // ---- softmax: warps 2..9. The two warps of a TMEM lane quarter share 32
+    // query rows; warp half hh owns keys [64 hh, 64 hh + 64) of every block
+    // and runs its own online softmax over them (its own running maximum m,
+    // row sum l and TMEM accumulator O_hh), so the pair never synchronises
+    // inside the key loop. The halves are merged once at the end.
+    // O_hh and l are rescaled lazily: only when a block's maximum exceeds the
+    // reference m by more than 8 in log2 units (P <= 2^8 stays exact in f16).
     const int quarter = warp & 3;
-    const int hh = (warp - 2) >> 2;  // key half / output-dim half
+    const int hh = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_o = tmem + lane_off + TMEM_O + hh * 64;
     const float kLog2e = 1.4426950408889634f;
+    const float kLazy = 8.0f / kLog2e;
     float* xval = reinterpret_cast<float*>(sm + OFF_XCH);          // [3 slots][2 halves][128 rows]
     volatile int* xtag = reinterpret_cast<volatile int*>(sm + OFF_XTAG);  // [2 halves][128 rows]
-    float o[32];
-#pragma unroll
-    for (int d = 0; d < 32; ++d) o[d] = 0.0f;
-    float m = -CUDART_INF_F, l = 0.0f, alpha_prev = 0.0f;
+    float m = -CUDART_INF_F, l = 0.0f;
     bool ok = true;
-    // Hand `val` to the partner warp (same row, other half) and return the
-    // partner's value for the same tag. Tags grow monotonically; the wait is
-    // bounded and records kDevTimeoutAttn instead of hanging.
-    auto exchange = [&](float val, int slot, int tag, bool& good) -> float {
-      xval[(slot * 2 + hh) * 128 + row] = val;
-      __threadfence_block();
-      xtag[hh * 128 + row] = tag;
-      const long long t0 = clock64();
-      while (xtag[(hh ^ 1) * 128 + row] < tag) {
-        if (clock64() - t0 > kWaitBudgetCycles) {
-          if (status) atomicCAS(status, 0u, static_cast<unsigned int>(kDevTimeoutAttn));
-          good = false;
-          return 0.0f;
-        }
-      }
-      __threadfence_block();
-      return xval[(slot * 2 + (hh ^ 1)) * 128 + row];
-    };
-    auto accumulate_o = [&](int jp) -> bool {
-      const int st = jp & 1;
-      if (!mbar_wait(&o_full[st], (jp >> 1) & 1, status, kDevTimeoutAttn)) return false;
-      tc_fence_after();
-      uint32_t r0[32];
-      tmem_ld32_async(tmem + lane_off + TMEM_O + st * 64 + hh * 32, r0);
-      tmem_wait_ld();
-      reg_fence32(r0);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[st]);
-      if (warp == 2 && lane == 0 && jp < 8) ATTN_TRACE(50 + jp);
-#pragma unroll
-      for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha_prev + __uint_as_float(r0[d]);
-      return true;
-    };
     for (int j = 0; j < nkb && ok; ++j) {
       const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait(&s_full[st], ph, status, kDevTimeoutAttn)) {
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1, status, kDevTimeoutAttn)) {
         ok = false;
         break;
       }
@@ -292,22 +261,45 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 #pragma unroll
         for (int k = 0; k < 64; ++k) sr[k] = __float_as_uint(__uint_as_float(sr[k]) + brow[k]);
       }
-      // Row max: 8 partial maxima over this warp's 64 keys, then the partner's.
       float mp[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mp[e] = __uint_as_float(sr[e]);
 #pragma unroll
       for (int k = 8; k < 64; ++k) mp[k & 7] = fmaxf(mp[k & 7], __uint_as_float(sr[k]));
-      float mine = mp[0];
+      float mb = mp[0];
 #pragma unroll
-      for (int e = 1; e < 8; ++e) mine = fmaxf(mine, mp[e]);
-      const float other = exchange(mine, st, j + 1, ok);
-      if (!ok) break;
-      const float mx = fmaxf(m, fmaxf(mine, other));
-      const float ref = (mx == -CUDART_INF_F) ? 0.0f : mx;
-      const float alpha = ex2_approx((m - ref) * kLog2e);
-      const float nref = -ref * kLog2e;
-      m = mx;
+      for (int e = 1; e < 8; ++e) mb = fmaxf(mb, mp[e]);
+      if (mb > m + kLazy) {  // the first live key, or a maximum grown past 2^8
+        if (m != -CUDART_INF_F) {
+          // O_hh and l hold contributions relative to m: rescale them once
+          // the previous block's O MMA has landed.
+          const float alpha = ex2_approx((m - mb) * kLog2e);
+          l *= alpha;
+          if (!mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, status, kDevTimeoutAttn)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t ov[32];
+            tmem_ld32_async(t_o + c * 32, ov);
+            tmem_wait_ld();
+            reg_fence32(ov);
+#pragma unroll
+            for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+            tmem_st32(t_o + c * 32, ov);
+          }
+          tmem_wait_st();
+        }
+        m = mb;
+      }
+      // P buffer st is free once the O MMA of block j - 2 has read it.
+      if (j >= 2 && !mbar_wait(&o_full[st], ((j - 2) >> 1) & 1, status, kDevTimeoutAttn)) {
+        ok = false;
+        break;
+      }
+      const float nref = (m == -CUDART_INF_F) ? 0.0f : -m * kLog2e;
       float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
       uint8_t* ptile = sm + OFF_P + st * 32768 + hh * 16384 + row * 128;
 #pragma unroll
@@ -328,34 +320,66 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         for (int e = 0; e < 4; ++e) pk.h2[e] = __floats2half2_rn(p[2 * e], p[2 * e + 1]);
         *reinterpret_cast<uint4*>(ptile + ((c ^ (row & 7)) << 4)) = pk.u;
       }
-      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-      l = l * alpha + sum;  // this warp's partial row sum
+      l += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       fence_proxy_async_shared();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[st]);
       if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(30 + j);
-      if (j >= 1 && !accumulate_o(j - 1)) {
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
     }
-    if (ok) ok = accumulate_o(nkb - 1);
-    // Combine the two partial row sums.
-    float l_all = l;
-    if (ok) l_all += exchange(l, 2, nkb + 1, ok);
-    if (ok && q0 + row < T) {
-      const float inv = l_all > 0.0f ? 1.0f / l_all : 0.0f;
-      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(seq0 + q0 + row) * 512 + h * 64 + hh * 32);
+    // Merge the two key halves of the row: each warp hands the partner the 32
+    // output dims the partner writes (through the now idle P buffers), its
+    // reference maximum and its row sum.
+    uint32_t ov[32], oth[32];  // O_hh at this warp's output dims / at the partner's
+    if (ok) ok = mbar_wait(&o_full[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, status, kDevTimeoutAttn);
+    if (ok) {
+      tc_fence_after();
+      tmem_ld32_async(t_o + hh * 32, ov);
+      tmem_ld32_async(t_o + (hh ^ 1) * 32, oth);
+      tmem_wait_ld();
+      reg_fence32(ov);
+      reg_fence32(oth);
+      float* ox = reinterpret_cast<float*>(sm + OFF_P);  // [reader half][32 dims][128 rows]
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        union {
-          __half2 h2[4];
-          uint4 u;
-        } pk;
+      for (int d = 0; d < 32; ++d) ox[((hh ^ 1) * 32 + d) * 128 + row] = __uint_as_float(oth[d]);
+      xval[(1 * 2 + hh) * 128 + row] = l;
+      xval[(0 * 2 + hh) * 128 + row] = m;
+      __threadfence_block();
+      xtag[hh * 128 + row] = 1;
+      const long long t0 = clock64();
+      while (xtag[(hh ^ 1) * 128 + row] < 1) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+          if (status) atomicCAS(status, 0u, static_cast<unsigned int>(kDevTimeoutAttn));
+          ok = false;
+          break;
+        }
+      }
+      __threadfence_block();
+      if (ok && q0 + row < T) {
+        const float mo = xval[(0 * 2 + (hh ^ 1)) * 128 + row];
+        const float lo = xval[(1 * 2 + (hh ^ 1)) * 128 + row];
+        const float mm = fmaxf(m, mo);
+        const float as = (m == -CUDART_INF_F) ? 0.0f : ex2_approx((m - mm) * kLog2e);
+        const float ao = (mo == -CUDART_INF_F) ? 0.0f : ex2_approx((mo - mm) * kLog2e);
+        const float lsum = l * as + lo * ao;
+        const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+        const float* mine = ox + (hh * 32) * 128 + row;
+        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(seq0 + q0 + row) * 512 + h * 64 + hh * 32);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) pk.h2[e] = __floats2half2_rn(o[c * 8 + 2 * e] * inv, o[c * 8 + 2 * e + 1] * inv);
-        dst[c] = pk.u;
+        for (int c = 0; c < 4; ++c) {
+          union {
+            __half2 h2[4];
+            uint4 u;
+          } pk;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d0 = c * 8 + 2 * e;
+            const float v0 = (__uint_as_float(ov[d0]) * as + mine[d0 * 128] * ao) * inv;
+            const float v1 = (__uint_as_float(ov[d0 + 1]) * as + mine[(d0 + 1) * 128] * ao) * inv;
+            pk.h2[e] = __floats2half2_rn(v0, v1);
+          }
+          dst[c] = pk.u;
+        }
       }
     }
   }
