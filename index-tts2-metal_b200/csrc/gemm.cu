@@ -557,6 +557,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The B operand is always weights, which no kernel of the stream writes: the
+  // producer starts the first tile's B loads before waiting for the previous
+  // kernel, so they overlap its tail. Stage accounting is unchanged (one
+  // arrive with the full stage byte count; the A half follows below).
+  const int num_pre = num_sb < STAGES ? num_sb : STAGES;
+  if (warp == 0 && lane == 0) {
+    const int n0 = (blockIdx.x % n_tiles) * BN;
+    for (int sbk = 0; sbk < num_pre; ++sbk) {
+      uint8_t* sb = smem + sbk * STAGE_BYTES + A_BYTES;
+      mbar_arrive_expect_tx(&full_bar[sbk], STAGE_BYTES);
+      tma_load_3d(sb, &tmB, &full_bar[sbk], 0, n0, sbk * KBOX);
+    }
+  }
   // Everything below reads or writes memory of the previous kernel in the stream.
   griddep_wait();
   griddep_launch();
@@ -575,7 +588,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (it == 0) GEMM_TRACE(18);
-          if (!mbar_wait(&empty_bar[s], ph ^ 1, args.status, kDevTimeoutEmpty)) {
+          const bool pre = it < num_pre;  // B already in flight (issued before griddep_wait)
+          if (!pre && !mbar_wait(&empty_bar[s], ph ^ 1, args.status, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
@@ -583,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + s * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           if (it == 0) GEMM_TRACE(8);
-          mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+          if (!pre) mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
           if (args.a_mode == kAConv5) {
             const int tap = kb / args.kb_per_tap;
             const int kc = kb - tap * args.kb_per_tap;
@@ -593,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0, kb);
           }
-          tma_load_3d(sb, &tmB, &full_bar[s], 0, n0, kb);
+          if (!pre) tma_load_3d(sb, &tmB, &full_bar[s], 0, n0, kb);
           if (it == 0) GEMM_TRACE(2);
         }
       }
