@@ -41,14 +41,16 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_K = 16384;                      // kKV stages x 16 KB
 constexpr int OFF_V = OFF_K + kKV * 16384;        // kKV stages x 16 KB
 constexpr int OFF_P = OFF_V + kKV * 16384;        // 2 buffers x 32 KB
-constexpr int OFF_BIAS = OFF_P + 2 * 32768;       // kKV x 128 floats
+constexpr int OFF_ONES = OFF_P + 2 * 32768;       // 16 rows x 128 B: the ones column appended to V
+constexpr int OFF_BIAS = OFF_ONES + 2048;         // kKV x 128 floats
 constexpr int OFF_FLAG = OFF_BIAS + kKV * kKB * 4;  // kKV ints: block has no masked key
 constexpr int OFF_XCH = OFF_FLAG + 16;               // row-max / row-sum exchange: 6 x 128 floats
 constexpr int OFF_XTAG = OFF_XCH + 6 * 128 * 4;      // exchange tags: 2 halves x 128 rows
 constexpr int OFF_BAR = OFF_XTAG + 2 * 128 * 4;
 constexpr int SMEM_A = 1024 + OFF_BAR + 256;
 constexpr uint32_t TMEM_S = 0;    // + 128 * stage
-constexpr uint32_t TMEM_O = 256;  // + 64 * stage
+constexpr uint32_t TMEM_O = 256;  // + 128 * key half: 64 output dims, then the row sum (column 64)
+constexpr int kON = 80;           // O MMA width: 64 dims of V plus the ones column (and 15 zero columns)
 
 enum : unsigned int { kDevTimeoutAttn = 16 };
 
@@ -69,22 +71,29 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 // 2^x on the FMA/ALU pipes, for x <= 8 (the lazily rescaled softmax keeps
 // exponents there): x = i + f with i = round(x) (via the 1.5*2^23 rounding
-// constant) and f in [-0.5, 0.5]; 2^f from a degree-4 polynomial fitted to
-// relative error 2.7e-6 on that interval; 2^i added to the exponent bits. x is
-// clamped at -125 so the result stays a normal number (2^-125 rounds to 0 in
-// the f16 P operand).
+// constant) and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted
+// (weighted least squares iterated towards minimax) to relative error 7.5e-5
+// on that interval, below the 4.9e-4 rounding of the f16 P operand; 2^i added
+// to the exponent bits. x is clamped at -125 so the result stays a normal
+// number (2^-125 rounds to 0 in the f16 P operand).
 __device__ __forceinline__ float ex2_poly(float x) {
   x = fmaxf(x, -125.0f);
   const float kRound = 12582912.0f;  // 1.5 * 2^23
   const float t = x + kRound;
   const int i = __float_as_int(t) - __float_as_int(kRound);
   const float f = x - (t - kRound);
-  float p = 0.00956052f;
-  p = fmaf(p, f, 0.05591704f);
-  p = fmaf(p, f, 0.24024981f);
-  p = fmaf(p, f, 0.69312197f);
-  p = fmaf(p, f, 0.99999917f);
+  float p = 0.05517167f;
+  p = fmaf(p, f, 0.24261114f);
+  p = fmaf(p, f, 0.69326097f);
+  p = fmaf(p, f, 0.99992806f);
   return __int_as_float(__float_as_int(p) + (i << 23));
+}
+
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __global__ void __launch_bounds__(kThreadsA, 1)
@@ -133,6 +142,15 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   // Exchange tags start at 0 for every row and half (shared memory is not
   // cleared between CTAs); the barrier below publishes them.
   if (threadIdx.x < 2 * 128) reinterpret_cast<int*>(sm + OFF_XTAG)[threadIdx.x] = 0;
+  // The ones column of the O MMA: element 64 of every key row of V's second
+  // MN atom is 1 (so column 64 of O accumulates the row sum of P), elements
+  // 65..127 are 0. 16 key rows in the 128-byte swizzle (chunk c of row r at
+  // chunk c ^ (r & 7)); every K16 step of the MMA points here through its LBO.
+  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+    const int r = i >> 5, w = i & 31;
+    reinterpret_cast<uint32_t*>(sm + OFF_ONES)[i] = ((w >> 2) == (r & 7) && (w & 3) == 0) ? 0x3C00u : 0u;
+  }
+  fence_proxy_async_shared();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -174,7 +192,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     // ---- MMA issuer ----
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(128, kKB);
-      constexpr uint32_t idesc_o = idesc_f16_f32(128, 64) | (1u << 16);  // B (V) MN-major
+      constexpr uint32_t idesc_o = idesc_f16_f32(128, kON) | (1u << 16);  // B (V | ones) MN-major
+      const uint32_t s_ones = smem_u32(sm + OFF_ONES);
       const uint32_t sq = smem_u32(sm + OFF_Q);
       bool ok = mbar_wait(q_full, 0, status, kDevTimeoutAttn);
       auto issue_s = [&](int j) -> bool {
@@ -200,14 +219,16 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         if (j < 4) ATTN_TRACE(56 + j);  // slots 56..59: O_j waits done
         const uint32_t sp = smem_u32(sm + OFF_P + st * 32768);
         const uint32_t sv = smem_u32(sm + OFF_V + (j % kKV) * 16384);
-        // O_h += P_h V_h for the two 64-key halves; each half accumulates
-        // into its own TMEM columns across all key blocks.
+        // [O_h | l_h] += P_h [V_h | 1] for the two 64-key halves; each half
+        // accumulates into its own TMEM columns across all key blocks.
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_f16_ss(tmem + TMEM_O + hh * 64, sdesc_k_sw128(sp + hh * 16384 + kk * 32),
-                        sdesc_mn_sw128(sv + (hh * 4 + kk) * 2048), idesc_o, (j | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t vb = sv + (hh * 4 + kk) * 2048;
+            umma_f16_ss(tmem + TMEM_O + hh * 128, sdesc_k_sw128(sp + hh * 16384 + kk * 32),
+                        sdesc_mn_sw128_lbo(vb, s_ones - vb), idesc_o, (j | kk) != 0 ? 1u : 0u);
+          }
         }
         umma_commit(&o_full[st]);
         umma_commit(&kv_empty[j % kKV]);
@@ -226,12 +247,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     const int hh = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t t_o = tmem + lane_off + TMEM_O + hh * 64;
+    const uint32_t t_o = tmem + lane_off + TMEM_O + hh * 128;
     const float kLog2e = 1.4426950408889634f;
     const float kLazy = 8.0f / kLog2e;
     float* xval = reinterpret_cast<float*>(sm + OFF_XCH);          // [3 slots][2 halves][128 rows]
     volatile int* xtag = reinterpret_cast<volatile int*>(sm + OFF_XTAG);  // [2 halves][128 rows]
-    float m = -CUDART_INF_F, l = 0.0f;
+    float m = -CUDART_INF_F;  // reference maximum of O_hh and its row sum (TMEM column 64)
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       const int st = j & 1;
@@ -263,18 +284,22 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       }
       float mp[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mp[e] = __uint_as_float(sr[e]);
+      for (int e = 0; e < 8; ++e)
+        mp[e] = fmax3(__uint_as_float(sr[e]), __uint_as_float(sr[8 + e]), __uint_as_float(sr[16 + e]));
 #pragma unroll
-      for (int k = 8; k < 64; ++k) mp[k & 7] = fmaxf(mp[k & 7], __uint_as_float(sr[k]));
-      float mb = mp[0];
+      for (int k = 24; k < 56; k += 16) {
 #pragma unroll
-      for (int e = 1; e < 8; ++e) mb = fmaxf(mb, mp[e]);
+        for (int e = 0; e < 8; ++e) mp[e] = fmax3(mp[e], __uint_as_float(sr[k + e]), __uint_as_float(sr[k + 8 + e]));
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mp[e] = fmaxf(mp[e], __uint_as_float(sr[56 + e]));
+      const float mb = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+      if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(40 + j);
       if (mb > m + kLazy) {  // the first live key, or a maximum grown past 2^8
         if (m != -CUDART_INF_F) {
-          // O_hh and l hold contributions relative to m: rescale them once
-          // the previous block's O MMA has landed.
+          // O_hh and its row sum hold contributions relative to m: rescale
+          // them once the previous block's O MMA has landed.
           const float alpha = ex2_approx((m - mb) * kLog2e);
-          l *= alpha;
           if (!mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, status, kDevTimeoutAttn)) {
             ok = false;
             break;
@@ -290,6 +315,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
             for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
             tmem_st32(t_o + c * 32, ov);
           }
+          uint32_t lv[16];
+          tmem_ld16_async(t_o + 64, lv);
+          tmem_wait_ld();
+          reg_fence16(lv);
+          lv[0] = __float_as_uint(__uint_as_float(lv[0]) * alpha);
+          tmem_st16(t_o + 64, lv);
           tmem_wait_st();
         }
         m = mb;
@@ -300,7 +331,6 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         break;
       }
       const float nref = (m == -CUDART_INF_F) ? 0.0f : -m * kLog2e;
-      float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
       uint8_t* ptile = sm + OFF_P + st * 32768 + hh * 16384 + row * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 keys = this warp's 64-key k-block of P
@@ -310,7 +340,6 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           // One in four on the FMA pipe, the rest on the SFU (the units run in parallel).
           const float xe = fmaf(__uint_as_float(sr[c * 8 + e]), kLog2e, nref);
           p[e] = (e & 3) == 3 ? ex2_poly(xe) : ex2_approx(xe);
-          sp[e] += p[e];
         }
         union {
           __half2 h2[4];
@@ -320,7 +349,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         for (int e = 0; e < 4; ++e) pk.h2[e] = __floats2half2_rn(p[2 * e], p[2 * e + 1]);
         *reinterpret_cast<uint4*>(ptile + ((c ^ (row & 7)) << 4)) = pk.u;
       }
-      l += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+      if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(50 + j);
       fence_proxy_async_shared();
       tc_fence_before();
       __syncwarp();
@@ -330,15 +359,18 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     // Merge the two key halves of the row: each warp hands the partner the 32
     // output dims the partner writes (through the now idle P buffers), its
     // reference maximum and its row sum.
-    uint32_t ov[32], oth[32];  // O_hh at this warp's output dims / at the partner's
+    uint32_t ov[32], oth[32], lv[16];  // O_hh at this warp's output dims / at the partner's; row sum
     if (ok) ok = mbar_wait(&o_full[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, status, kDevTimeoutAttn);
     if (ok) {
       tc_fence_after();
       tmem_ld32_async(t_o + hh * 32, ov);
       tmem_ld32_async(t_o + (hh ^ 1) * 32, oth);
+      tmem_ld16_async(t_o + 64, lv);
       tmem_wait_ld();
       reg_fence32(ov);
       reg_fence32(oth);
+      reg_fence16(lv);
+      const float l = __uint_as_float(lv[0]);
       float* ox = reinterpret_cast<float*>(sm + OFF_P);  // [reader half][32 dims][128 rows]
 #pragma unroll
       for (int d = 0; d < 32; ++d) ox[((hh ^ 1) * 32 + d) * 128 + row] = __uint_as_float(oth[d]);
