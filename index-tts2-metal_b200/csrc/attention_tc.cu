@@ -5,12 +5,13 @@
 //   warp 0      : TMA producer (Q once; K and V blocks into a 2-deep ring) and
 //                 the per-block key-mask bias row
 //   warp 1 (l0) : tcgen05.mma issuer: S_j = Q K_j^T (M=128, N=128, K=64) and
-//                 O_h += P_j,h V_j,h per 64-key half h (M=128, N=64, K=64; V
-//                 is read MN-major)
+//                 [O_h | l_h] += P_j,h [V_j,h | 1] per 64-key half h (M=128,
+//                 N=80, K=64; P from TMEM, V read MN-major from shared memory)
 //   warps 2..9  : online softmax, two warps per query row quarter, each over
 //                 its own 64-key half of every block: S_j from TMEM, P_j (f16)
-//                 into shared memory in the UMMA operand layout; O stays in
-//                 TMEM (rescaled lazily there); the halves merge at the end.
+//                 back into TMEM over the S_j columns it has read (the O MMA's
+//                 A operand); O stays in TMEM (rescaled lazily there); the
+//                 halves merge at the end.
 // TMEM: S double buffer (2 x 128 columns) and one O accumulator per key half
 // (2 x 64 columns).
 //
@@ -40,8 +41,7 @@ constexpr int kKV = 4;     // K/V ring depth (blocks in flight)
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = 16384;                      // kKV stages x 16 KB
 constexpr int OFF_V = OFF_K + kKV * 16384;        // kKV stages x 16 KB
-constexpr int OFF_P = OFF_V + kKV * 16384;        // 2 buffers x 32 KB
-constexpr int OFF_ONES = OFF_P + 2 * 32768;       // 16 rows x 128 B: the ones column appended to V
+constexpr int OFF_ONES = OFF_V + kKV * 16384;     // 16 rows x 128 B: the ones column appended to V
 constexpr int OFF_BIAS = OFF_ONES + 2048;         // kKV x 128 floats
 constexpr int OFF_FLAG = OFF_BIAS + kKV * kKB * 4;  // kKV ints: block has no masked key
 constexpr int OFF_XCH = OFF_FLAG + 16;               // row-max / row-sum exchange: 6 x 128 floats
@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   uint64_t* s_full = kv_empty + kKV;     // 2
   uint64_t* s_free = s_full + 2;         // 2
   uint64_t* p_full = s_free + 2;         // 2
-  uint64_t* o_full = p_full + 2;         // 2: O MMAs of the blocks using P buffer 0 / 1
+  uint64_t* o_full = p_full + 2;         // 2: O MMAs of the blocks using S/P buffer 0 / 1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
   float* bias = reinterpret_cast<float*>(sm + OFF_BIAS);
   int* full_block = reinterpret_cast<int*>(sm + OFF_FLAG);
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 8);  // one arrival per softmax warp
+      mbar_init(&s_free[i], 1);  // commit after the O MMA that read P from this S buffer
       mbar_init(&p_full[i], 8);
       mbar_init(&o_full[i], 1);
     }
@@ -217,7 +217,6 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         if (!mbar_wait(&p_full[st], (j >> 1) & 1, status, kDevTimeoutAttn)) break;
         tc_fence_after();
         if (j < 4) ATTN_TRACE(56 + j);  // slots 56..59: O_j waits done
-        const uint32_t sp = smem_u32(sm + OFF_P + st * 32768);
         const uint32_t sv = smem_u32(sm + OFF_V + (j % kKV) * 16384);
         // [O_h | l_h] += P_h [V_h | 1] for the two 64-key halves; each half
         // accumulates into its own TMEM columns across all key blocks.
@@ -226,11 +225,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t vb = sv + (hh * 4 + kk) * 2048;
-            umma_f16_ss(tmem + TMEM_O + hh * 128, sdesc_k_sw128(sp + hh * 16384 + kk * 32),
+            umma_f16_ts(tmem + TMEM_O + hh * 128, tmem + TMEM_S + st * 128 + hh * 64 + kk * 8,
                         sdesc_mn_sw128_lbo(vb, s_ones - vb), idesc_o, (j | kk) != 0 ? 1u : 0u);
           }
         }
         umma_commit(&o_full[st]);
+        umma_commit(&s_free[st]);  // P_j (over S_j) consumed: the buffer may take S_{j+2}
         umma_commit(&kv_empty[j % kKV]);
       }
     }
@@ -267,9 +267,6 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       tmem_wait_ld();
       reg_fence32(sr);
       reg_fence32(sr + 32);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[st]);
       if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(20 + j);
       // The mask row of this block was published with kv_full (already complete).
       const int kst = j % kKV;
@@ -325,15 +322,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         }
         m = mb;
       }
-      // P buffer st is free once the O MMA of block j - 2 has read it.
-      if (j >= 2 && !mbar_wait(&o_full[st], ((j - 2) >> 1) & 1, status, kDevTimeoutAttn)) {
-        ok = false;
-        break;
-      }
+      // P (f16 pairs, key order) overwrites the first 32 of this warp's 64 S
+      // columns, which it has already read; the O MMA takes it from there.
       const float nref = (m == -CUDART_INF_F) ? 0.0f : -m * kLog2e;
-      uint8_t* ptile = sm + OFF_P + st * 32768 + hh * 16384 + row * 128;
+      uint32_t pw[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 keys = this warp's 64-key k-block of P
+      for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 keys
         float p[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -341,16 +335,15 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           const float xe = fmaf(__uint_as_float(sr[c * 8 + e]), kLog2e, nref);
           p[e] = (e & 3) == 3 ? ex2_poly(xe) : ex2_approx(xe);
         }
-        union {
-          __half2 h2[4];
-          uint4 u;
-        } pk;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) pk.h2[e] = __floats2half2_rn(p[2 * e], p[2 * e + 1]);
-        *reinterpret_cast<uint4*>(ptile + ((c ^ (row & 7)) << 4)) = pk.u;
+        for (int e = 0; e < 4; ++e) {
+          const __half2 h2 = __floats2half2_rn(p[2 * e], p[2 * e + 1]);
+          pw[c * 4 + e] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
       }
       if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(50 + j);
-      fence_proxy_async_shared();
+      tmem_st32(tmem + lane_off + TMEM_S + st * 128 + hh * 64, pw);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[st]);
@@ -371,7 +364,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       reg_fence32(oth);
       reg_fence16(lv);
       const float l = __uint_as_float(lv[0]);
-      float* ox = reinterpret_cast<float*>(sm + OFF_P);  // [reader half][32 dims][128 rows]
+      float* ox = reinterpret_cast<float*>(sm + OFF_K);  // [reader half][32 dims][128 rows] over the idle K ring
 #pragma unroll
       for (int d = 0; d < 32; ++d) ox[((hh ^ 1) * 32 + d) * 128 + row] = __uint_as_float(oth[d]);
       xval[(1 * 2 + hh) * 128 + row] = l;

@@ -172,6 +172,18 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t tmem_d, uint64_t adesc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (M x K, f16) read from tensor memory,
+// row m in lane m and two consecutive K elements per 32-bit column.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // ---- CTA-pair (cta_group::2) variants: M = 256 split over the pair, each CTA
 // holding 128 rows of A, half of B's rows and its 128 accumulator rows ----
 
