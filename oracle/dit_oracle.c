@@ -301,11 +301,17 @@ int orc_attention_layer(const orc_model* m, const float* xin, const uint32_t* ma
         sc[tk] = expf(sc[tk] - mx);
         den += sc[tk];
       }
-      for (int d = 0; d < 64; ++d) {
-        float acc = 0.0f;
-        for (int tk = 0; tk < T; ++tk) acc += (sc[tk] / den) * v[(size_t)tk * 512 + h * 64 + d];
-        cat[(size_t)tq * 512 + h * 64 + d] = acc;
+      /* acc[d] = sum over tk (ascending) of (sc[tk] / den) * v[tk][d]: the
+       * same operands and order per output as a d-outer loop, walked key-major
+       * so that V is read contiguously. */
+      float acc[64];
+      for (int d = 0; d < 64; ++d) acc[d] = 0.0f;
+      for (int tk = 0; tk < T; ++tk) {
+        const float pk = sc[tk] / den;
+        const float* vr = v + (size_t)tk * 512 + h * 64;
+        for (int d = 0; d < 64; ++d) acc[d] += pk * vr[d];
       }
+      for (int d = 0; d < 64; ++d) cat[(size_t)tq * 512 + h * 64 + d] = acc[d];
       free(sc);
     }
   }

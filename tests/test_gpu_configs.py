@@ -1,0 +1,93 @@
+"""BASELINE configs 3 and 4 at their full sizes on the GPU, through the C ABI.
+
+Config 4 (one utterance of T=4096, P=300, 25 steps, CFG 0.7) stresses the
+masked RoPE attention at long sequence length: one teacher-forced guided step
+is checked against the CPU oracle, and the full sampler for determinism.
+Config 3 (64 utterances, lengths drawn from 200..1500, 16 steps, CFG 0.7,
+length-bucketed with key-padding masks) is run whole through
+itts_cfm_run_batch; the shortest utterance is checked against the oracle's
+masked sampler at its bucket length, and the longest against a padded run of
+itself alone (bitwise: rows never mix across sequences).
+
+Gates as in test_gpu_parity: velocity cosine >= 0.999 and rel-L2 <= 1e-2;
+final mel max-abs <= 2e-2 or rel-L2 <= 1e-2."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import itts_cfm
+import oracle as O
+import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.999
+VEL_REL_L2 = 1e-2
+MEL_MAX_ABS = 2e-2
+MEL_REL_L2 = 1e-2
+
+
+def _vel_ok(ref, got):
+    c = O.compare(ref, got)
+    assert c["cosine"] >= COS_MIN and c["rel_l2"] <= VEL_REL_L2, c
+
+
+def _mel_ok(ref, got):
+    c = O.compare(ref, got)
+    assert c["max_abs"] <= MEL_MAX_ABS or c["rel_l2"] <= MEL_REL_L2, c
+
+
+@pytest.mark.timeout(900)
+def test_config4_long_utterance_step_vs_oracle(ctx_baseline, port_baseline):
+    """T=4096 (config 4): one guided step at t=0.48 on a noisy state, both CFG
+    branches on the GPU; the conditional velocity against the oracle."""
+    u = W.config_utterances(4)[0]
+    assert u.T == 4096
+    x = u.noise.copy()
+    x[: u.P] = 0
+    px = u.prompt_x()
+    mask = np.ones((1, u.T), np.uint32)
+    vel = ctx_baseline.estimator(x[None], px[None], u.cond[None], u.style[None], mask, t=0.48, branches=2)
+    assert np.isfinite(vel).all()
+    _vel_ok(port_baseline.estimator(x, px, u.cond, u.style, 0.48, mask[0]), vel[0, 0])
+
+
+@pytest.mark.timeout(600)
+def test_config4_full_sampler_deterministic(ctx_baseline):
+    """The whole config-4 sampler (25 steps, CFG 0.7) twice: bitwise identical,
+    finite, prompt rows zero."""
+    u = W.config_utterances(4)[0]
+    a = ctx_baseline.run(u.noise, u.prompt, u.cond, u.style, 25, 0.7)
+    b = ctx_baseline.run(u.noise, u.prompt, u.cond, u.style, 25, 0.7)
+    assert a.shape == (4096, 80)
+    assert np.isfinite(a).all()
+    assert np.all(a[: u.P] == 0.0)
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.timeout(900)
+def test_config3_bucketed_batch_full_size(ctx_baseline, port_baseline):
+    """All 64 config-3 utterances through itts_cfm_run_batch (16 steps, CFG 0.7)."""
+    utts = W.config_utterances(3)
+    assert len(utts) == 64
+    outs = ctx_baseline.run_batch(
+        [dict(noise=u.noise, prompt=u.prompt, cond=u.cond, style=u.style) for u in utts], 16, 0.7)
+    for u, o in zip(utts, outs):
+        assert o.shape == (u.T, 80)
+        assert np.isfinite(o).all()
+        assert np.all(o[: u.P] == 0.0)
+    # Shortest utterance: the oracle's masked sampler at the bucket length.
+    i = int(np.argmin([u.T for u in utts]))
+    u = utts[i]
+    Tp = itts_cfm.bucket_len(u.T)
+    vl, pl, noise, px, cond, style = W.pad_batch([u], Tp)
+    mask = (np.arange(Tp) < u.T).astype(np.uint32)
+    ref = port_baseline.euler(noise[0], px[0], cond[0], style[0], u.P, 16, 0.7, mask=mask)
+    _mel_ok(ref[: u.T], outs[i])
+    # Longest utterance: identical to a padded run of itself alone.
+    j = int(np.argmax([u.T for u in utts]))
+    u = utts[j]
+    vl, pl, noise, px, cond, style = W.pad_batch([u], itts_cfm.bucket_len(u.T))
+    alone = ctx_baseline.run_padded(vl, pl, noise, px, cond, style, 16, 0.7)[0, : u.T]
+    assert np.array_equal(alone, outs[j])
