@@ -368,9 +368,11 @@ int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a
     itts::GemmLaunch g;
     std::memset(&g, 0, sizeof(g));
     const uint32_t ka = a1 ? k0 : K;
-    need(!a1 || (k0 % 128 == 0 && k0 < K), "k0 must be a multiple of 128 below K");
-    need(K % 64 == 0, "K must be a multiple of 64 (zero-pad the operands)");
     const uint32_t kbox = static_cast<uint32_t>(itts::gemm_kbox(static_cast<int>(bn)));
+    need(!a1 || (k0 % (64 * kbox) == 0 && k0 < K),
+         "k0 must be below K and a multiple of 64 x the k-blocks per TMA box (256 for bn 64, 128 for bn 80/128, 64 for "
+         "bn 256)");
+    need(K % 64 == 0, "K must be a multiple of 64 (zero-pad the operands)");
     if (!itts::make_tmap_f16(&g.tmA0, a0, ka, M, lda0, 128, kbox)) throw ShapeError("A0 layout rejected by TMA");
     if (a1) {
       if (!itts::make_tmap_f16(&g.tmA1, a1, K - k0, M, lda1, 128, kbox)) throw ShapeError("A1 layout rejected by TMA");

@@ -86,8 +86,9 @@ struct GemmLaunch {
 };
 
 // k-blocks (64 columns each) fetched per TMA instruction: one TMA box moves
-// kbox x rows x 128 B, and larger boxes raise the per-SM ingest rate.
-__host__ __device__ constexpr int gemm_kbox(int bn) { return bn <= 128 ? 2 : 1; }
+// kbox x rows x 128 B, and larger boxes raise the per-SM ingest rate (a
+// 1600x512x512 F32 GEMM at BN=64 runs 3-4% faster with 4 than with 2).
+__host__ __device__ constexpr int gemm_kbox(int bn) { return bn <= 64 ? 4 : bn <= 128 ? 2 : 1; }
 
 // Pipeline depth for a tile width: as many stages (kbox k-blocks of A and B)
 // as fit next to the epilogue's shared memory (constants, 8 x 4 KB store

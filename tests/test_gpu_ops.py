@@ -36,6 +36,8 @@ def _rel_err(ref, got):
         (257, 512, 832, 128),
         (129, 512, 704, 64),
         (1000, 1024, 2560, 256),
+        (1600, 512, 128, 64),
+        (300, 512, 832, 64),
     ],
 )
 def test_gemm_plain(ctx_unit, M, N, K, bn):
@@ -52,7 +54,8 @@ def test_gemm_plain(ctx_unit, M, N, K, bn):
     assert rel < 1e-5 and mx < 1e-3, (rel, mx)
 
 
-def test_gemm_split_two_sources(ctx_unit):
+@pytest.mark.parametrize("bn", [64, 128])
+def test_gemm_split_two_sources(ctx_unit, bn):
     """[x_normed(512) | x_mel(80)] @ W^T without a concat buffer (skip_linear shape)."""
     dev = _dev()
     M = 333
@@ -68,7 +71,7 @@ def test_gemm_split_two_sources(ctx_unit):
     c = torch.empty(M, 512, device=dev)
     # columns 80..127 of a1 and 592..639 of w are the zero padding of the 64-column k-blocks
     ctx_unit.op_gemm(a0.data_ptr(), 512, a1.data_ptr(), 128, 512, w.data_ptr(), 640, bias.data_ptr(), c.data_ptr(), 512,
-                     M, 512, 640, 128)
+                     M, 512, 640, bn)
     ref = torch.cat([a0, a1], 1).float() @ w.float().T + bias
     rel, mx = _rel_err(ref, c)
     assert rel < 1e-5 and mx < 1e-3, (rel, mx)
