@@ -27,7 +27,8 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 f16 = one 128-byte swizzle row
 constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each owning half of the columns
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kBWarp = 2 + kEpiWarps;            // issues the B (weight) TMA loads
+constexpr int kThreads = 64 + 32 * kEpiWarps + 32;
 
 // Phase timestamps for performance investigation: compiled out unless a
 // harness defines ITTS_GEMM_TRACE and provides itts_gemm_trace_point(slot).
@@ -557,18 +558,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // The B operand is always weights, which no kernel of the stream writes: the
-  // producer starts the first tile's B loads before waiting for the previous
-  // kernel, so they overlap its tail. Stage accounting is unchanged (one
-  // arrive with the full stage byte count; the A half follows below).
+  // Two TMA issuers: warp 0 loads A and arrives on each full barrier with the
+  // whole stage byte count; warp kBWarp loads B (its bytes complete the same
+  // transaction count, possibly before the arrive). B is always weights,
+  // which no kernel of the stream writes, so the first tile's B loads start
+  // before the wait for the previous kernel and overlap its tail.
   const int num_pre = num_sb < STAGES ? num_sb : STAGES;
-  if (warp == 0 && lane == 0) {
+  if (warp == kBWarp && lane == 0) {
     const int n0 = (blockIdx.x % n_tiles) * BN;
-    for (int sbk = 0; sbk < num_pre; ++sbk) {
-      uint8_t* sb = smem + sbk * STAGE_BYTES + A_BYTES;
-      mbar_arrive_expect_tx(&full_bar[sbk], STAGE_BYTES);
-      tma_load_3d(sb, &tmB, &full_bar[sbk], 0, n0, sbk * KBOX);
-    }
+    for (int sbk = 0; sbk < num_pre; ++sbk)
+      tma_load_3d(smem + sbk * STAGE_BYTES + A_BYTES, &tmB, &full_bar[sbk], 0, n0, sbk * KBOX);
   }
   // Everything below reads or writes memory of the previous kernel in the stream.
   griddep_wait();
@@ -577,27 +576,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- TMA producer ----
+      // ---- A producer (arrives on each stage with its full byte count) ----
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * kBM;
-        const int n0 = (tile % n_tiles) * BN;
         for (int sbk = 0; sbk < num_sb; ++sbk, ++it) {
           const int kb = sbk * KBOX;  // first k-block of the stage (kb_split and kb_per_tap are multiples of KBOX)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (it == 0) GEMM_TRACE(18);
-          const bool pre = it < num_pre;  // B already in flight (issued before griddep_wait)
+          const bool pre = it < num_pre;  // a fresh stage: nothing to wait for
           if (!pre && !mbar_wait(&empty_bar[s], ph ^ 1, args.status, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
           if (it == 0) GEMM_TRACE(19);
           uint8_t* sa = smem + s * STAGE_BYTES;
-          uint8_t* sb = sa + A_BYTES;
           if (it == 0) GEMM_TRACE(8);
-          if (!pre) mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+          mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
           if (args.a_mode == kAConv5) {
             const int tap = kb / args.kb_per_tap;
             const int kc = kb - tap * args.kb_per_tap;
@@ -607,8 +604,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0, kb);
           }
-          if (!pre) tma_load_3d(sb, &tmB, &full_bar[s], 0, n0, kb);
           if (it == 0) GEMM_TRACE(2);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kBWarp) {
+    if (lane == 0) {
+      // ---- B (weight) producer: stages after the pre-issued ones ----
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int n0 = (tile % n_tiles) * BN;
+        for (int sbk = 0; sbk < num_sb; ++sbk, ++it) {
+          if (it < num_pre) continue;
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, args.status, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          tma_load_3d(smem + s * STAGE_BYTES + A_BYTES, &tmB, &full_bar[s], 0, n0, sbk * KBOX);
         }
       }
     }
@@ -678,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
-  if (lane == 0) GEMM_TRACE(warp == 0 ? 7 : 8 + warp);
+  if (lane == 0 && warp < kBWarp) GEMM_TRACE(warp == 0 ? 7 : 8 + warp);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
