@@ -155,10 +155,13 @@ double itts_cfm_step_flops(uint32_t S, uint32_t T);
  * of single kernels. They run on the context's stream and synchronise.
  *
  * itts_op_gemm: C[M,N] (f32, row stride ldc) = A[M,K] · B[N,K]^T + bias, A and B
- * f16 row-major; with a1 != NULL the first kb_split*64 columns of K come from
- * a0 and the rest from a1 (a concat without a buffer). Replaces the MPS GEMM
- * of linear_rows_f32_pass (runtime/metal_context.mm:344-381).
+ * f16 row-major; with a1 != NULL the first k0 columns of K come from a0 and
+ * the rest from a1 (a concat without a buffer). bn is the tile width (64, 80,
+ * 128 or 256); bn | ITTS_GEMM_PAIR selects the CTA-pair form (256-row tiles
+ * over two CTAs, bn 64/128/256). Replaces the MPS GEMM of
+ * linear_rows_f32_pass (runtime/metal_context.mm:344-381).
  */
+#define ITTS_GEMM_PAIR 0x10000u
 int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a1, uint32_t lda1, uint32_t k0,
                  const void* b, uint32_t ldb, const float* bias, float* c, uint32_t ldc, uint32_t M, uint32_t N,
                  uint32_t K, uint32_t bn);

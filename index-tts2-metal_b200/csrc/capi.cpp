@@ -363,7 +363,10 @@ int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a
                  uint32_t K, uint32_t bn) {
   return guarded(ctx, [&] {
     need(a0 && b && c && M > 0 && N > 0 && K > 0, "bad gemm arguments");
+    const bool pair = (bn & ITTS_GEMM_PAIR) != 0;
+    bn &= ~ITTS_GEMM_PAIR;
     need(bn == 64 || bn == 80 || bn == 128 || bn == 256, "bn must be 64, 80, 128 or 256");
+    need(!pair || bn != 80, "the CTA-pair form takes bn 64, 128 or 256");
     need(N % 16 == 0 && ldc % 4 == 0, "N must be a multiple of 16, ldc of 4");
     itts::GemmLaunch g;
     std::memset(&g, 0, sizeof(g));
@@ -379,7 +382,8 @@ int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a
     } else {
       g.tmA1 = g.tmA0;
     }
-    if (!itts::make_tmap_f16(&g.tmB, b, K, N, ldb, bn, kbox)) throw ShapeError("B layout rejected by TMA");
+    if (!itts::make_tmap_f16(&g.tmB, b, K, N, ldb, pair ? bn / 2 : bn, kbox))
+      throw ShapeError("B layout rejected by TMA");
     g.args.M = static_cast<int>(M);
     g.args.N = static_cast<int>(N);
     g.args.a_mode = a1 ? itts::kASplit : itts::kAPlain;
@@ -391,7 +395,7 @@ int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a
     g.args.ld32 = static_cast<int>(ldc);
     g.args.seq_T = 1;
     g.bn = static_cast<int>(bn);
-    g.stages = 4;
+    g.pair = pair ? 1 : 0;
     itts::Engine& e = *ctx->eng;
     e.clear_status();
     cuda_ok(itts::gemm_run(g, e.stream()), "gemm launch");
@@ -407,9 +411,13 @@ int itts_op_conv5(itts_cfm_ctx* ctx, const void* xp, uint32_t S, uint32_t T, con
     itts::GemmLaunch g;
     std::memset(&g, 0, sizeof(g));
     const uint32_t Rp = S * (T + 4);
-    if (!itts::make_tmap_f16(&g.tmA0, xp, 512, Rp, 512, 128, 2)) throw ShapeError("xp layout rejected by TMA");
+    // Tile shape and form as the engine picks them for its WaveNet convs.
+    const itts::GemmPick pk = itts::gemm_pick(static_cast<int>(Rp), static_cast<int>(N), false);
+    const uint32_t kbox = static_cast<uint32_t>(itts::gemm_kbox(pk.bn));
+    if (!itts::make_tmap_f16(&g.tmA0, xp, 512, Rp, 512, 128, kbox)) throw ShapeError("xp layout rejected by TMA");
     g.tmA1 = g.tmA0;
-    if (!itts::make_tmap_f16(&g.tmB, w, 2560, N, 2560, 128, 2)) throw ShapeError("w layout rejected by TMA");
+    if (!itts::make_tmap_f16(&g.tmB, w, 2560, N, 2560, static_cast<uint32_t>(pk.pair ? pk.bn / 2 : pk.bn), kbox))
+      throw ShapeError("w layout rejected by TMA");
     g.args.M = static_cast<int>(Rp);
     g.args.N = static_cast<int>(N);
     g.args.a_mode = itts::kAConv5;
@@ -421,8 +429,8 @@ int itts_op_conv5(itts_cfm_ctx* ctx, const void* xp, uint32_t S, uint32_t T, con
     g.args.out32 = out;
     g.args.ld32 = static_cast<int>(N);
     g.args.seq_T = static_cast<int>(T);
-    g.bn = 128;
-    g.stages = 4;
+    g.bn = pk.bn;
+    g.pair = pk.pair;
     itts::Engine& e = *ctx->eng;
     e.clear_status();
     cuda_ok(itts::gemm_run(g, e.stream()), "conv launch");

@@ -32,8 +32,14 @@ GemmLaunch make_gemm(Operand a0, Operand a1, Operand b, int M, int N, int K, int
                      int kb_per_tap, int bn, int epi) {
   GemmLaunch g;
   std::memset(&g, 0, sizeof(g));
-  if (bn == 0) bn = gemm_pick_bn(M, N, epi == kEpiSwiGLU || epi == kEpiWnGate || epi == kEpiWnResSkip);
+  int pair = 0;
+  if (bn == 0) {
+    const GemmPick pk = gemm_pick(M, N, epi == kEpiSwiGLU || epi == kEpiWnGate || epi == kEpiWnResSkip);
+    bn = pk.bn;
+    pair = pk.pair;
+  }
   const uint32_t kbox = static_cast<uint32_t>(gemm_kbox(bn));
+  const uint32_t b_rows = static_cast<uint32_t>(pair ? bn / 2 : bn);
   if (!make_tmap_f16(&g.tmA0, a0.p, a0.cols, a0.rows, a0.ld, 128, kbox))
     throw std::runtime_error("gemm: tensor map for A0 rejected");
   if (a1.p) {
@@ -42,7 +48,7 @@ GemmLaunch make_gemm(Operand a0, Operand a1, Operand b, int M, int N, int K, int
   } else {
     g.tmA1 = g.tmA0;
   }
-  if (!make_tmap_f16(&g.tmB, b.p, b.cols, b.rows, b.ld, static_cast<uint32_t>(bn), kbox))
+  if (!make_tmap_f16(&g.tmB, b.p, b.cols, b.rows, b.ld, b_rows, kbox))
     throw std::runtime_error("gemm: tensor map for B rejected");
   g.args.M = M;
   g.args.N = N;
@@ -52,7 +58,7 @@ GemmLaunch make_gemm(Operand a0, Operand a1, Operand b, int M, int N, int K, int
   g.args.kb_per_tap = kb_per_tap;
   g.args.epi = epi;
   g.bn = bn;
-  g.stages = 4;
+  g.pair = pair;
   return g;
 }
 

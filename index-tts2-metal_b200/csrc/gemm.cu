@@ -409,12 +409,15 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
     float rs = 1.0f;
     if constexpr (EPI == kEpiQKV) rs = folded_row_scale(args, m, row_ok);
     float ssg = 0.0f;  // F32 producer: sum of squares of the current 32-column group
+    if (threadIdx.x == 64 && parity == 0) GEMM_TRACE(20);
     if (!mbar_wait(acc_bar, parity, args.status, kDevTimeoutAccum)) return false;
     tc_fence_after();
+    if (threadIdx.x == 64 && parity == 0) GEMM_TRACE(21);
     uint32_t tc[16], tn[16];
     tmem_ld16_async(taddr + c_begin * 16, tc);
     tmem_wait_ld();
     reg_fence16(tc);
+    if (threadIdx.x == 64 && parity == 0) GEMM_TRACE(22);
     float vg[32];
 #pragma unroll 1
     for (int cp = c_begin; cp < c_end; cp += 2) {
@@ -477,11 +480,15 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
       int ncols = (cp + 1 < c_end) ? 32 : 16;
       if (ng + ncols > args.N) ncols = args.N > ng ? args.N - ng : 0;
       __syncwarp();
+      const bool tr = threadIdx.x == 64 && parity == 0 && cp == c_begin;
+      if (tr) GEMM_TRACE(24);
       if constexpr (EPI == kEpiF16 || EPI == kEpiQKV) {
         flush_f16(stg, static_cast<const __half*>(d0), ng, ncols, lane);
       } else if constexpr (EPI == kEpiF32) {
         flush_f32(stg, static_cast<const float*>(d0), ng, ncols, lane);
+        if (tr) GEMM_TRACE(25);
         if (args.out16) flush_f16(stg, static_cast<const __half*>(d1), ng, ncols, lane);
+        if (tr) GEMM_TRACE(26);
         if (args.nrm16) flush_f16_scaled(stg, static_cast<const __half*>(d2), ng, ncols, lane, sconst + BN + (ng - n0));
         if (args.ss_out) {
           if (row_ok) args.ss_out[static_cast<size_t>(ng >> 5) * args.ss_ld + mo] = ssg;
@@ -498,24 +505,36 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
         }
       }
       __syncwarp();
+      if (threadIdx.x == 64 && parity == 0 && cp == c_begin) GEMM_TRACE(23);
     }
   }
   return true;
 }
 
-template <int BN, int STAGES, int EPI>
+// PAIR: the CTA-pair form (cluster of 2, tcgen05 cta_group::2). A work unit
+// is a 256 x BN tile; CTA rank r of the pair holds A rows [128 r, 128 r + 128)
+// and B rows [BN/2 r, BN/2 r + BN/2) of it in its own shared memory, and its
+// 128 accumulator rows in its own TMEM. The leader (rank 0) issues the M=256
+// MMAs and every load of both CTAs completes on the leader's full barrier;
+// the leader's commits release both CTAs' stages and accumulators. Each CTA
+// ingests 16 KB + BN/2 x 128 B per k-block instead of 16 KB + BN x 128 B.
+// No TMA multicast is involved.
+template <int BN, int STAGES, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
   constexpr int KBOX = gemm_kbox(BN);      // k-blocks per stage (one TMA box per operand)
+  constexpr int BNL = PAIR ? BN / 2 : BN;  // B rows held by this CTA
   constexpr int A_KB = kBM * kBK * 2;       // one 128 x 64 k-block of A
-  constexpr int B_KB = BN * kBK * 2;        // one BN x 64 k-block of B
+  constexpr int B_KB = BNL * kBK * 2;       // one BNL x 64 k-block of B
   constexpr int A_BYTES = KBOX * A_KB;
   constexpr int B_BYTES = KBOX * B_KB;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int UNIT_M = PAIR ? 2 * kBM : kBM;  // rows of one work unit
   constexpr int ACC_STRIDE = pow2_cols(BN);  // columns between the two accumulator buffers
   constexpr uint32_t TMEM_COLS = pow2_cols(2 * ACC_STRIDE);
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+  static_assert(!PAIR || BN % 32 == 0, "pair tiles split B in halves of 16-row multiples");
   static_assert(2 * ACC_STRIDE <= 512, "two accumulator buffers must fit TMEM");
 
   extern __shared__ uint8_t smem_raw[];
@@ -530,9 +549,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   const int num_sb = (args.num_kb + KBOX - 1) / KBOX;  // stages per tile (a missing k-block reads zeros)
   const int n_tiles = (args.N + BN - 1) / BN;
-  const int num_tiles = ((args.M + kBM - 1) / kBM) * n_tiles;
+  const int num_tiles = ((args.M + UNIT_M - 1) / UNIT_M) * n_tiles;
+  // Barrier addresses in the cluster window: loads of both CTAs complete on
+  // the leader's full barriers; epilogues release the leader's accumulators.
+  auto full_addr = [&](int s) -> uint32_t { return PAIR ? mapa_shared(&full_bar[s], 0) : smem_u32(&full_bar[s]); };
 
   if (threadIdx.x == 0) GEMM_TRACE(0);
   if (warp == 0 && lane == 0) {
@@ -542,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kEpiWarps);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[a], (PAIR ? 2 : 1) * kEpiWarps);  // one arrival per epilogue warp (of both CTAs)
     }
     fence_barrier_init();
     fence_proxy_async_shared();
@@ -551,23 +576,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA signal
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Two TMA issuers: warp 0 loads A and arrives on each full barrier with the
-  // whole stage byte count; warp kBWarp loads B (its bytes complete the same
-  // transaction count, possibly before the arrive). B is always weights,
-  // which no kernel of the stream writes, so the first tile's B loads start
-  // before the wait for the previous kernel and overlap its tail.
+  // Two TMA issuers: warp 0 loads A and (in the leader) arrives on each full
+  // barrier with the whole stage byte count of the unit; warp kBWarp loads B
+  // (its bytes complete the same transaction count, possibly before the
+  // arrive). B is always weights, which no kernel of the stream writes, so the
+  // first tile's B loads start before the wait for the previous kernel and
+  // overlap its tail.
   const int num_pre = num_sb < STAGES ? num_sb : STAGES;
-  if (warp == kBWarp && lane == 0) {
-    const int n0 = (blockIdx.x % n_tiles) * BN;
-    for (int sbk = 0; sbk < num_pre; ++sbk)
-      tma_load_3d(smem + sbk * STAGE_BYTES + A_BYTES, &tmB, &full_bar[sbk], 0, n0, sbk * KBOX);
+  auto load_b = [&](int s, int n0, int kb) {
+    uint8_t* dst = smem + s * STAGE_BYTES + A_BYTES;
+    if constexpr (PAIR) {
+      tma_load_3d_pair(dst, &tmB, full_addr(s), 0, n0 + static_cast<int>(rank) * BNL, kb);
+    } else {
+      tma_load_3d(dst, &tmB, &full_bar[s], 0, n0, kb);
+    }
+  };
+  if (warp == kBWarp && lane == 0 && unit0 < num_tiles) {
+    const int n0 = (unit0 % n_tiles) * BN;
+    for (int sbk = 0; sbk < num_pre; ++sbk) load_b(sbk, n0, sbk * KBOX);
   }
   // Everything below reads or writes memory of the previous kernel in the stream.
   griddep_wait();
@@ -576,11 +618,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- A producer (arrives on each stage with its full byte count) ----
+      // ---- A producer ----
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * kBM;
+      for (int tile = unit0; tile < num_tiles && ok; tile += units) {
+        const int m0 = (tile / n_tiles) * UNIT_M + static_cast<int>(rank) * kBM;
         for (int sbk = 0; sbk < num_sb; ++sbk, ++it) {
           const int kb = sbk * KBOX;  // first k-block of the stage (kb_split and kb_per_tap are multiples of KBOX)
           const int s = it % STAGES;
@@ -594,15 +636,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (it == 0) GEMM_TRACE(19);
           uint8_t* sa = smem + s * STAGE_BYTES;
           if (it == 0) GEMM_TRACE(8);
-          mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], (PAIR ? 2 : 1) * STAGE_BYTES);
+          // Each branch names its tensor map directly (a runtime-selected
+          // pointer to a grid-constant parameter costs a local copy).
           if (args.a_mode == kAConv5) {
             const int tap = kb / args.kb_per_tap;
             const int kc = kb - tap * args.kb_per_tap;
-            tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0 + tap - 2, kc);
+            if constexpr (PAIR) {
+              tma_load_3d_pair(sa, &tmA0, full_addr(s), 0, m0 + tap - 2, kc);
+            } else {
+              tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0 + tap - 2, kc);
+            }
           } else if (args.a_mode == kASplit && kb >= args.kb_split) {
-            tma_load_3d(sa, &tmA1, &full_bar[s], 0, m0, kb - args.kb_split);
+            if constexpr (PAIR) {
+              tma_load_3d_pair(sa, &tmA1, full_addr(s), 0, m0, kb - args.kb_split);
+            } else {
+              tma_load_3d(sa, &tmA1, &full_bar[s], 0, m0, kb - args.kb_split);
+            }
           } else {
-            tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0, kb);
+            if constexpr (PAIR) {
+              tma_load_3d_pair(sa, &tmA0, full_addr(s), 0, m0, kb);
+            } else {
+              tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0, kb);
+            }
           }
           if (it == 0) GEMM_TRACE(2);
         }
@@ -614,7 +670,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- B (weight) producer: stages after the pre-issued ones ----
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit0; tile < num_tiles && ok; tile += units) {
         const int n0 = (tile % n_tiles) * BN;
         for (int sbk = 0; sbk < num_sb; ++sbk, ++it) {
           if (it < num_pre) continue;
@@ -624,18 +680,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          tma_load_3d(smem + s * STAGE_BYTES + A_BYTES, &tmB, &full_bar[s], 0, n0, sbk * KBOX);
+          load_b(s, n0, sbk * KBOX);
         }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---- MMA issuer ----
-      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
+    if (lane == 0 && rank == 0) {
+      // ---- MMA issuer (the leader of a pair) ----
+      constexpr uint32_t idesc = idesc_f16_f32(UNIT_M, BN);
       int it = 0, local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = unit0; tile < num_tiles && ok; tile += units, ++local) {
         const int a = local & 1;
         if (!mbar_wait(&acc_empty[a], ((local >> 1) & 1) ^ 1, args.status, kDevTimeoutAccum)) break;
         tc_fence_after();
@@ -655,13 +711,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < KBOX; ++j) {
 #pragma unroll
             for (int k = 0; k < kBK / 16; ++k) {
-              umma_f16_ss(d, sdesc_k_sw128(sa + j * A_KB + k * 32), sdesc_k_sw128(sb + j * B_KB + k * 32), idesc,
-                          (sbk | j | k) != 0 ? 1u : 0u);
+              const uint64_t ad = sdesc_k_sw128(sa + j * A_KB + k * 32);
+              const uint64_t bd = sdesc_k_sw128(sb + j * B_KB + k * 32);
+              const uint32_t acc = (sbk | j | k) != 0 ? 1u : 0u;
+              if constexpr (PAIR) {
+                umma_f16_ss_pair(d, ad, bd, idesc, acc);
+              } else {
+                umma_f16_ss(d, ad, bd, idesc, acc);
+              }
             }
           }
-          umma_commit(&empty_bar[s]);
+          if constexpr (PAIR) {
+            umma_commit_pair(mapa_shared(&empty_bar[s], 0));
+            umma_commit_pair(mapa_shared(&empty_bar[s], 1));
+          } else {
+            umma_commit(&empty_bar[s]);
+          }
         }
-        umma_commit(&acc_full[a]);
+        if constexpr (PAIR) {
+          umma_commit_pair(mapa_shared(&acc_full[a], 0));
+          umma_commit_pair(mapa_shared(&acc_full[a], 1));
+        } else {
+          umma_commit(&acc_full[a]);
+        }
         if (local == 0) GEMM_TRACE(4);
       }
     }
@@ -674,9 +746,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int etid = threadIdx.x - 64;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = unit0; tile < num_tiles; tile += units, ++local) {
       const int a = local & 1;
-      const int m0 = (tile / n_tiles) * kBM;
+      const int m0 = (tile / n_tiles) * UNIT_M + static_cast<int>(rank) * kBM;
       const int n0 = (tile % n_tiles) * BN;
       epi_bar();  // every epilogue thread is done with the previous tile's constants
       stage_tile_consts<BN, EPI>(args, n0, sconst, etid);
@@ -689,15 +761,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (local == 0 && warp == 2 && lane == 0) GEMM_TRACE(5);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (lane == 0) {
+        if constexpr (PAIR) {
+          mbar_arrive_cluster(mapa_shared(&acc_empty[a], 0));
+        } else {
+          mbar_arrive(&acc_empty[a]);
+        }
+      }
       if (local == 0 && warp == 2 && lane == 0) GEMM_TRACE(6);
     }
   }
-  __syncthreads();
+  if constexpr (PAIR) {
+    // Neither CTA frees its TMEM (or exits, which would drop the barriers the
+    // other one signals) before both are done.
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+  } else {
+    __syncthreads();
+  }
   if (lane == 0 && warp < kBWarp) GEMM_TRACE(warp == 0 ? 7 : 8 + warp);
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    } else {
+      tmem_dealloc(tmem_base, TMEM_COLS);
+    }
   }
 }
 
@@ -728,11 +818,11 @@ int sm_count() {
   return n;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
-  constexpr int STAGES = gemm_stages(BN);
-  auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
-  const size_t smem = gemm_smem_bytes(BN, STAGES);
+  constexpr int STAGES = gemm_stages(BN, PAIR);
+  auto kern = gemm_tc_kernel<BN, STAGES, EPI, PAIR>;
+  const size_t smem = gemm_smem_bytes(BN, STAGES, PAIR);
   // The shared-memory opt-in is set once per device for each instantiation.
   static std::atomic<uint32_t> configured{0};
   int dev = 0;
@@ -743,26 +833,34 @@ cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit);
   }
-  const int tiles = ((g.args.M + kBM - 1) / kBM) * ((g.args.N + BN - 1) / BN);
-  const int grid = tiles < sm_count() ? tiles : sm_count();
-  return launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, g.tmA0, g.tmA1, g.tmB, g.args);
+  const int unit_m = PAIR ? 2 * kBM : kBM;
+  const int units = ((g.args.M + unit_m - 1) / unit_m) * ((g.args.N + BN - 1) / BN);
+  if constexpr (PAIR) {
+    const int slots = sm_count() / 2;
+    const int clusters = units < slots ? units : slots;
+    return launch_pdl_cluster(kern, dim3(2 * clusters), dim3(kThreads), smem, stream, 2u, g.tmA0, g.tmA1, g.tmB,
+                              g.args);
+  } else {
+    const int grid = units < sm_count() ? units : sm_count();
+    return launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, g.tmA0, g.tmA1, g.tmB, g.args);
+  }
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream) {
   switch (g.args.epi) {
-    case kEpiF16: return launch_t<BN, kEpiF16>(g, stream);
-    case kEpiF32: return launch_t<BN, kEpiF32>(g, stream);
-    case kEpiQKV: return launch_t<BN, kEpiQKV>(g, stream);
-    case kEpiWnLast: return launch_t<BN, kEpiWnLast>(g, stream);
-    case kEpiConv1Res: return launch_t<BN, kEpiConv1Res>(g, stream);
+    case kEpiF16: return launch_t<BN, kEpiF16, PAIR>(g, stream);
+    case kEpiF32: return launch_t<BN, kEpiF32, PAIR>(g, stream);
+    case kEpiQKV: return launch_t<BN, kEpiQKV, PAIR>(g, stream);
+    case kEpiWnLast: return launch_t<BN, kEpiWnLast, PAIR>(g, stream);
+    case kEpiConv1Res: return launch_t<BN, kEpiConv1Res, PAIR>(g, stream);
     default: break;
   }
   if constexpr (BN % 128 == 0) {
     switch (g.args.epi) {
-      case kEpiSwiGLU: return launch_t<BN, kEpiSwiGLU>(g, stream);
-      case kEpiWnGate: return launch_t<BN, kEpiWnGate>(g, stream);
-      case kEpiWnResSkip: return launch_t<BN, kEpiWnResSkip>(g, stream);
+      case kEpiSwiGLU: return launch_t<BN, kEpiSwiGLU, PAIR>(g, stream);
+      case kEpiWnGate: return launch_t<BN, kEpiWnGate, PAIR>(g, stream);
+      case kEpiWnResSkip: return launch_t<BN, kEpiWnResSkip, PAIR>(g, stream);
       default: break;
     }
   }
@@ -771,26 +869,35 @@ cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream) {
 
 }  // namespace
 
-size_t gemm_smem_bytes(int bn, int stages) {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * gemm_kbox(bn) * (kBM * kBK * 2 + bn * kBK * 2) +
-         256 /*barriers*/ +
+size_t gemm_smem_bytes(int bn, int stages, bool pair) {
+  return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * gemm_stage_bytes(bn, pair) + 256 /*barriers*/ +
          static_cast<size_t>(tile_const_floats(bn)) * 4 + kEpiWarps * kStageFloats * 4 /*epilogue stages*/;
 }
 
-int gemm_pick_bn(int M, int N, bool paired) {
+GemmPick gemm_pick(int M, int N, bool paired_epilogue) {
+  // The CTA-pair form ingests fewer bytes per CTA but measured slower on every
+  // DiT shape (1600 x 512 x 512: 7.99 vs 7.48 us; 1600 x 1536 x 512: 10.8 vs
+  // 9.4 us; 102400 x 3072 x 512: 353 vs 337 us), so the picker keeps to the
+  // single-CTA form; the pair form stays selectable per launch.
   const int sms = sm_count();
-  const int m_tiles = (M + kBM - 1) / kBM;
-  int best = 0;
+  GemmPick best{0, 0};
   double best_cost = 0.0;
-  for (int bn : {256, 128, 64}) {
-    if (paired && bn % 128) continue;
-    if (N % bn && bn > N) continue;
-    const int tiles = m_tiles * ((N + bn - 1) / bn);
-    const int waves = (tiles + sms - 1) / sms;
-    const double cost = static_cast<double>(waves) * (bn + 64);
-    if (best == 0 || cost < best_cost - 1e-9) {
-      best = bn;
-      best_cost = cost;
+  for (int pair = 0; pair >= 0; --pair) {
+    for (int bn : {256, 128, 64}) {
+      if (paired_epilogue && bn % 128) continue;
+      if (N % bn && bn > N) continue;
+      const int unit_m = pair ? 256 : 128;
+      const int units = ((M + unit_m - 1) / unit_m) * ((N + bn - 1) / bn);
+      const int slots = pair ? sms / 2 : sms;
+      const int waves = (units + slots - 1) / slots;
+      // Per-tile cost in units that track the measured tile times (A share 64
+      // plus the B rows a CTA holds): e.g. 1600 x 3072 at bn 128 (3 waves)
+      // beats bn 256 (2 waves).
+      const double cost = static_cast<double>(waves) * ((pair ? bn / 2 : bn) + 64);
+      if (best.bn == 0 || cost < best_cost - 1e-9) {
+        best = GemmPick{bn, pair};
+        best_cost = cost;
+      }
     }
   }
   return best;
@@ -815,11 +922,19 @@ bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t ro
 
 cudaError_t gemm_run(const GemmLaunch& g, cudaStream_t stream) {
   if (g.args.M <= 0 || g.args.N <= 0 || g.args.num_kb <= 0) return cudaErrorInvalidValue;
+  if (g.pair) {
+    switch (g.bn) {
+      case 64: return launch_epi<64, true>(g, stream);
+      case 128: return launch_epi<128, true>(g, stream);
+      case 256: return launch_epi<256, true>(g, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (g.bn) {
-    case 64: return launch_epi<64>(g, stream);
-    case 80: return launch_epi<80>(g, stream);
-    case 128: return launch_epi<128>(g, stream);
-    case 256: return launch_epi<256>(g, stream);
+    case 64: return launch_epi<64, false>(g, stream);
+    case 80: return launch_epi<80, false>(g, stream);
+    case 128: return launch_epi<128, false>(g, stream);
+    case 256: return launch_epi<256, false>(g, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -79,10 +79,10 @@ struct GemmArgs {
 struct GemmLaunch {
   CUtensorMap tmA0;
   CUtensorMap tmA1;
-  CUtensorMap tmB;
+  CUtensorMap tmB;  // box rows: bn, or bn / 2 for the CTA-pair form
   GemmArgs args;
   int bn;
-  int stages;
+  int pair;  // 1: CTA-pair form (clusters of 2, cta_group::2 MMA over 256-row tiles)
 };
 
 // k-blocks (64 columns each) fetched per TMA instruction: one TMA box moves
@@ -90,13 +90,19 @@ struct GemmLaunch {
 // 1600x512x512 F32 GEMM at BN=64 runs 3-4% faster with 4 than with 2).
 __host__ __device__ constexpr int gemm_kbox(int bn) { return bn <= 64 ? 4 : bn <= 128 ? 2 : 1; }
 
-// Pipeline depth for a tile width: as many stages (kbox k-blocks of A and B)
-// as fit next to the epilogue's shared memory (constants, 8 x 4 KB store
-// stages, barriers) in the 227 KB a CTA may use.
-__host__ __device__ constexpr int gemm_stages(int bn) {
-  return ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / (gemm_kbox(bn) * (128 * 64 * 2 + bn * 64 * 2))) > 8
+// Bytes of one pipeline stage of a CTA: kbox k-blocks of A (128 rows) and of
+// B (bn rows, or bn / 2 in the CTA-pair form).
+__host__ __device__ constexpr int gemm_stage_bytes(int bn, bool pair) {
+  return gemm_kbox(bn) * (128 * 64 * 2 + (pair ? bn / 2 : bn) * 64 * 2);
+}
+
+// Pipeline depth for a tile width: as many stages as fit next to the
+// epilogue's shared memory (constants, 8 x 4 KB store stages, barriers) in the
+// 227 KB a CTA may use, at most 8.
+__host__ __device__ constexpr int gemm_stages(int bn, bool pair) {
+  return ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / gemm_stage_bytes(bn, pair)) > 8
              ? 8
-             : ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / (gemm_kbox(bn) * (128 * 64 * 2 + bn * 64 * 2)));
+             : ((232448 - 1024 - 256 - 8 * bn - 32768 - 512) / gemm_stage_bytes(bn, pair));
 }
 
 // Host helpers (gemm.cu).
@@ -106,9 +112,15 @@ __host__ __device__ constexpr int gemm_stages(int bn) {
 bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
                    uint32_t box_rows, uint32_t kbox);
 cudaError_t gemm_run(const GemmLaunch& g, cudaStream_t stream);
-size_t gemm_smem_bytes(int bn, int stages);
+size_t gemm_smem_bytes(int bn, int stages, bool pair);
 // Tile width (64, 128 or 256; paired epilogues need a multiple of 128) that
-// minimises waves x per-tile cost for an M x N output on this GPU.
-int gemm_pick_bn(int M, int N, bool paired);
+// minimises waves x per-tile cost for an M x N output on this GPU; the
+// per-tile cost is dominated by the bytes a CTA ingests per k-block (16 KB of
+// A plus 128 B per B row it holds). Always the single-CTA form (see gemm.cu).
+struct GemmPick {
+  int bn;
+  int pair;
+};
+GemmPick gemm_pick(int M, int N, bool paired_epilogue);
 
 }  // namespace itts

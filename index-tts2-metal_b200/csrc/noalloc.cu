@@ -143,7 +143,7 @@ extern "C" int itts_op_conv5_noalloc(const void* x, uint32_t S, uint32_t T, cons
   g.args.seq_T = static_cast<int>(T);
   g.args.status = status;
   g.bn = 128;
-  g.stages = 4;
+  g.pair = 0;
 
   const unsigned blocks = static_cast<unsigned>((rows + 3) / 4);
   pad_into_scratch<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<int>(S), static_cast<int>(T));

@@ -22,6 +22,7 @@ ITTS_ETIMEOUT = -4
 ITTS_ECAP = -5
 ITTS_ENODEV = -6
 ITTS_CREATE_VERIFY_SHA256 = 0x1
+ITTS_GEMM_PAIR = 0x10000
 
 EXPORTED = [
     "itts_cfm_create", "itts_cfm_create_ex", "itts_cfm_destroy", "itts_cfm_last_error", "itts_cfm_create_error",

@@ -54,7 +54,37 @@ def test_gemm_plain(ctx_unit, M, N, K, bn):
     assert rel < 1e-5 and mx < 1e-3, (rel, mx)
 
 
-@pytest.mark.parametrize("bn", [64, 128])
+@pytest.mark.parametrize(
+    "M,N,K,bn",
+    [
+        (128, 512, 512, 64),
+        (1600, 512, 512, 64),
+        (300, 1536, 512, 256),
+        (1600, 3072, 512, 128),
+        (257, 512, 832, 128),
+        (129, 512, 704, 64),
+        (1000, 1024, 2560, 256),
+        (4096, 512, 1536, 256),
+    ],
+)
+def test_gemm_pair(ctx_unit, M, N, K, bn):
+    """CTA-pair form (clusters of 2, cta_group::2 MMA over 256-row tiles)."""
+    import itts_cfm
+
+    dev = _dev()
+    g = torch.Generator(device="cpu").manual_seed(M * 11 + N + K)
+    a = torch.randn(M, K, generator=g).half().to(dev)
+    b = (torch.randn(N, K, generator=g) / K**0.5).half().to(dev)
+    bias = torch.randn(N, generator=g).float().to(dev)
+    c = torch.full((M, N), float("nan"), device=dev)
+    ctx_unit.op_gemm(a.data_ptr(), K, None, 0, 0, b.data_ptr(), K, bias.data_ptr(), c.data_ptr(), N, M, N, K,
+                     bn | itts_cfm.ITTS_GEMM_PAIR)
+    ref = a.float() @ b.float().T + bias
+    rel, mx = _rel_err(ref, c)
+    assert rel < 1e-5 and mx < 1e-3, (rel, mx)
+
+
+@pytest.mark.parametrize("bn", [64, 128, 128 | 0x10000])
 def test_gemm_split_two_sources(ctx_unit, bn):
     """[x_normed(512) | x_mel(80)] @ W^T without a concat buffer (skip_linear shape)."""
     dev = _dev()
