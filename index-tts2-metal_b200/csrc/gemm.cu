@@ -883,7 +883,8 @@ GemmPick gemm_pick(int M, int N, bool paired_epilogue) {
   GemmPick best{0, 0};
   double best_cost = 0.0;
   for (int pair = 0; pair >= 0; --pair) {
-    for (int bn : {256, 128, 64}) {
+    for (int bn : {256, 192, 128, 64}) {
+      if (bn == 192 && (pair || paired_epilogue)) continue;
       if (paired_epilogue && bn % 128) continue;
       if (N % bn && bn > N) continue;
       const int unit_m = pair ? 256 : 128;
@@ -934,6 +935,7 @@ cudaError_t gemm_run(const GemmLaunch& g, cudaStream_t stream) {
     case 64: return launch_epi<64, false>(g, stream);
     case 80: return launch_epi<80, false>(g, stream);
     case 128: return launch_epi<128, false>(g, stream);
+    case 192: return launch_epi<192, false>(g, stream);
     case 256: return launch_epi<256, false>(g, stream);
     default: return cudaErrorInvalidValue;
   }

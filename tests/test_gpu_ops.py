@@ -38,6 +38,8 @@ def _rel_err(ref, got):
         (1000, 1024, 2560, 256),
         (1600, 512, 128, 64),
         (300, 512, 832, 64),
+        (1600, 1536, 512, 192),
+        (77, 1536, 512, 192),
     ],
 )
 def test_gemm_plain(ctx_unit, M, N, K, bn):
