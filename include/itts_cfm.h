@@ -157,7 +157,7 @@ double itts_cfm_step_flops(uint32_t S, uint32_t T);
  * itts_op_gemm: C[M,N] (f32, row stride ldc) = A[M,K] · B[N,K]^T + bias, A and B
  * f16 row-major; with a1 != NULL the first k0 columns of K come from a0 and
  * the rest from a1 (a concat without a buffer). bn is the tile width (64, 80,
- * 128 or 256); bn | ITTS_GEMM_PAIR selects the CTA-pair form (256-row tiles
+ * 128, 192 or 256); bn | ITTS_GEMM_PAIR selects the CTA-pair form (256-row tiles
  * over two CTAs, bn 64/128/256). Replaces the MPS GEMM of
  * linear_rows_f32_pass (runtime/metal_context.mm:344-381).
  */

@@ -366,8 +366,7 @@ int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a
     const bool pair = (bn & ITTS_GEMM_PAIR) != 0;
     bn &= ~ITTS_GEMM_PAIR;
     need(bn == 64 || bn == 80 || bn == 128 || bn == 192 || bn == 256, "bn must be 64, 80, 128, 192 or 256");
-    need(!pair || bn != 192, "the CTA-pair form takes bn 64, 128 or 256");
-    need(!pair || bn != 80, "the CTA-pair form takes bn 64, 128 or 256");
+    need(!pair || bn == 64 || bn == 128 || bn == 256, "the CTA-pair form takes bn 64, 128 or 256");
     need(N % 16 == 0 && ldc % 4 == 0, "N must be a multiple of 16, ldc of 4");
     itts::GemmLaunch g;
     std::memset(&g, 0, sizeof(g));

@@ -235,7 +235,7 @@ Work* Engine::work(int B, int T, int branches) {
     w->x16 = carve<__half>(cur, R * 512);
     for (int i = 0; i < 6; ++i) w->skip16[i] = carve<__half>(cur, R * 512);
     w->xn16 = carve<__half>(cur, R * 512);
-    w->ss = carve<float>(cur, R * 16);
+    w->ss = carve<float>(cur, R * 32);
     w->qkv16 = carve<__half>(cur, R * 1536);
     w->attn16 = carve<__half>(cur, R * 512);
     w->h = carve<float>(cur, R * 512);
@@ -347,7 +347,7 @@ void Engine::build_work_launches(Work* w) {
   };
   auto consumer = [&](GemmLaunch& g) {
     g.args.ss_in = w->ss;
-    g.args.ss_parts = 16;
+    g.args.ss_parts = 32;
     g.args.ss_n = 512;
     g.args.ss_ld = R;
   };

@@ -408,7 +408,6 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
     if constexpr (kPre2) fetch(c_begin + 1, x0_nxt, x1_nxt);
     float rs = 1.0f;
     if constexpr (EPI == kEpiQKV) rs = folded_row_scale(args, m, row_ok);
-    float ssg = 0.0f;  // F32 producer: sum of squares of the current 32-column group
     if (threadIdx.x == 64 && parity == 0) GEMM_TRACE(20);
     if (!mbar_wait(acc_bar, parity, args.status, kDevTimeoutAccum)) return false;
     tc_fence_after();
@@ -440,9 +439,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
 #pragma unroll
               for (int e = 0; e < 16; ++e) v[e] += x0_cur[e];
             }
-            if (args.ss_out) {
+            if (args.ss_out && row_ok && n < args.N) {
+              float sc = 0.0f;
 #pragma unroll
-              for (int e = 0; e < 16; ++e) ssg = fmaf(v[e], v[e], ssg);
+              for (int e = 0; e < 16; ++e) sc = fmaf(v[e], v[e], sc);
+              args.ss_out[static_cast<size_t>(n >> 4) * args.ss_ld + mo] = sc;
             }
           } else if constexpr (EPI == kEpiQKV) {
             if (n < 1024) {
@@ -490,16 +491,13 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
         if (args.out16) flush_f16(stg, static_cast<const __half*>(d1), ng, ncols, lane);
         if (tr) GEMM_TRACE(26);
         if (args.nrm16) flush_f16_scaled(stg, static_cast<const __half*>(d2), ng, ncols, lane, sconst + BN + (ng - n0));
-        if (args.ss_out) {
-          if (row_ok) args.ss_out[static_cast<size_t>(ng >> 5) * args.ss_ld + mo] = ssg;
-          ssg = 0.0f;
-        }
       } else if constexpr (EPI == kEpiWnLast) {
         flush_f32(stg, static_cast<const float*>(d0), ng, ncols, lane);
       } else if constexpr (EPI == kEpiConv1Res) {
         if (ng < 512) {
           flush_f16(stg, static_cast<const __half*>(d0), ng, ncols, lane);
           if (row_ok && ncols == 32) write_halos<32>(args.wn_xp, s, t, T, ng, vg);
+          if (row_ok && ncols == 16) write_halos<16>(args.wn_xp, s, t, T, ng, vg);
         } else {
           flush_f32(stg, static_cast<const float*>(d1), ng - 512, ncols, lane);
         }

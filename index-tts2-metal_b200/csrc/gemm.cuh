@@ -59,8 +59,8 @@ struct GemmArgs {
   // AdaRMSNorm folded across a producer/consumer GEMM pair:
   //   y = w*g*(x*inv) + b,  inv = 1/sqrt(mean_k x^2 + 1e-5)
   //   y . W^T = inv * ((x*w*g) . W^T) + (b . W^T)
-  // Producer (kEpiF32): nrm16 = f16(v * nrm_w * nrm_g) and, per 32-column
-  // group p of the output, ss_out[p * ss_ld + row] = sum of v^2 over the group
+  // Producer (kEpiF32): nrm16 = f16(v * nrm_w * nrm_g) and, per 16-column
+  // chunk p of the output, ss_out[p * ss_ld + row] = sum of v^2 over the chunk
   // (the partial count never depends on the tile width).
   // Consumer (kEpiQKV, kEpiSwiGLU): the accumulator of row m is multiplied by
   // 1/sqrt(sum_p ss_in[p * ss_ld + m] / ss_n + 1e-5) before `bias` (which then
