@@ -151,6 +151,17 @@ int itts_cfm_profile_step(itts_cfm_ctx* ctx, int reps, itts_kernel_stat* out, in
 double itts_cfm_step_flops(uint32_t S, uint32_t T);
 
 /*
+ * Failure-detection self-test: launches one kernel that waits on a barrier
+ * nothing completes, through the bounded wait every kernel of this library
+ * uses, with a budget of `budget_cycles` SM clock cycles (1e3..1e9). Returns
+ * ITTS_ETIMEOUT once the kernel has given up and reported it through the
+ * context's device status word, exactly as a stalled production kernel would;
+ * the context stays usable afterwards. No counterpart in the reference (its
+ * Metal kernels have no device-side wait).
+ */
+int itts_cfm_selftest_timeout(itts_cfm_ctx* ctx, uint64_t budget_cycles);
+
+/*
  * Kernel-level entry points on caller-owned DEVICE pointers, for parity tests
  * of single kernels. They run on the context's stream and synchronise.
  *

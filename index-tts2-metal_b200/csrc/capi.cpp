@@ -358,6 +358,19 @@ int itts_cfm_profile_step(itts_cfm_ctx* ctx, int reps, itts_kernel_stat* out, in
   });
 }
 
+int itts_cfm_selftest_timeout(itts_cfm_ctx* ctx, uint64_t budget_cycles) {
+  return guarded(ctx, [&] {
+    need(budget_cycles >= 1000 && budget_cycles <= 1000000000ull, "budget_cycles must be within 1e3..1e9");
+    itts::Engine& e = *ctx->eng;
+    e.clear_status();
+    cuda_ok(itts::bounded_wait_probe_run(e.status_ptr(), static_cast<long long>(budget_cycles), e.stream()),
+            "self-test launch");
+    cuda_ok(cudaStreamSynchronize(e.stream()), "self-test sync");
+    check_status(e);
+    throw std::runtime_error("self-test: the bounded wait did not report its expiry");
+  });
+}
+
 int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a1, uint32_t lda1, uint32_t k0,
                  const void* b, uint32_t ldb, const float* bias, float* c, uint32_t ldc, uint32_t M, uint32_t N,
                  uint32_t K, uint32_t bn) {

@@ -241,6 +241,21 @@ inline unsigned grid_for(size_t n, int threads) {
 
 }  // namespace
 
+// Failure-detection self-test: one thread waits on an mbarrier that nothing
+// will complete, through the same bounded wait every kernel here uses, and
+// gives up after `budget` cycles with kDevTimeoutProbe in the status word.
+__global__ void bounded_wait_probe_kernel(unsigned int* status, long long budget) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  mbar_wait_for(&bar, 0, status, kDevTimeoutProbe, budget);
+}
+
+cudaError_t bounded_wait_probe_run(unsigned int* status, long long budget_cycles, cudaStream_t st) {
+  bounded_wait_probe_kernel<<<1, 1, 0, st>>>(status, budget_cycles);
+  return cudaGetLastError();
+}
+
 cudaError_t adarms_run(const float* x, int R, const float* wb, const float* gamma, __half* out, cudaStream_t st) {
   return launch_pdl(adarms_kernel, dim3((R + 7) / 8), dim3(256), 0, st, x, R, wb, gamma, out);
 }

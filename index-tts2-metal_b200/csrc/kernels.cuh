@@ -57,6 +57,9 @@ cudaError_t gemv_f32w_run(const float* W, const float* bias, const float* x, int
 // Sinusoidal timestep embedding: emb[b] = [cos(scale*t_b*freqs) | sin(...)], 128 freqs.
 cudaError_t tembed_run(const float* t, const float* freqs, float* emb, int nb, float scale, cudaStream_t st);
 
+// Failure-detection self-test kernel (see bounded_wait_probe_kernel).
+cudaError_t bounded_wait_probe_run(unsigned int* status, long long budget_cycles, cudaStream_t st);
+
 // SiLU in place on fp32 (table build).
 cudaError_t silu_run(float* x, size_t n, cudaStream_t st);
 

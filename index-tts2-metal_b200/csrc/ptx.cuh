@@ -20,6 +20,7 @@ enum DevStatusCode : unsigned int {
   kDevTimeoutFull = 1,   // MMA warp waited too long for a TMA stage
   kDevTimeoutEmpty = 2,  // producer waited too long for a free stage
   kDevTimeoutAccum = 3,  // epilogue waited too long for the accumulator
+  kDevTimeoutProbe = 6,  // the bounded-wait self-test gave up (as it should)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -56,19 +57,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait on an mbarrier phase. Returns false (and records `code`) when
-// the budget runs out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status,
-                                          unsigned int code) {
+// `budget` cycles run out.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, unsigned int* status,
+                                              unsigned int code, long long budget) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long start = clock64();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
-    if (clock64() - start > kWaitBudgetCycles) {
+    if (clock64() - start > budget) {
       if (status) atomicCAS(status, 0u, code);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status,
+                                          unsigned int code) {
+  return mbar_wait_for(bar, parity, status, code, kWaitBudgetCycles);
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {

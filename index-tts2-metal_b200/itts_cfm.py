@@ -29,7 +29,7 @@ EXPORTED = [
     "itts_cfm_strerror", "itts_cfm_run", "itts_cfm_run_batch", "itts_cfm_bucket_len", "itts_cfm_run_padded",
     "itts_cfm_estimator", "itts_cfm_stage_padded", "itts_cfm_launch", "itts_cfm_sync", "itts_cfm_fetch",
     "itts_cfm_stream", "itts_cfm_launch_kernels", "itts_cfm_profile_step", "itts_cfm_step_flops", "itts_op_gemm", "itts_op_conv5",
-    "itts_op_attention", "itts_op_adarms", "itts_op_conv5_noalloc",
+    "itts_op_attention", "itts_op_adarms", "itts_op_conv5_noalloc", "itts_cfm_selftest_timeout",
 ]
 
 
@@ -87,6 +87,7 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_op_attention": (i32, [vp, vp, vp, vp, u32, u32]),
         "itts_op_adarms": (i32, [vp, vp, u32, vp, vp, vp]),
         "itts_op_conv5_noalloc": (i32, [vp, u32, u32, vp, vp, vp, u32, vp, C.c_char_p, u32]),
+        "itts_cfm_selftest_timeout": (i32, [vp, C.c_uint64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -225,6 +226,11 @@ class Context:
     # ---- kernel-level (device pointers as ints) ----
     def op_gemm(self, a0, lda0, a1, lda1, k0, b, ldb, bias, c, ldc, M, N, K, bn=128) -> None:
         self._check(self.lib.itts_op_gemm(self.h, a0, lda0, a1, lda1, k0, b, ldb, bias, c, ldc, M, N, K, bn))
+
+    def selftest_timeout(self, budget_cycles: int) -> tuple[int, str]:
+        """Run the bounded-wait self-test; returns (status code, message)."""
+        rc = self.lib.itts_cfm_selftest_timeout(self.h, int(budget_cycles))
+        return rc, self.lib.itts_cfm_last_error(self.h).decode()
 
     def op_conv5(self, xp, S, T, w, bias, out, N) -> None:
         self._check(self.lib.itts_op_conv5(self.h, xp, S, T, w, bias, out, N))
