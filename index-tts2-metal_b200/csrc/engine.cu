@@ -235,7 +235,7 @@ Work* Engine::work(int B, int T, int branches) {
     w->x16 = carve<__half>(cur, R * 512);
     for (int i = 0; i < 6; ++i) w->skip16[i] = carve<__half>(cur, R * 512);
     w->xn16 = carve<__half>(cur, R * 512);
-    w->ss = carve<float>(cur, R * 32);
+    w->ss = carve<float>(cur, R * 16);
     w->qkv16 = carve<__half>(cur, R * 1536);
     w->attn16 = carve<__half>(cur, R * 512);
     w->h = carve<float>(cur, R * 512);
@@ -259,12 +259,13 @@ Work* Engine::work(int B, int T, int branches) {
   layout(static_cast<uint8_t*>(w->arena));
   if (!make_attn_tmap(&w->tm_attn, w->qkv16, w->R)) throw std::runtime_error("cuda: attention tensor map rejected");
   // RoPE table with the reference's float arithmetic (apply_rope_inplace,
-  // runtime/impl/tokenizer_tests.cpp:4266-4281).
+  // runtime/impl/tokenizer_tests.cpp:4266-4281), pair-major [32][T] so that
+  // the 32 rows of an epilogue warp read consecutive entries.
   std::vector<float2> rope(static_cast<size_t>(T) * 32);
   for (int t = 0; t < T; ++t) {
     for (int p = 0; p < 32; ++p) {
       const float theta = static_cast<float>(t) / std::pow(10000.0f, static_cast<float>(p * 2) / 64.0f);
-      rope[static_cast<size_t>(t) * 32 + p] = make_float2(std::cos(theta), std::sin(theta));
+      rope[static_cast<size_t>(p) * T + t] = make_float2(std::cos(theta), std::sin(theta));
     }
   }
   check(cudaMemcpy(w->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope upload");
@@ -344,10 +345,11 @@ void Engine::build_work_launches(Work* w) {
     g.args.nrm_g = gamma;
     g.args.ss_out = w->ss;
     g.args.ss_ld = R;
+    if (g.bn % 32 != 0) throw std::runtime_error("folded-norm producer needs a tile width that is a multiple of 32");
   };
   auto consumer = [&](GemmLaunch& g) {
     g.args.ss_in = w->ss;
-    g.args.ss_parts = 32;
+    g.args.ss_parts = 16;
     g.args.ss_n = 512;
     g.args.ss_ld = R;
   };
@@ -475,10 +477,33 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
                           std::vector<KernelTiming>* prof) {
   const double R = w->R, T = w->T, S = w->S;
   Prof P{prof, stream_, {}, {}};
+  // Compulsory HBM bytes of one GEMM launch: A once, the weights once, and
+  // what its epilogue must read and write (f16 = 2 B, f32 = 4 B per element).
+  auto gemm_bytes = [&](const GemmLaunch& g, double rows, double K) {
+    const GemmArgs& a = g.args;
+    const double N = a.N;
+    // (the implicit k=5 conv reads each A row once from HBM, five times from L2)
+    double b = rows * (a.a_mode == kAConv5 ? K / 5.0 : K) * 2.0 + N * K * 2.0;
+    switch (a.epi) {
+      case kEpiF16: b += rows * N * 2.0; break;
+      case kEpiQKV: b += rows * N * 2.0; break;
+      case kEpiSwiGLU: case kEpiWnGate: b += rows * N; break;
+      case kEpiF32:
+        b += rows * N * 4.0 * (a.resid32 ? 2.0 : 1.0);
+        if (a.out16) b += rows * N * 2.0;
+        if (a.nrm16) b += rows * N * 2.0 + rows * (N / 16.0) * 4.0;
+        break;
+      case kEpiWnResSkip: b += rows * 512.0 * (2.0 * 2.0 + (a.wn_first ? 1.0 : 2.0) * 4.0); break;
+      case kEpiWnLast: b += rows * N * 4.0 * 3.0; break;
+      case kEpiConv1Res: b += rows * 512.0 * (2.0 + 4.0); break;
+      default: break;
+    }
+    return b;
+  };
   auto G = [&](const char* name, const GemmLaunch& g, double K) {
     const double rows = g.args.a_mode == kAConv5 ? R : static_cast<double>(g.args.M);
     const double flops = 2.0 * rows * g.args.N * K;
-    P.run(name, flops, 0.0, [&] { check(gemm_run(g, stream_), name); });
+    P.run(name, flops, prof ? gemm_bytes(g, rows, K) : 0.0, [&] { check(gemm_run(g, stream_), name); });
   };
   // Launch copies carrying this step's folded-norm constants (nrm_w: the
   // norm's w row; bias of QKV / w13: the norm's b through the weights).
@@ -490,32 +515,32 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
     g.args.bias = b;
     return g;
   };
-  G("gemm", with_w(w->g_merge, tab + kTabAttn), 80);
+  G("gemm.merge", with_w(w->g_merge, tab + kTabAttn), 80);
   for (int l = 0; l < kLayers; ++l) {
-    if (l > kLayers / 2) G("gemm", with_w(w->g_skip[l], tab + kTabAttn + l * 1024), 1024);
-    G("gemm", with_bias(w->g_qkv[l], tab + kTabQkvC + l * 1536), 512);
+    if (l > kLayers / 2) G("gemm.skip_in", with_w(w->g_skip[l], tab + kTabAttn + l * 1024), 1024);
+    G("gemm.qkv", with_bias(w->g_qkv[l], tab + kTabQkvC + l * 1536), 512);
     P.run("attention", S * 4.0 * T * T * 512.0, R * (1536 + 512) * 2.0,
           [&] { check(attention_tc_run(w->tm_attn, w->mask, w->attn16, w->S, w->T, d_status_, stream_), "attention"); });
-    G("gemm", with_w(w->g_wo[l], tab + kTabFfn + l * 1024), 512);
-    G("gemm", with_bias(w->g_w13[l], tab + kTabW13C + l * 3072), 512);
-    if (l + 1 <= kLayers / 2) G("gemm", with_w(w->g_w2[l], tab + kTabAttn + (l + 1) * 1024), 1536);
-    else G("gemm", w->g_w2[l], 1536);
+    G("gemm.wo", with_w(w->g_wo[l], tab + kTabFfn + l * 1024), 512);
+    G("gemm.w13", with_bias(w->g_w13[l], tab + kTabW13C + l * 3072), 512);
+    if (l + 1 <= kLayers / 2) G("gemm.w2", with_w(w->g_w2[l], tab + kTabAttn + (l + 1) * 1024), 1536);
+    else G("gemm.w2", w->g_w2[l], 1536);
   }
   P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
     check(adarms_run(w->xres, w->R, tab + kTabNorm, w_.g_norm, w->xn16, stream_), "adarms");
   });
-  G("gemm", w->g_sl, 592);
-  G("gemm", w->g_c1res, 512);
+  G("gemm.skip_linear", w->g_sl, 592);
+  G("gemm.conv1_res", w->g_c1res, 512);
   for (int l = 0; l < kWnLayers; ++l) {
     GemmLaunch gi = w->g_in[l];
     gi.args.wn_cond = tab + kTabWn + l * 1024;
-    G("gemm", gi, 2560);
-    G("gemm", w->g_rs[l], 512);
+    G("gemm.wn_in_k5", gi, 2560);
+    G("gemm.wn_res_skip", w->g_rs[l], 512);
   }
   P.run("adaln", 0.0, R * 512 * (4 + 2),
         [&] { check(adaln_run(w->fin, w->R, tab + kTabFinal, w->fn16, stream_), "adaln"); });
-  G("gemm", w->g_fin, 512);
-  G("gemm", w->g_c2, 512);
+  G("gemm.final_linear", w->g_fin, 512);
+  G("gemm.conv2", w->g_c2, 512);
   if (do_update) {
     P.run("euler", 0.0, static_cast<double>(w->B) * T * 80 * 4.0 * (w->br + 2), [&] {
       check(euler_run(w->X, w->vel, w->XD, w->plen, w->B, w->T, w->br, dt, cfg, stream_), "euler");

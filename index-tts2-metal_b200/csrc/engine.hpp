@@ -50,7 +50,7 @@ struct Work {
   __half* x16 = nullptr;
   __half* skip16[6] = {};
   __half* xn16 = nullptr;  // normalised GEMM operand (folded AdaRMS: x * w * g)
-  float* ss = nullptr;     // [32][R] per-16-column partial sums of squares of the normalised x
+  float* ss = nullptr;     // [16][R] per-32-column partial sums of squares of the normalised x
   __half* qkv16 = nullptr;
   __half* attn16 = nullptr;
   float* h = nullptr;

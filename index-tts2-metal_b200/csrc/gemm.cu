@@ -60,35 +60,48 @@ __device__ __forceinline__ void u2f16(const uint32_t (&r)[16], float* v) {
 // Epilogue helpers: the 256 epilogue threads (warps 2..9) share a named barrier.
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
 
-// Per-tile column constants staged in shared memory before the accumulator is
-// ready: bias[n0 .. n0+BN) and, for the WaveNet gate, the global condition of
-// the tile's channels (a-part then b-part, BN/2 each); for a folded-norm
-// producer the column scale nrm_w * nrm_g.
+// Per-tile column constants, 2*BN floats staged in shared memory: [0, BN) the
+// bias of columns n0 .. n0+BN; [BN, 2 BN) for a folded-norm producer the
+// column scale nrm_w * nrm_g, for the WaveNet gate the global condition of
+// the tile's channels (a-part then b-part, BN/2 each), else 0. Entry i
+// belongs to epilogue thread i mod 256; each thread loads its entries of the
+// next tile into registers while the current tile is processed, so the
+// global-load latency stays off the per-tile critical path.
+__host__ __device__ constexpr int tile_const_floats(int bn) { return 2 * bn; }
+__host__ __device__ constexpr int consts_per_thread(int bn) { return (2 * bn + 32 * kEpiWarps - 1) / (32 * kEpiWarps); }
+
 template <int BN, int EPI>
-__device__ __forceinline__ void stage_tile_consts(const GemmArgs& args, int n0, float* sconst, int etid) {
-  for (int i = etid; i < BN; i += 128) {
-    const int n = n0 + i;
-    sconst[i] = (args.bias && n < args.N) ? args.bias[n] : 0.0f;
-  }
-  if constexpr (EPI == kEpiF32) {
-    if (args.nrm16) {
-      for (int i = etid; i < BN; i += 128) {
-        const int n = n0 + i;
-        sconst[BN + i] = n < args.N ? args.nrm_w[n] * args.nrm_g[n] : 0.0f;
+__device__ __forceinline__ void load_tile_consts(const GemmArgs& args, int n0, int etid,
+                                                 float (&r)[consts_per_thread(BN)]) {
+#pragma unroll
+  for (int k = 0; k < consts_per_thread(BN); ++k) {
+    const int i = etid + k * 32 * kEpiWarps;
+    float x = 0.0f;
+    if (i < BN) {
+      const int n = n0 + i;
+      if (args.bias && n < args.N) x = args.bias[n];
+    } else if (i < 2 * BN) {
+      const int j = i - BN;
+      if constexpr (EPI == kEpiF32) {
+        const int n = n0 + j;
+        if (args.nrm16 && n < args.N) x = args.nrm_w[n] * args.nrm_g[n];
+      } else if constexpr (EPI == kEpiWnGate) {
+        const int ch = (n0 >> 1) + (j < BN / 2 ? j : j - BN / 2);
+        if (2 * ch < args.N) x = args.wn_cond[(j < BN / 2 ? 0 : 512) + ch];
       }
     }
-  }
-  if constexpr (EPI == kEpiWnGate) {
-    for (int i = etid; i < BN / 2; i += 128) {
-      const int ch = (n0 >> 1) + i;
-      const bool in = 2 * ch < args.N;
-      sconst[BN + i] = in ? args.wn_cond[ch] : 0.0f;
-      sconst[BN + BN / 2 + i] = in ? args.wn_cond[512 + ch] : 0.0f;
-    }
+    r[k] = x;
   }
 }
 
-__host__ __device__ constexpr int tile_const_floats(int bn) { return 2 * bn; }
+template <int BN>
+__device__ __forceinline__ void store_tile_consts(float* sconst, int etid, const float (&r)[consts_per_thread(BN)]) {
+#pragma unroll
+  for (int k = 0; k < consts_per_thread(BN); ++k) {
+    const int i = etid + k * 32 * kEpiWarps;
+    if (i < 2 * BN) sconst[i] = r[k];
+  }
+}
 
 // ---- coalesced epilogue stores through a per-warp shared-memory stage ----
 // Each epilogue warp owns 32 accumulator rows (one per lane). Values of a
@@ -177,10 +190,22 @@ __device__ __forceinline__ void flush_f16_scaled(const float4* stg, const __half
 
 // Row scale of a folded-norm consumer: 1/sqrt(mean of squares + 1e-5) from the
 // producer's per-group partial sums (summed in group order), or 1.
+// The 16 partials of the usual 512-wide norm are all loaded before the first
+// add (one round of load latency instead of 16), then summed in group order.
 __device__ __forceinline__ float folded_row_scale(const GemmArgs& args, int m, bool row_ok) {
   if (!args.ss_in || !row_ok) return 1.0f;
+  const float* src = args.ss_in + m;
+  const size_t ld = static_cast<size_t>(args.ss_ld);
   float t = 0.0f;
-  for (int p = 0; p < args.ss_parts; ++p) t += args.ss_in[static_cast<size_t>(p) * args.ss_ld + m];
+  if (args.ss_parts == 16) {
+    float v[16];
+#pragma unroll
+    for (int p = 0; p < 16; ++p) v[p] = src[p * ld];
+#pragma unroll
+    for (int p = 0; p < 16; ++p) t += v[p];
+  } else {
+    for (int p = 0; p < args.ss_parts; ++p) t += src[p * ld];
+  }
   return 1.0f / sqrtf(t / static_cast<float>(args.ss_n) + 1e-5f);
 }
 
@@ -393,7 +418,17 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
       if constexpr (EPI == kEpiF32) {
         if (args.resid32) load_f32x16(args.resid32 + static_cast<size_t>(mo) * args.ldr + n, x0);
       } else if constexpr (EPI == kEpiQKV) {
-        if (n < 1024) load_f32x16(reinterpret_cast<const float*>(args.rope + static_cast<size_t>(t) * 32 + ((n & 63) >> 1)), x0);
+        if (n < 1024) {
+          // Pairs p0..p0+7 of this row: one 8-byte load per pair, coalesced
+          // across the warp's consecutive rows.
+          const float2* rp = args.rope + static_cast<size_t>((n & 63) >> 1) * T + t;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float2 cs = rp[static_cast<size_t>(e) * T];
+            x0[2 * e] = cs.x;
+            x0[2 * e + 1] = cs.y;
+          }
+        }
       } else if constexpr (EPI == kEpiWnLast) {
         load_f32x16(args.wn_acc + static_cast<size_t>(m) * 512 + n, x0);
         load_f32x16(args.wn_res + static_cast<size_t>(m) * 512 + n, x1);
@@ -420,6 +455,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
     float vg[32];
 #pragma unroll 1
     for (int cp = c_begin; cp < c_end; cp += 2) {
+      float sc = 0.0f;  // folded-norm producer: sum of squares over this 32-column group
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = cp + h;
@@ -439,11 +475,9 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
 #pragma unroll
               for (int e = 0; e < 16; ++e) v[e] += x0_cur[e];
             }
-            if (args.ss_out && row_ok && n < args.N) {
-              float sc = 0.0f;
+            if (args.ss_out && n < args.N) {
 #pragma unroll
               for (int e = 0; e < 16; ++e) sc = fmaf(v[e], v[e], sc);
-              args.ss_out[static_cast<size_t>(n >> 4) * args.ss_ld + mo] = sc;
             }
           } else if constexpr (EPI == kEpiQKV) {
             if (n < 1024) {
@@ -478,6 +512,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
       }
       // Flush the group (two chunks, or one at the end).
       const int ng = n0 + cp * 16;
+      if constexpr (EPI == kEpiF32) {
+        // n0 and the first chunk of each half are multiples of 32 columns for
+        // every producer tile width (the host accepts only BN % 32 == 0).
+        if (args.ss_out && row_ok && ng < args.N) args.ss_out[static_cast<size_t>(ng >> 5) * args.ss_ld + mo] = sc;
+      }
       int ncols = (cp + 1 < c_end) ? 32 : 16;
       if (ng + ncols > args.N) ncols = args.N > ng ? args.N - ng : 0;
       __syncwarp();
@@ -744,13 +783,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int etid = threadIdx.x - 64;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     int local = 0;
+    float cst[consts_per_thread(BN)];
+    if (unit0 < num_tiles) load_tile_consts<BN, EPI>(args, (unit0 % n_tiles) * BN, etid, cst);
     for (int tile = unit0; tile < num_tiles; tile += units, ++local) {
       const int a = local & 1;
       const int m0 = (tile / n_tiles) * UNIT_M + static_cast<int>(rank) * kBM;
       const int n0 = (tile % n_tiles) * BN;
       epi_bar();  // every epilogue thread is done with the previous tile's constants
-      stage_tile_consts<BN, EPI>(args, n0, sconst, etid);
+      store_tile_consts<BN>(sconst, etid, cst);
       epi_bar();
+      if (tile + units < num_tiles) load_tile_consts<BN, EPI>(args, ((tile + units) % n_tiles) * BN, etid, cst);
       const bool ok = epilogue_tile<BN, EPI>(args, m0, n0, row, half,
                                              tmem_base + lane_off + static_cast<uint32_t>(a * ACC_STRIDE), sconst,
                                              stage_all + (warp - 2) * (kStageFloats / 4), &acc_full[a],

@@ -47,7 +47,7 @@ struct GemmArgs {
   const float* resid32;
   int ldr;
   int seq_T;              // rows per sequence (T)
-  const float2* rope;     // [T][32] (cos, sin) of t / 10000^(2p/64)
+  const float2* rope;     // [32][T] (cos, sin) of t / 10000^(2p/64) at rope[p * T + t]
   const float* wn_cond;   // [1024] WaveNet global condition of this layer: a-part | b-part
   const float* row_mask;  // [R] 0/1 per compact row
   float* wn_acc;          // [R,512] skip accumulator
@@ -59,9 +59,9 @@ struct GemmArgs {
   // AdaRMSNorm folded across a producer/consumer GEMM pair:
   //   y = w*g*(x*inv) + b,  inv = 1/sqrt(mean_k x^2 + 1e-5)
   //   y . W^T = inv * ((x*w*g) . W^T) + (b . W^T)
-  // Producer (kEpiF32): nrm16 = f16(v * nrm_w * nrm_g) and, per 16-column
-  // chunk p of the output, ss_out[p * ss_ld + row] = sum of v^2 over the chunk
-  // (the partial count never depends on the tile width).
+  // Producer (kEpiF32, tile width a multiple of 32): nrm16 = f16(v * nrm_w *
+  // nrm_g) and, per 32-column group p of the output, ss_out[p * ss_ld + row] =
+  // sum of v^2 over the group (the partial count never depends on the tile width).
   // Consumer (kEpiQKV, kEpiSwiGLU): the accumulator of row m is multiplied by
   // 1/sqrt(sum_p ss_in[p * ss_ld + m] / ss_n + 1e-5) before `bias` (which then
   // holds b . W^T) is added.

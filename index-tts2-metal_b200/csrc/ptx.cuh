@@ -372,8 +372,11 @@ __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.
 
 // ---- small math helpers ----
 
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
-__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + __expf(-v)); }
+// Fast division (reciprocal approximation, about 2 ulp in fp32): both feed
+// f16 outputs, whose rounding is 2^13 times coarser. For v -> -inf the
+// denominator overflows and both return 0, the limit of the exact forms.
+__device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+__device__ __forceinline__ float sigmoid_f(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
 
 // Pack 16 floats into 16 f16 and store as two 16-byte vectors.
 __device__ __forceinline__ void store_h16(__half* dst, const float* v) {
