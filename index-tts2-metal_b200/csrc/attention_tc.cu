@@ -2,18 +2,25 @@
 // queries of one (sequence, head) against all keys of its sequence in blocks
 // of 128 keys.
 //
-//   warp 0      : TMA producer (Q once; K and V blocks into a 2-deep ring) and
+//   warp 0      : TMA producer (Q once; K and V blocks into a 4-deep ring) and
 //                 the per-block key-mask bias row
-//   warp 1 (l0) : tcgen05.mma issuer: S_j = Q K_j^T (M=128, N=128, K=64) and
-//                 [O_h | l_h] += P_j,h [V_j,h | 1] per 64-key half h (M=128,
-//                 N=80, K=64; P from TMEM, V read MN-major from shared memory)
+//   warps 1, 10 : tcgen05.mma issuers (lane 0), one per 64-key half h; per
+//                 block j:
+//                 S_j,h = Q K_j,h^T (M=128, N=64, K=64) and
+//                 [O_h | l_h] += P_j,h [V_j,h | 1] (M=128, N=80, K=64; P from
+//                 TMEM, V read MN-major from shared memory)
 //   warps 2..9  : online softmax, two warps per query row quarter, each over
-//                 its own 64-key half of every block: S_j from TMEM, P_j (f16)
-//                 back into TMEM over the S_j columns it has read (the O MMA's
-//                 A operand); O stays in TMEM (rescaled lazily there); the
-//                 halves merge at the end.
-// TMEM: S double buffer (2 x 128 columns) and one O accumulator per key half
-// (2 x 64 columns).
+//                 its own 64-key half of every block: S_j,h from TMEM, P_j,h
+//                 (f16) back into TMEM over the S columns it has read (the O
+//                 MMA's A operand); O stays in TMEM (rescaled lazily there);
+//                 the halves merge at the end.
+// The two halves are independent pipelines (own issuer, barriers, S buffers
+// and O), so the two softmax warps sharing an SM sub-partition need not run
+// in phase: one can compute exponentials while the other loads S and takes
+// its row maximum. The K/V ring is shared (a stage is free after both halves'
+// O MMAs of its block).
+// TMEM: S double buffer (2 x 128 columns: half h at columns 64 h of each) and
+// one O accumulator per key half (2 x 128 columns, 80 used).
 //
 // Semantics follow cpu_attention_single_head_masked
 // (runtime/impl/tokenizer_tests.cpp:3960-3997): keys with mask 0 get
@@ -36,7 +43,8 @@ namespace {
 
 constexpr int kQ = 128;    // queries per CTA
 constexpr int kKB = 128;   // keys per block
-constexpr int kThreadsA = 64 + 8 * 32;  // producer, MMA, 8 softmax warps
+constexpr int kThreadsA = 64 + 8 * 32 + 32;  // producer, MMA (half 0), 8 softmax warps, MMA (half 1)
+constexpr int kIssuer1 = 10;                  // warp issuing the MMAs of key half 1
 constexpr int kKV = 4;     // K/V ring depth (blocks in flight)
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = 16384;                      // kKV stages x 16 KB
@@ -105,11 +113,13 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   uint64_t* q_full = bars;               // 1
   uint64_t* kv_full = bars + 1;          // kKV
   uint64_t* kv_empty = kv_full + kKV;    // kKV
-  uint64_t* s_full = kv_empty + kKV;     // 2
-  uint64_t* s_free = s_full + 2;         // 2
-  uint64_t* p_full = s_free + 2;         // 2
-  uint64_t* o_full = p_full + 2;         // 2: O MMAs of the blocks using S/P buffer 0 / 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  // Per key half h and S buffer b, index 2 h + b.
+  uint64_t* s_full = kv_empty + kKV;     // 4: S_j,h landed
+  uint64_t* s_free = s_full + 4;         // 4: the O MMA that read P_j,h (over S_j,h) is done
+  uint64_t* p_full = s_free + 4;         // 4: P_j,h written by the half's 4 softmax warps
+  uint64_t* o_full = p_full + 4;         // 4: O_h MMA of block j landed
+  uint64_t* stagger = o_full + 4;        // 1: half 0 has taken the row maximum of block 0
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stagger + 1);
   float* bias = reinterpret_cast<float*>(sm + OFF_BIAS);
   int* full_block = reinterpret_cast<int*>(sm + OFF_FLAG);
 
@@ -123,14 +133,15 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     mbar_init(q_full, 1);
     for (int i = 0; i < kKV; ++i) {
       mbar_init(&kv_full[i], 1 + 32);  // producer expect_tx + 32 lanes writing the mask row
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);  // one commit per key half
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 1);  // commit after the O MMA that read P from this S buffer
-      mbar_init(&p_full[i], 8);
+      mbar_init(&p_full[i], 4);
       mbar_init(&o_full[i], 1);
     }
+    mbar_init(stagger, 4);
     fence_barrier_init();
     fence_proxy_async_shared();
     prefetch_tmap(&tm);
@@ -170,6 +181,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       const uint32_t ph = (j / kKV) & 1;
       if (!mbar_wait(&kv_empty[st], ph ^ 1, status, kDevTimeoutAttn)) break;
       if (lane == 0) {
+        if (j < 8) ATTN_TRACE(192 + j);  // slots 192..199: K/V block j requested
         mbar_arrive_expect_tx(&kv_full[st], 2 * kKB * 128);
         tma_load_3d(sm + OFF_K + st * 16384, &tm, &kv_full[st], 0, seq0 + j * kKB, 8 + h);
         tma_load_3d(sm + OFF_V + st * 16384, &tm, &kv_full[st], 0, seq0 + j * kKB, 16 + h);
@@ -188,50 +200,56 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       __syncwarp();
       mbar_arrive(&kv_full[st]);
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer ----
+  } else if (warp == 1 || warp == kIssuer1) {
+    // ---- MMA issuers: warp 1 for key half 0, warp kIssuer1 for key half 1 ----
+    const int hh = warp == 1 ? 0 : 1;
     if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_f16_f32(128, kKB);
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, kKB / 2);
       constexpr uint32_t idesc_o = idesc_f16_f32(128, kON) | (1u << 16);  // B (V | ones) MN-major
       const uint32_t s_ones = smem_u32(sm + OFF_ONES);
       const uint32_t sq = smem_u32(sm + OFF_Q);
       bool ok = mbar_wait(q_full, 0, status, kDevTimeoutAttn);
+      // S_j,h into S buffer j & 1, columns 64 h, once K/V block j has landed
+      // and the O MMA that last read the buffer (block j - 2) is done. K rows
+      // [64 h, 64 h + 64) of the block start 8 KB (eight 1 KB swizzle atoms)
+      // into its stage.
       auto issue_s = [&](int j) -> bool {
-        const int kst = j % kKV;           // K/V stage
-        const int st = j & 1;              // S buffer
-        if (!mbar_wait(&kv_full[kst], (j / kKV) & 1, status, kDevTimeoutAttn)) return false;
-        if (!mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, status, kDevTimeoutAttn)) return false;
+        const int b = 2 * hh + (j & 1);
+        if (!mbar_wait(&kv_full[j % kKV], (j / kKV) & 1, status, kDevTimeoutAttn)) return false;
+        if (!mbar_wait(&s_free[b], ((j >> 1) & 1) ^ 1, status, kDevTimeoutAttn)) return false;
         tc_fence_after();
-        const uint32_t sk = smem_u32(sm + OFF_K + kst * 16384);
+        if (j < 8) ATTN_TRACE(160 + 2 * j + hh);  // slots 160..175: S_j,h issued
+        const uint32_t sk = smem_u32(sm + OFF_K + (j % kKV) * 16384 + hh * 8192);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_f16_ss(tmem + TMEM_S + st * 128, sdesc_k_sw128(sq + k * 32), sdesc_k_sw128(sk + k * 32), idesc_s,
-                      k != 0 ? 1u : 0u);
-        umma_commit(&s_full[st]);
+          umma_f16_ss(tmem + TMEM_S + (j & 1) * 128 + hh * 64, sdesc_k_sw128(sq + k * 32), sdesc_k_sw128(sk + k * 32),
+                      idesc_s, k != 0 ? 1u : 0u);
+        umma_commit(&s_full[b]);
         return true;
       };
+      // Half 1 starts once half 0 has its first row maximum, so that the two
+      // halves' exponential phases (which share the SFU) do not coincide.
+      if (ok && hh == 1) ok = mbar_wait(stagger, 0, status, kDevTimeoutAttn);
       if (ok) ok = issue_s(0);
+      if (ok && nkb > 1) ok = issue_s(1);
       for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        if (j + 1 < nkb && !issue_s(j + 1)) break;
-        if (!mbar_wait(&p_full[st], (j >> 1) & 1, status, kDevTimeoutAttn)) break;
+        // [O_h | l_h] += P_j,h [V_j,h | 1]; the half accumulates into its own
+        // TMEM columns across all key blocks.
+        const int b = 2 * hh + (j & 1);
+        if (!mbar_wait(&p_full[b], (j >> 1) & 1, status, kDevTimeoutAttn)) break;
         tc_fence_after();
-        if (j < 4) ATTN_TRACE(56 + j);  // slots 56..59: O_j waits done
+        if (j < 8) ATTN_TRACE(128 + 2 * j + hh);  // slots 128..143: O_j,h issued
         const uint32_t sv = smem_u32(sm + OFF_V + (j % kKV) * 16384);
-        // [O_h | l_h] += P_h [V_h | 1] for the two 64-key halves; each half
-        // accumulates into its own TMEM columns across all key blocks.
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t vb = sv + (hh * 4 + kk) * 2048;
-            umma_f16_ts(tmem + TMEM_O + hh * 128, tmem + TMEM_S + st * 128 + hh * 64 + kk * 8,
-                        sdesc_mn_sw128_lbo(vb, s_ones - vb), idesc_o, (j | kk) != 0 ? 1u : 0u);
-          }
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t vb = sv + (hh * 4 + kk) * 2048;
+          umma_f16_ts(tmem + TMEM_O + hh * 128, tmem + TMEM_S + (j & 1) * 128 + hh * 64 + kk * 8,
+                      sdesc_mn_sw128_lbo(vb, s_ones - vb), idesc_o, (j | kk) != 0 ? 1u : 0u);
         }
-        umma_commit(&o_full[st]);
-        umma_commit(&s_free[st]);  // P_j (over S_j) consumed: the buffer may take S_{j+2}
-        umma_commit(&kv_empty[j % kKV]);
+        umma_commit(&o_full[b]);
+        umma_commit(&s_free[b]);           // P_j,h consumed: the buffer may take S_j+2,h
+        umma_commit(&kv_empty[j % kKV]);   // this half is done with K/V block j
+        if (j + 2 < nkb) ok = issue_s(j + 2);
       }
     }
     __syncwarp();
@@ -256,7 +274,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       const int st = j & 1;
-      if (!mbar_wait(&s_full[st], (j >> 1) & 1, status, kDevTimeoutAttn)) {
+      const int b = 2 * hh + st;  // this half's barriers of S buffer st
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, status, kDevTimeoutAttn)) {
         ok = false;
         break;
       }
@@ -267,7 +286,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       tmem_wait_ld();
       reg_fence32(sr);
       reg_fence32(sr + 32);
-      if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(20 + j);
+      if (quarter == 0 && lane == 0 && j < 8) ATTN_TRACE(64 * hh + 20 + j);
       // The mask row of this block was published with kv_full (already complete).
       const int kst = j % kKV;
       if (!mbar_wait(&kv_full[kst], (j / kKV) & 1, status, kDevTimeoutAttn)) {
@@ -291,13 +310,14 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 #pragma unroll
       for (int e = 0; e < 8; ++e) mp[e] = fmaxf(mp[e], __uint_as_float(sr[56 + e]));
       const float mb = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
-      if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(40 + j);
+      if (quarter == 0 && lane == 0 && j < 8) ATTN_TRACE(64 * hh + 40 + j);
+      if (j == 0 && hh == 0 && lane == 0) mbar_arrive(stagger);
       if (mb > m + kLazy) {  // the first live key, or a maximum grown past 2^8
         if (m != -CUDART_INF_F) {
           // O_hh and its row sum hold contributions relative to m: rescale
           // them once the previous block's O MMA has landed.
           const float alpha = ex2_approx((m - mb) * kLog2e);
-          if (!mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, status, kDevTimeoutAttn)) {
+          if (!mbar_wait(&o_full[2 * hh + ((j - 1) & 1)], ((j - 1) >> 1) & 1, status, kDevTimeoutAttn)) {
             ok = false;
             break;
           }
@@ -341,19 +361,23 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           pw[c * 4 + e] = *reinterpret_cast<const uint32_t*>(&h2);
         }
       }
-      if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(50 + j);
+      if (quarter == 0 && lane == 0 && j < 8) ATTN_TRACE(64 * hh + 50 + j);
       tmem_st32(tmem + lane_off + TMEM_S + st * 128 + hh * 64, pw);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[st]);
-      if (warp == 2 && lane == 0 && j < 8) ATTN_TRACE(30 + j);
+      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (quarter == 0 && lane == 0 && j < 8) ATTN_TRACE(64 * hh + 30 + j);
     }
     // Merge the two key halves of the row: each warp hands the partner the 32
     // output dims the partner writes (through the now idle P buffers), its
     // reference maximum and its row sum.
     uint32_t ov[32], oth[32], lv[16];  // O_hh at this warp's output dims / at the partner's; row sum
-    if (ok) ok = mbar_wait(&o_full[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, status, kDevTimeoutAttn);
+    // Both halves' last O MMAs (which follow all their S MMAs) must be done:
+    // this warp's own result, and the K ring (reused for the exchange below)
+    // no longer read by the other half.
+    if (ok) ok = mbar_wait(&o_full[2 * hh + ((nkb - 1) & 1)], ((nkb - 1) >> 1) & 1, status, kDevTimeoutAttn);
+    if (ok) ok = mbar_wait(&o_full[2 * (hh ^ 1) + ((nkb - 1) & 1)], ((nkb - 1) >> 1) & 1, status, kDevTimeoutAttn);
     if (ok) {
       tc_fence_after();
       tmem_ld32_async(t_o + hh * 32, ov);
@@ -409,7 +433,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) ATTN_TRACE(60);
+  if (threadIdx.x == 0) ATTN_TRACE(63);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
