@@ -233,6 +233,115 @@ def make_dit_bundle(out_dir: str | Path, seed: int = 0, init: str = "baseline") 
     return out
 
 
+# BigVGAN generator layout (runtime/impl/dit_cfm_bigvgan.cpp:3681-3688, 3961-3980):
+# transposed-conv upsamplers (in, out, kernel, stride, padding) and the three
+# resblock kernels of each upsampling stage (dilations 1, 3, 5 in every resblock).
+BIGVGAN_UPSAMPLERS = [(1536, 768, 8, 4, 2), (768, 384, 8, 4, 2), (384, 192, 4, 2, 1),
+                      (192, 96, 4, 2, 1), (96, 48, 4, 2, 1), (48, 24, 4, 2, 1)]
+BIGVGAN_RESBLOCK_KERNELS = (3, 7, 11)
+BIGVGAN_DILATIONS = (1, 3, 5)
+BIGVGAN_HOP = 256
+
+
+def kaiser_sinc_lowpass(cutoff: float, half_width: float, taps: int = 12) -> np.ndarray:
+    """Kaiser-windowed sinc low-pass filter (the anti-aliasing filter design of
+    the BigVGAN paper: Kaiser's beta formula for the stop-band attenuation of
+    the transition width, window times sinc, normalised to unit DC gain)."""
+    half = taps // 2
+    delta_f = 4.0 * half_width
+    atten = 2.285 * (half - 1) * math.pi * delta_f + 7.95
+    if atten > 50.0:
+        beta = 0.1102 * (atten - 8.7)
+    elif atten >= 21.0:
+        beta = 0.5842 * (atten - 21.0) ** 0.4 + 0.07886 * (atten - 21.0)
+    else:
+        beta = 0.0
+    t = np.arange(-half, half, dtype=np.float64) + 0.5
+    f = 2.0 * cutoff * np.kaiser(taps, beta) * np.sinc(2.0 * cutoff * t)
+    return (f / f.sum()).astype(np.float32)
+
+
+def bigvgan_tensor_specs() -> list[tuple[str, tuple[int, ...], str]]:
+    """(full name, shape, kind) of every BigVGAN tensor the vocoder reads.
+
+    kind: "wv"/"wg" weight norm (v, g), "b" bias, "filt" 12-tap filter,
+    "logscale" SnakeBeta alpha/beta (log scale)."""
+    s: list[tuple[str, tuple[int, ...], str]] = []
+
+    def conv(prefix: str, rows: int, inner: int, k: int, bias: bool = True):
+        s.extend([(f"{prefix}.weight_g", (rows, 1, 1), "wg"), (f"{prefix}.weight_v", (rows, inner, k), "wv")])
+        if bias:
+            s.append((f"{prefix}.bias", (inner if prefix.startswith("bigvgan.ups") else rows,), "b"))
+
+    def act(prefix: str, c: int):
+        s.extend([(f"{prefix}.upsample.filter", (1, 1, 12), "filt"),
+                  (f"{prefix}.downsample.lowpass.filter", (1, 1, 12), "filt"),
+                  (f"{prefix}.act.alpha", (c,), "logscale"), (f"{prefix}.act.beta", (c,), "logscale")])
+
+    conv("bigvgan.conv_pre", 1536, 80, 7)
+    for i, (cin, cout, k, _, _) in enumerate(BIGVGAN_UPSAMPLERS):
+        conv(f"bigvgan.ups.{i}.0", cin, cout, k)  # transposed: rows = input channels
+        for j, rk in enumerate(BIGVGAN_RESBLOCK_KERNELS):
+            r = f"bigvgan.resblocks.{3 * i + j}"
+            for p in range(3):
+                conv(f"{r}.convs1.{p}", cout, cout, rk)
+                conv(f"{r}.convs2.{p}", cout, cout, rk)
+            for a in range(6):
+                act(f"{r}.activations.{a}", cout)
+    act("bigvgan.activation_post", 24)
+    conv("bigvgan.conv_post", 1, 24, 7, bias=False)
+    return s
+
+
+def make_bigvgan_tensors(seed: int) -> list[tuple[str, np.ndarray]]:
+    """Deterministic synthetic BigVGAN weights: weight_v ~ N(0, 1/fan_in)
+    (f16) with weight_g = 0.8 ||v_row|| so each folded conv keeps roughly unit
+    gain, biases N(0, 0.02), SnakeBeta log-scale alpha/beta N(0, 0.1), and the
+    anti-aliasing filters of a ratio-2 resampler (cutoff 0.25, half-width 0.3)."""
+    rng = np.random.default_rng(seed)
+    lp = kaiser_sinc_lowpass(0.25, 0.3)
+    out: list[tuple[str, np.ndarray]] = []
+    v_rows: dict[str, np.ndarray] = {}
+    for name, shape, kind in bigvgan_tensor_specs():
+        if kind == "wv":
+            fan_in = int(np.prod(shape[1:]))
+            arr = (rng.standard_normal(shape, dtype=np.float32) / math.sqrt(fan_in)).astype(np.float16)
+            v_rows[name[: -len("weight_v")]] = arr
+        elif kind == "wg":
+            continue  # written after its v (below), in spec order
+        elif kind == "b":
+            arr = (rng.standard_normal(shape, dtype=np.float32) * 0.02).astype(np.float16)
+        elif kind == "filt":
+            arr = lp.reshape(shape).copy()
+        elif kind == "logscale":
+            arr = (rng.standard_normal(shape, dtype=np.float32) * 0.1).astype(np.float32)
+        else:
+            raise AssertionError(kind)
+        out.append((name, arr))
+    by_name = dict(out)
+    ordered: list[tuple[str, np.ndarray]] = []
+    for name, shape, kind in bigvgan_tensor_specs():
+        if kind == "wg":
+            v = v_rows[name[: -len("weight_g")]].astype(np.float32)
+            norms = np.sqrt((v.reshape(v.shape[0], -1) ** 2).sum(axis=1))
+            ordered.append((name, (0.8 * norms).reshape(shape).astype(np.float16)))
+        else:
+            ordered.append((name, by_name[name]))
+    return ordered
+
+
+def make_vocoder_bundle(out_dir: str | Path, seed: int = 0) -> Path:
+    """Write the synthetic BigVGAN bundle; skips work when an identical one exists."""
+    out = Path(out_dir)
+    stamp = out / ".synthetic"
+    key = f"bigvgan seed={seed} v1"
+    if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():
+        return out
+    write_bundle(out, make_bigvgan_tensors(seed), metadata={"synthetic": True, "seed": seed, "model": "bigvgan"})
+    stamp.write_text(key)
+    return out
+
+
 def bundle_f32(bundle_dir: str | Path) -> dict[str, np.ndarray]:
     """All estimator tensors decoded to contiguous float32 (f16 decoding is exact)."""
     return {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in read_bundle(bundle_dir).items()}

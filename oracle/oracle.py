@@ -122,6 +122,46 @@ class PortOracle:
         return out
 
 
+class VocoderOracle:
+    """fp32 CPU restatement of the reference's BigVGAN vocoder
+    (oracle/bigvgan_oracle.c), over the bundle's bigvgan.* tensors."""
+
+    def __init__(self, tensors: dict[str, np.ndarray], lib_path: Path = PORT_LIB):
+        self.lib = C.CDLL(str(lib_path))
+        L = self.lib
+        L.voc_model_new.restype = C.c_void_p
+        L.voc_model_free.argtypes = [C.c_void_p]
+        L.voc_model_set.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]
+        L.voc_vocoder.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.voc_activation.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        self._keep = {k: _f32(v) for k, v in tensors.items() if k.startswith("bigvgan.")}
+        self.m = C.c_void_p(L.voc_model_new())
+        for k, v in self._keep.items():
+            L.voc_model_set(self.m, k.encode(), _p(v), v.size)
+
+    def __del__(self):
+        try:
+            self.lib.voc_model_free(self.m)
+        except Exception:
+            pass
+
+    def vocoder(self, mel):
+        mel = _f32(mel)
+        T = mel.shape[0]
+        out = np.empty(T * 256, np.float32)
+        if self.lib.voc_vocoder(self.m, _p(mel), T, _p(out)):
+            raise RuntimeError(f"oracle vocoder failed (line {self.lib.voc_last_error()})")
+        return out
+
+    def activation(self, prefix: str, x):
+        x = _f32(x)
+        T, Cc = x.shape
+        out = np.empty_like(x)
+        if self.lib.voc_activation(self.m, prefix.encode(), _p(x), T, Cc, _p(out)):
+            raise RuntimeError(f"oracle activation failed (line {self.lib.voc_last_error()})")
+        return out
+
+
 def ref_available() -> bool:
     return REF_LIB.exists()
 
@@ -144,6 +184,8 @@ class RefOracle:
         L.ref_wavenet.argtypes = [C.c_char_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p]
         L.ref_timestep_embed.argtypes = [C.c_char_p, C.c_float, C.c_int, C.c_void_p]
         L.ref_noise.argtypes = [C.c_uint32, C.c_uint32, C.c_uint64, C.c_float, C.c_void_p]
+        L.ref_bigvgan_vocoder.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_void_p]
+        L.ref_bigvgan_activation.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
 
     def _ok(self, rc):
         if rc:
@@ -197,6 +239,20 @@ class RefOracle:
     def noise(self, T, C_, seed, temperature=1.0):
         out = np.empty((T, C_), np.float32)
         self._ok(self.lib.ref_noise(T, C_, seed, temperature, _p(out)))
+        return out
+
+    def vocoder(self, mel):
+        mel = _f32(mel)
+        T = mel.shape[0]
+        out = np.empty(T * 256, np.float32)
+        self._ok(self.lib.ref_bigvgan_vocoder(self.dir, _p(mel), T, _p(out)))
+        return out
+
+    def activation(self, prefix: str, x):
+        x = _f32(x)
+        T, Cc = x.shape
+        out = np.empty_like(x)
+        self._ok(self.lib.ref_bigvgan_activation(self.dir, prefix.encode(), _p(x), T, Cc, _p(out)))
         return out
 
 

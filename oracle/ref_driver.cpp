@@ -31,6 +31,9 @@ std::vector<float> run_timestep_embedder_cpu(const mit2::Bundle& bundle, const s
                                              const std::string& prefix);
 std::vector<float> make_deterministic_normal_noise(uint32_t tokens, uint32_t channels, uint64_t seed,
                                                    float temperature);
+std::vector<float> run_bigvgan_vocoder_cpu(const mit2::Bundle& bundle, std::vector<float> mel, uint32_t tokens);
+std::vector<float> run_bigvgan_activation_cpu(const mit2::Bundle& bundle, const std::string& prefix,
+                                              const std::vector<float>& x, uint32_t tokens, uint32_t channels);
 
 namespace {
 thread_local std::string g_err;
@@ -140,6 +143,25 @@ int ref_timestep_embed(const char* bundle_dir, float t, int which, float* out) {
 int ref_noise(uint32_t T, uint32_t C, uint64_t seed, float temperature, float* out) {
   return guard([&] {
     auto v = make_deterministic_normal_noise(T, C, seed, temperature);
+    std::memcpy(out, v.data(), v.size() * sizeof(float));
+  });
+}
+
+// run_bigvgan_vocoder_cpu: mel [T,80] -> waveform [T*256] in [-1, 1].
+int ref_bigvgan_vocoder(const char* bundle_dir, const float* mel, uint32_t T, float* out) {
+  return guard([&] {
+    mit2::Bundle b(bundle_dir);
+    auto v = run_bigvgan_vocoder_cpu(b, vec(mel, T * 80ull), T);
+    std::memcpy(out, v.data(), v.size() * sizeof(float));
+  });
+}
+
+// run_bigvgan_activation_cpu: the anti-aliased SnakeBeta of `prefix` on x [T,C].
+int ref_bigvgan_activation(const char* bundle_dir, const char* prefix, const float* x, uint32_t T, uint32_t C,
+                           float* out) {
+  return guard([&] {
+    mit2::Bundle b(bundle_dir);
+    auto v = run_bigvgan_activation_cpu(b, prefix, vec(x, static_cast<size_t>(T) * C), T, C);
     std::memcpy(out, v.data(), v.size() * sizeof(float));
   });
 }

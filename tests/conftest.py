@@ -63,6 +63,23 @@ def port_baseline(baseline_tensors):
     return oracle.PortOracle(baseline_tensors)
 
 
+@pytest.fixture(scope="session")
+def vocoder_bundle() -> Path:
+    return mit2.make_vocoder_bundle(BUNDLE_ROOT / "bigvgan_seed0", seed=0)
+
+
+@pytest.fixture(scope="session")
+def vocoder_tensors(vocoder_bundle):
+    return mit2.bundle_f32(vocoder_bundle)
+
+
+@pytest.fixture(scope="session")
+def port_vocoder(vocoder_tensors):
+    import oracle
+
+    return oracle.VocoderOracle(vocoder_tensors)
+
+
 def _gpu_ctx(bundle):
     import itts_cfm
 

@@ -19,6 +19,11 @@ Cases (inputs follow the reference's self-tests where it has them):
   kat_wavenet_t6    WaveNet stack with a global condition, mask 111100
   kat_euler_t5      run_cfm_euler_test inputs (T=5, P=2): 3 steps cfg 0 and 25 steps cfg 0.5
   kat_euler_masked  T=8 (2 padded), P=2, 2 steps, cfg 0.7 (padded-batch semantics)
+  kat_bigvgan       BigVGAN vocoder (run_bigvgan_vocoder_cpu) on a seeded T=3 mel,
+                    and two anti-aliased SnakeBeta activations (768 and 24
+                    channels) on seeded inputs, synthetic vocoder bundle seed 0
+
+    python tests/golden/make_golden.py [--only bigvgan]
 """
 from __future__ import annotations
 
@@ -68,7 +73,25 @@ def estimator_selftest_inputs():
     return f32(x).reshape(T, 80), f32(px).reshape(T, 80), f32(cond).reshape(T, 512), f32(style)
 
 
+def bigvgan_cases():
+    voc = mit2.make_vocoder_bundle(ROOT / "bigvgan_seed0", seed=0)
+    rv = oracle.RefOracle(voc)
+    rng = np.random.default_rng(9)
+    mel = f32(rng.standard_normal((3, 80)))
+    xa = f32(rng.standard_normal((13, 768)))
+    xp = f32(rng.standard_normal((41, 24)) * 0.5)
+    np.savez_compressed(HERE / "kat_bigvgan.npz", mel=mel, wave=rv.vocoder(mel), x_act=xa,
+                        act_rb0=rv.activation("bigvgan.resblocks.0.activations.0", xa), x_post=xp,
+                        act_post=rv.activation("bigvgan.activation_post", xp), bundle_seed=0,
+                        weights_sha256=weights_sha(voc))
+
+
 def main():
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "bigvgan":
+        bigvgan_cases()
+        print("golden vectors written to", HERE)
+        return
+    bigvgan_cases()
     unit = mit2.make_dit_bundle(ROOT / "seed0_unit", seed=0, init="unit")
     base = mit2.make_dit_bundle(ROOT / "seed0_baseline", seed=0, init="baseline")
     ru, rb = oracle.RefOracle(unit), oracle.RefOracle(base)

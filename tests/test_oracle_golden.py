@@ -1,4 +1,4 @@
-"""Pin the CPU oracle (oracle/dit_oracle.c) to the reference's own CPU
+"""Pin the CPU oracles (oracle/dit_oracle.c, oracle/bigvgan_oracle.c) to the reference's own CPU
 functions through the committed golden vectors (tests/golden/, made by
 tests/golden/make_golden.py from oracle/_ref). fp32 vs fp32 with a different
 summation order: the reference's own unit tolerance ladder applies (1e-4
@@ -104,3 +104,31 @@ def test_oracle_detects_planted_error(port_unit, unit_tensors):
     args = (g["x"], g["prompt_x"], g["cond"], g["style"], float(g["t"]), g["mask"])
     with pytest.raises(AssertionError):
         _close(g["vel_unit"], wrong.estimator(*args))
+
+
+def test_bigvgan_bundle_matches_golden_generator(vocoder_bundle):
+    assert _sha(vocoder_bundle) == str(_load("kat_bigvgan")["weights_sha256"])
+
+
+def test_bigvgan_activations(port_vocoder):
+    g = _load("kat_bigvgan")
+    _close(g["act_rb0"], port_vocoder.activation("bigvgan.resblocks.0.activations.0", g["x_act"]))
+    _close(g["act_post"], port_vocoder.activation("bigvgan.activation_post", g["x_post"]))
+
+
+def test_bigvgan_vocoder(port_vocoder):
+    g = _load("kat_bigvgan")
+    wave = port_vocoder.vocoder(g["mel"])
+    assert wave.shape == (3 * 256,)
+    _close(g["wave"], wave)
+
+
+def test_bigvgan_oracle_detects_planted_error(vocoder_tensors):
+    """A wrong resblock weight in the vocoder oracle must break the pin."""
+    g = _load("kat_bigvgan")
+    bad = dict(vocoder_tensors)
+    k = "bigvgan.resblocks.4.convs2.1.weight_v"
+    bad[k] = bad[k].copy()
+    bad[k][5] *= -1.0
+    with pytest.raises(AssertionError):
+        _close(g["wave"], O.VocoderOracle(bad).vocoder(g["mel"]))
