@@ -222,6 +222,44 @@ int itts_op_adarms(itts_cfm_ctx* ctx, const float* x, uint32_t R, const float* w
 int itts_op_conv5_noalloc(const void* x, uint32_t S, uint32_t T, const void* w, const float* bias, float* out,
                           uint32_t N, void* stream, char* err, uint32_t err_cap);
 
+/* ------------------------------------------------------------------------
+ * BigVGAN vocoder: mel [T,80] (token-major, the CFM output rows after the
+ * prompt) -> waveform [256 T] in [-1, 1]. Replaces
+ * run_bigvgan_vocoder_metal(MetalContext&, const Bundle&, std::vector<float>
+ * mel, uint32_t tokens) (runtime/impl/dit_cfm_bigvgan.cpp:4196-4223; CPU twin
+ * run_bigvgan_vocoder_cpu, :4058-4061), which the synthesis pipeline calls on
+ * the generated mel rows (runtime/impl/tts_synthesis/synthesis_pipeline.cpp:1085-1089).
+ * ------------------------------------------------------------------------ */
+typedef struct itts_vocoder_ctx itts_vocoder_ctx;
+
+#define ITTS_VOCODER_MAX_T 16384u /* mel frames per call (4.2 M samples) */
+
+/* Loads the bundle's bigvgan.* tensors (weight norm folded at load) onto
+ * `device`. Replaces the lazy resident upload of the vocoder weights
+ * (runtime/impl/dit_cfm_bigvgan.cpp:4064-4101). */
+int itts_vocoder_create(const char* bundle_dir, int device, itts_vocoder_ctx** out);
+void itts_vocoder_destroy(itts_vocoder_ctx* ctx);
+const char* itts_vocoder_last_error(const itts_vocoder_ctx* ctx);
+const char* itts_vocoder_create_error(void);
+
+/* Host mel [T,80] f32 -> host wave [256 T] f32 (the caller owns both). The
+ * first call for a length T builds that length's workspace and CUDA graph. */
+int itts_vocoder_run(itts_vocoder_ctx* ctx, const float* mel, uint32_t T, float* wave);
+
+/* The pieces of itts_vocoder_run for timing: stage (upload + plan), launch
+ * (graph replay on the context's stream, asynchronous), fetch (download and
+ * synchronise). No reference counterpart. */
+int itts_vocoder_stage(itts_vocoder_ctx* ctx, const float* mel, uint32_t T);
+int itts_vocoder_launch(itts_vocoder_ctx* ctx);
+int itts_vocoder_fetch(itts_vocoder_ctx* ctx, float* wave);
+void* itts_vocoder_stream(itts_vocoder_ctx* ctx);
+/* Kernels in the staged length's graph (>= 0), or a negative status. */
+int itts_vocoder_launch_kernels(itts_vocoder_ctx* ctx);
+/* Event-timed launches of one vocoder pass over the staged mel, per kind. */
+int itts_vocoder_profile(itts_vocoder_ctx* ctx, int reps, itts_kernel_stat* out, int cap, int* n_out);
+/* Algorithmic FLOPs of one pass over T mel frames (conv MACs x 2). */
+double itts_vocoder_flops(uint32_t T);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,8 @@ GemmLaunch make_gemm(Operand a0, Operand a1, Operand b, int M, int N, int K, int
   g.args.a_mode = a_mode;
   g.args.kb_split = kb_split;
   g.args.kb_per_tap = kb_per_tap;
+  g.args.conv_dil = 1;   // the k=5 WaveNet conv over reflect-padded rows: taps at rows m - 2 .. m + 2
+  g.args.conv_off = -2;
   g.args.epi = epi;
   g.bn = bn;
   g.pair = pair;
@@ -374,7 +376,7 @@ void Engine::build_work_launches(Work* w) {
   w->g_c1res.args.out32 = w->res;
   w->g_c1res.args.ld32 = 512;
   for (int l = 0; l < kWnLayers; ++l) {
-    w->g_in[l] = make_gemm(act(w->xp16, 512, w->Rp), none, wt(w_.win[l], 2560, 1024), w->Rp, 1024, 2560, kAConv5, 0, 8,
+    w->g_in[l] = make_gemm(act(w->xp16, 512, w->Rp), none, wt(w_.win[l], 2560, 1024), w->Rp, 1024, 2560, kAConv, 0, 8,
                            0, kEpiWnGate);
     w->g_in[l].args.bias = w_.bin[l];
     w->g_in[l].args.out16 = w->gate16;
@@ -482,8 +484,8 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
   auto gemm_bytes = [&](const GemmLaunch& g, double rows, double K) {
     const GemmArgs& a = g.args;
     const double N = a.N;
-    // (the implicit k=5 conv reads each A row once from HBM, five times from L2)
-    double b = rows * (a.a_mode == kAConv5 ? K / 5.0 : K) * 2.0 + N * K * 2.0;
+    // (an implicit conv reads each A row once from HBM, once per tap from L2)
+    double b = rows * (a.a_mode == kAConv ? a.kb_per_tap * 64.0 : K) * 2.0 + N * K * 2.0;
     switch (a.epi) {
       case kEpiF16: b += rows * N * 2.0; break;
       case kEpiQKV: b += rows * N * 2.0; break;
@@ -501,7 +503,7 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
     return b;
   };
   auto G = [&](const char* name, const GemmLaunch& g, double K) {
-    const double rows = g.args.a_mode == kAConv5 ? R : static_cast<double>(g.args.M);
+    const double rows = g.args.a_mode == kAConv ? R : static_cast<double>(g.args.M);
     const double flops = 2.0 * rows * g.args.N * K;
     P.run(name, flops, prof ? gemm_bytes(g, rows, K) : 0.0, [&] { check(gemm_run(g, stream_), name); });
   };

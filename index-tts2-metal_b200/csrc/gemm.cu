@@ -448,9 +448,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int m0, int 
     tc_fence_after();
     if (threadIdx.x == 64 && parity == 0) GEMM_TRACE(21);
     uint32_t tc[16], tn[16];
-    tmem_ld16_async(taddr + c_begin * 16, tc);
-    tmem_wait_ld();
-    reg_fence16(tc);
+    if (c_begin < c_end) {  // (a half of a 32-wide tile has no columns: its TMEM lies outside the allocation)
+      tmem_ld16_async(taddr + c_begin * 16, tc);
+      tmem_wait_ld();
+      reg_fence16(tc);
+    }
     if (threadIdx.x == 64 && parity == 0) GEMM_TRACE(22);
     float vg[32];
 #pragma unroll 1
@@ -676,13 +678,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], (PAIR ? 2 : 1) * STAGE_BYTES);
           // Each branch names its tensor map directly (a runtime-selected
           // pointer to a grid-constant parameter costs a local copy).
-          if (args.a_mode == kAConv5) {
+          if (args.a_mode == kAConv) {
             const int tap = kb / args.kb_per_tap;
             const int kc = kb - tap * args.kb_per_tap;
+            const int row = m0 + tap * args.conv_dil + args.conv_off;
             if constexpr (PAIR) {
-              tma_load_3d_pair(sa, &tmA0, full_addr(s), 0, m0 + tap - 2, kc);
+              tma_load_3d_pair(sa, &tmA0, full_addr(s), 0, row, kc);
             } else {
-              tma_load_3d(sa, &tmA0, &full_bar[s], 0, m0 + tap - 2, kc);
+              tma_load_3d(sa, &tmA0, &full_bar[s], 0, row, kc);
             }
           } else if (args.a_mode == kASplit && kb >= args.kb_split) {
             if constexpr (PAIR) {
@@ -888,6 +891,13 @@ cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
 
 template <int BN, bool PAIR>
 cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream) {
+  if constexpr (BN < 64) {  // narrow tiles: plain epilogues only
+    switch (g.args.epi) {
+      case kEpiF16: return launch_t<BN, kEpiF16, PAIR>(g, stream);
+      case kEpiF32: return launch_t<BN, kEpiF32, PAIR>(g, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (g.args.epi) {
     case kEpiF16: return launch_t<BN, kEpiF16, PAIR>(g, stream);
     case kEpiF32: return launch_t<BN, kEpiF32, PAIR>(g, stream);
@@ -972,6 +982,8 @@ cudaError_t gemm_run(const GemmLaunch& g, cudaStream_t stream) {
     }
   }
   switch (g.bn) {
+    case 32: return launch_epi<32, false>(g, stream);
+    case 48: return launch_epi<48, false>(g, stream);
     case 64: return launch_epi<64, false>(g, stream);
     case 80: return launch_epi<80, false>(g, stream);
     case 128: return launch_epi<128, false>(g, stream);

@@ -14,8 +14,10 @@ namespace itts {
 enum GemmAMode : int {
   kAPlain = 0,  // every k-block from A0
   kASplit = 1,  // k-blocks [0, kb_split) from A0, the rest from A1 (a concat without a buffer)
-  kAConv5 = 2,  // implicit k=5 conv over a reflect-padded row space: k-block kb reads A0 at
-                // column (kb % kb_per_tap)*64 and row (m0 + kb / kb_per_tap - 2)
+  kAConv = 2,   // implicit conv: k-block kb is tap (kb / kb_per_tap), reading A0 at column
+                // (kb % kb_per_tap)*64 and row (m0 + tap * conv_dil + conv_off); rows outside
+                // the tensor read as zeros (the k=5 WaveNet conv: conv_dil 1, conv_off -2 over
+                // a reflect-padded row space; a transposed-conv phase: conv_dil -1)
 };
 
 // Fused epilogues. "Paired" epilogues expect B rows interleaved in 64-row
@@ -38,6 +40,8 @@ struct GemmArgs {
   int a_mode;
   int kb_split;
   int kb_per_tap;
+  int conv_dil;           // kAConv: row step per tap (the dilation, or -1 for a transposed-conv phase)
+  int conv_off;           // kAConv: row offset of tap 0
   int epi;
   const float* bias;      // [N] in B-row order, or null
   float* out32;
@@ -88,7 +92,9 @@ struct GemmLaunch {
 // k-blocks (64 columns each) fetched per TMA instruction: one TMA box moves
 // kbox x rows x 128 B, and larger boxes raise the per-SM ingest rate (a
 // 1600x512x512 F32 GEMM at BN=64 runs 3-4% faster with 4 than with 2).
-__host__ __device__ constexpr int gemm_kbox(int bn) { return bn <= 64 ? 4 : bn <= 128 ? 2 : 1; }
+// Tiles narrower than 64 columns (32, 48: the late BigVGAN stages) fetch one
+// k-block per box, so that a conv tap of a single 64-channel block fits.
+__host__ __device__ constexpr int gemm_kbox(int bn) { return bn < 64 ? 1 : bn == 64 ? 4 : bn <= 128 ? 2 : 1; }
 
 // Bytes of one pipeline stage of a CTA: kbox k-blocks of A (128 rows) and of
 // B (bn rows, or bn / 2 in the CTA-pair form).

@@ -132,8 +132,10 @@ extern "C" int itts_op_conv5_noalloc(const void* x, uint32_t S, uint32_t T, cons
   }
   g.args.M = static_cast<int>(rows);
   g.args.N = static_cast<int>(N);
-  g.args.a_mode = itts::kAConv5;
+  g.args.a_mode = itts::kAConv;
   g.args.kb_per_tap = 8;
+  g.args.conv_dil = 1;
+  g.args.conv_off = -2;
   g.args.num_kb = 40;
   g.args.epi = itts::kEpiF32;
   g.args.pad_rows = 1;

@@ -30,7 +30,12 @@ EXPORTED = [
     "itts_cfm_estimator", "itts_cfm_stage_padded", "itts_cfm_launch", "itts_cfm_sync", "itts_cfm_fetch",
     "itts_cfm_stream", "itts_cfm_launch_kernels", "itts_cfm_profile_step", "itts_cfm_step_flops", "itts_op_gemm", "itts_op_conv5",
     "itts_op_attention", "itts_op_adarms", "itts_op_conv5_noalloc", "itts_cfm_selftest_timeout",
+    "itts_vocoder_create", "itts_vocoder_destroy", "itts_vocoder_last_error", "itts_vocoder_create_error",
+    "itts_vocoder_run", "itts_vocoder_stage", "itts_vocoder_launch", "itts_vocoder_fetch", "itts_vocoder_stream",
+    "itts_vocoder_launch_kernels", "itts_vocoder_profile", "itts_vocoder_flops",
 ]
+VOCODER_HOP = 256
+VOCODER_MAX_T = 16384
 
 
 class IttsError(RuntimeError):
@@ -88,6 +93,18 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_op_adarms": (i32, [vp, vp, u32, vp, vp, vp]),
         "itts_op_conv5_noalloc": (i32, [vp, u32, u32, vp, vp, vp, u32, vp, C.c_char_p, u32]),
         "itts_cfm_selftest_timeout": (i32, [vp, C.c_uint64]),
+        "itts_vocoder_create": (i32, [C.c_char_p, i32, C.POINTER(vp)]),
+        "itts_vocoder_destroy": (None, [vp]),
+        "itts_vocoder_last_error": (C.c_char_p, [vp]),
+        "itts_vocoder_create_error": (C.c_char_p, []),
+        "itts_vocoder_run": (i32, [vp, vp, u32, vp]),
+        "itts_vocoder_stage": (i32, [vp, vp, u32]),
+        "itts_vocoder_launch": (i32, [vp]),
+        "itts_vocoder_fetch": (i32, [vp, vp]),
+        "itts_vocoder_stream": (vp, [vp]),
+        "itts_vocoder_launch_kernels": (i32, [vp]),
+        "itts_vocoder_profile": (i32, [vp, i32, vp, i32, C.POINTER(i32)]),
+        "itts_vocoder_flops": (f64, [u32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -263,3 +280,80 @@ def bucket_len(T: int) -> int:
 
 def step_flops(S: int, T: int) -> float:
     return float(load().itts_cfm_step_flops(S, T))
+
+
+class Vocoder:
+    """BigVGAN vocoder bound to one GPU (itts_vocoder_create): mel [T, 80] ->
+    waveform [256 T] in [-1, 1]."""
+
+    def __init__(self, bundle_dir: str | Path, device: int = 0):
+        self.lib = load()
+        h = C.c_void_p()
+        rc = self.lib.itts_vocoder_create(str(bundle_dir).encode(), int(device), C.byref(h))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_vocoder_create_error().decode())
+        self.h = h
+        self.T = 0
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.itts_vocoder_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int) -> None:
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_vocoder_last_error(self.h).decode())
+
+    def run(self, mel) -> np.ndarray:
+        mel = _f32(mel)
+        if mel.ndim != 2 or mel.shape[1] != 80:
+            raise ValueError("mel must be [T, 80]")
+        wave = np.empty(mel.shape[0] * VOCODER_HOP, np.float32)
+        self._check(self.lib.itts_vocoder_run(self.h, _ptr(mel), mel.shape[0], _ptr(wave)))
+        return wave
+
+    def stage(self, mel) -> None:
+        mel = _f32(mel)
+        self._check(self.lib.itts_vocoder_stage(self.h, _ptr(mel), mel.shape[0]))
+        self.T = mel.shape[0]
+
+    def launch(self) -> None:
+        self._check(self.lib.itts_vocoder_launch(self.h))
+
+    def fetch(self) -> np.ndarray:
+        wave = np.empty(self.T * VOCODER_HOP, np.float32)
+        self._check(self.lib.itts_vocoder_fetch(self.h, _ptr(wave)))
+        return wave
+
+    def stream(self) -> int:
+        return int(self.lib.itts_vocoder_stream(self.h) or 0)
+
+    def launch_kernels(self) -> int:
+        n = int(self.lib.itts_vocoder_launch_kernels(self.h))
+        if n < 0:
+            raise IttsError(n, "nothing staged")
+        return n
+
+    def profile(self, reps: int = 1) -> list[dict]:
+        cap = 64
+        buf = (KernelStat * cap)()
+        n = C.c_int(0)
+        self._check(self.lib.itts_vocoder_profile(self.h, reps, C.cast(buf, C.c_void_p), cap, C.byref(n)))
+        return [dict(name=buf[i].name.decode(), launches=buf[i].launches, ms=buf[i].ms, flops=buf[i].flops,
+                     bytes=buf[i].bytes) for i in range(n.value)]
+
+    @staticmethod
+    def flops(T: int) -> float:
+        return float(load().itts_vocoder_flops(int(T)))

@@ -122,3 +122,36 @@ def test_workloads_deterministic():
     vl, pl, noise, px, cond, style = W.pad_batch(a[:2], 1536)
     assert noise.shape == (2, 1536, 80) and np.all(noise[0, a[0].T:] == 0)
     assert np.array_equal(px[1, : a[1].P], a[1].prompt) and np.all(px[1, a[1].P:] == 0)
+
+
+def test_vocoder_create_fails_loudly_without_gpu_or_bundle(tmp_path):
+    """No CPU fallback for the vocoder either."""
+    import itts_cfm
+
+    with pytest.raises(itts_cfm.IttsError) as e:
+        itts_cfm.Vocoder(tmp_path / "missing", device=0)
+    assert e.value.code in (itts_cfm.ITTS_ECUDA, itts_cfm.ITTS_ENODEV, itts_cfm.ITTS_EBUNDLE)
+
+
+def test_vocoder_flops_matches_layer_count():
+    import itts_cfm
+
+    def macs(T):
+        m, t = T * 80 * 1536 * 7, T
+        for cin, cout, k, s, _ in mit2.BIGVGAN_UPSAMPLERS:
+            m += t * cin * cout * k
+            t *= s
+            m += sum(3 * 2 * t * cout * cout * kk for kk in mit2.BIGVGAN_RESBLOCK_KERNELS)
+        return 2.0 * (m + t * 24 * 7)
+
+    for T in (1, 3, 800):
+        assert abs(itts_cfm.Vocoder.flops(T) - macs(T)) / macs(T) < 1e-12
+
+
+def test_bigvgan_tensor_specs_complete():
+    specs = mit2.bigvgan_tensor_specs()
+    names = [n for n, _, _ in specs]
+    assert len(names) == len(set(names)) == 783
+    assert "bigvgan.resblocks.17.convs2.2.weight_v" in names and "bigvgan.conv_post.weight_v" in names
+    f = mit2.kaiser_sinc_lowpass(0.25, 0.3)
+    assert f.shape == (12,) and abs(float(f.sum()) - 1.0) < 1e-6 and np.allclose(f, f[::-1])
