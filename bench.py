@@ -42,6 +42,8 @@ import workloads  # noqa: E402
 METRIC = "mel frames/s, 25-step CFG DiT CFM at 1/2/4/8 B200; ms per CFM step"
 UNIT = "mel frames/s"
 BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_seed0_baseline"
+VOC_BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_bigvgan_seed0"
+VOC_REF_FRAMES = 4  # mel frames per reference CPU vocoder call in the baseline sample
 REF_SAMPLE_FRAMES = 32
 
 
@@ -176,6 +178,112 @@ def _host_threads() -> int:
     return max(1, min(n, 64))
 
 
+def cpu_vocoder_rate(threads: int):
+    """The reference's run_bigvgan_vocoder_cpu on `threads` host threads at
+    once, each on a VOC_REF_FRAMES-frame mel: mel frames/s and the wall time."""
+    import oracle
+
+    ref = oracle.RefOracle(VOC_BUNDLE_DIR)
+    mel = np.random.default_rng(4).standard_normal((VOC_REF_FRAMES, 80)).astype(np.float32)
+    errs = []
+
+    def work():
+        try:
+            ref.vocoder(mel)
+        except Exception as e:  # pragma: no cover
+            errs.append(e)
+
+    ths = [threading.Thread(target=work) for _ in range(threads)]
+    t0 = time.perf_counter()
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    dt = time.perf_counter() - t0
+    if errs:
+        raise errs[0]
+    return threads * VOC_REF_FRAMES / dt, dt
+
+
+def vocoder_line(args, cfg, rank, world, local, barrier, max_over_ranks, peak, hbm_peak):
+    """BigVGAN vocoder throughput on this rank's generated mel rows (T - P of
+    the workload's utterance): device-timed graph replays, e2e through
+    itts_vocoder_run with pinned host buffers, per-kind profile, roofline of
+    the conv GEMMs and of the activation kernel, and the reference CPU vocoder."""
+    import ctypes as C
+
+    import torch
+
+    import itts_cfm
+
+    if rank == 0 or world == 1:
+        mit2.make_vocoder_bundle(VOC_BUNDLE_DIR, seed=0)
+    barrier()
+    Tv = cfg["T"] - cfg["P"]
+    mel = np.random.default_rng(1000 + rank).standard_normal((Tv, 80)).astype(np.float32)
+    voc = itts_cfm.Vocoder(VOC_BUNDLE_DIR, device=local)
+    voc.stage(mel)
+    for _ in range(3):
+        voc.launch()
+    voc.fetch()
+    st = torch.cuda.ExternalStream(voc.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nv = 10
+    barrier()
+    e0.record(st)
+    for _ in range(nv):
+        voc.launch()
+    e1.record(st)
+    e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / nv
+    pin = torch.from_numpy(mel).pin_memory().numpy()
+    wave = torch.empty(Tv * itts_cfm.VOCODER_HOP, dtype=torch.float32).pin_memory().numpy()
+    lib = itts_cfm.load()
+
+    def e2e_once():
+        rc = lib.itts_vocoder_run(voc.h, pin.ctypes.data_as(C.c_void_p), Tv, wave.ctypes.data_as(C.c_void_p))
+        if rc != 0:
+            raise RuntimeError(lib.itts_vocoder_last_error(voc.h).decode())
+
+    e2e_once()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(nv):
+        e2e_once()
+    t_e2e = max_over_ranks(time.perf_counter() - t0) / nv
+    prof = sorted(voc.profile(2), key=lambda d: -d["ms"])
+    gem = [d for d in prof if d["name"].startswith(("upsample", "resblock_conv", "conv_pre"))]
+    act = [d for d in prof if d["name"].startswith("snake_aa")]
+    g_ms = sum(d["ms"] for d in gem)
+    a_ms = sum(d["ms"] for d in act)
+    g_ach = sum(d["flops"] for d in gem) / (g_ms / 1e3) / 1e12
+    a_ach = sum(d["bytes"] for d in act) / (a_ms / 1e3) / 1e9
+    launches = voc.launch_kernels()
+    voc.close()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        if oracle.ref_available():
+            threads = max(1, min(_host_threads(), 16))
+            fps, t = cpu_vocoder_rate(threads)
+            cpu = {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": f"{threads} threads, each one run_bigvgan_vocoder_cpu call on a {VOC_REF_FRAMES}-frame "
+                             f"mel; {t:.2f} s"}
+    return {"metric": "BigVGAN vocoder mel frames/s (mel -> 256 samples per frame)",
+            "value": Tv * world / (ms / 1e3), "unit": UNIT, "T": Tv, "ms_per_utterance": ms,
+            "tflops": itts_cfm.Vocoder.flops(Tv) / (ms / 1e3) / 1e12, "gpu_launches": launches,
+            "e2e": {"value": Tv * world / t_e2e, "unit": UNIT, "h2d_bytes_per_step": int(mel.nbytes),
+                    "d2h_bytes_per_step": int(wave.nbytes)},
+            "roofline": {"conv_gemm": {"bound": "tensor", "achieved": g_ach, "peak": peak, "unit": "TFLOP/s",
+                                       "frac": g_ach / peak},
+                         "snake_activation": {"bound": "hbm", "achieved": a_ach, "peak": hbm_peak, "unit": "GB/s",
+                                              "frac": a_ach / hbm_peak}},
+            "cpu_baseline": cpu,
+            "kernels": [kernel_row(d, 2) for d in prof]}
+
+
 def cpu_reference_rate(u, steps_cfm: int, threads: int, reps: int = 1):
     import oracle
 
@@ -235,6 +343,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batched", type=int, default=64,
                     help="also time a padded batch of this many utterances per GPU (0 = skip)")
+    ap.add_argument("--vocoder", type=int, default=1, help="also time the BigVGAN vocoder (0 = skip)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -387,6 +496,11 @@ def main():
                    "gemm_tflops": b_ach, "gemm_frac": b_ach / peak,
                    "kernels": [kernel_row(d, 2) for d in bprof]}
 
+    vocoder = None
+    if args.vocoder:
+        vocoder = vocoder_line(args, cfg, rank, world, local, barrier, max_over_ranks, peak,
+                               float(peaks.get("hbm_gbs", 6546.0)))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
@@ -418,6 +532,7 @@ def main():
             "cpu_baseline": cpu,
             "clocks": clk,
             "batched": batched,
+            "vocoder": vocoder,
         }
         print(json.dumps(line))
     if dist is not None:

@@ -68,4 +68,32 @@ inline std::vector<float> run_dit_estimator_step_cuda(CudaCfmContext& ctx, const
   return vel;
 }
 
+// BigVGAN vocoder context (itts_vocoder_create): one per (thread, GPU).
+class CudaVocoderContext {
+ public:
+  explicit CudaVocoderContext(const std::string& bundle_dir, int device = 0) {
+    const int rc = itts_vocoder_create(bundle_dir.c_str(), device, &h_);
+    if (rc != ITTS_OK) throw std::runtime_error(std::string("itts_vocoder_create: ") + itts_vocoder_create_error());
+  }
+  ~CudaVocoderContext() { itts_vocoder_destroy(h_); }
+  CudaVocoderContext(const CudaVocoderContext&) = delete;
+  CudaVocoderContext& operator=(const CudaVocoderContext&) = delete;
+  itts_vocoder_ctx* get() const { return h_; }
+
+ private:
+  itts_vocoder_ctx* h_ = nullptr;
+};
+
+// Drop-in for run_bigvgan_vocoder_metal (runtime/impl/dit_cfm_bigvgan.cpp:4196):
+// mel [tokens, 80] -> waveform [256 tokens] in [-1, 1].
+inline std::vector<float> run_bigvgan_vocoder_cuda(CudaVocoderContext& ctx, std::vector<float> mel, uint32_t tokens) {
+  if (mel.size() != static_cast<size_t>(tokens) * 80) throw std::runtime_error("run_bigvgan_vocoder_cuda: mel size mismatch");
+  std::vector<float> wave(static_cast<size_t>(tokens) * 256);
+  const int rc = itts_vocoder_run(ctx.get(), mel.data(), tokens, wave.data());
+  if (rc != ITTS_OK)
+    throw std::runtime_error(std::string("run_bigvgan_vocoder_cuda: ") + itts_cfm_strerror(rc) + ": " +
+                             itts_vocoder_last_error(ctx.get()));
+  return wave;
+}
+
 }  // namespace itts

@@ -636,11 +636,11 @@ void Vocoder::enqueue(Plan* p, std::vector<KernelTiming>* prof) {
                          static_cast<double>(cv.cout) * cv.taps * cv.cin_pad * 2.0;
     P.run(name, flops, bytes, [&] { check(gemm_run(g, stream_), name); });
   };
-  auto A = [&](const VocAct& a, const float* x, int tg, void* out, int ldo, bool f16) {
+  auto A = [&](const char* name, const VocAct& a, const float* x, int tg, void* out, int ldo, bool f16) {
     const int cw = f16 ? ldo : a.c;  // columns written (the f16 operand's padding as zeros)
     const dim3 grid((tg + kActTT - 1) / kActTT, (cw + kActCC - 1) / kActCC);
     const double bytes = static_cast<double>(tg) * a.c * (4.0 + (f16 ? 2.0 : 4.0));
-    P.run("snake_aa", 0.0, bytes, [&] {
+    P.run(name, 0.0, bytes, [&] {
       if (f16) {
         snake_aa_kernel<true><<<grid, 256, 0, stream_>>>(x, a.c, tg, a.c, cw, a.alpha, a.inv_beta, a.up, a.down, out, ldo);
       } else {
@@ -657,15 +657,17 @@ void Vocoder::enqueue(Plan* p, std::vector<KernelTiming>* prof) {
   int tg = T;
   for (int i = 0; i < 6; ++i) {
     const VocStage& s = st_[i];
-    for (int r = 0; r < s.s; ++r) G("upsample", p->ups[i][r], s.phase[r]);
+    const std::string sg = "." + std::to_string(i);  // profile names per stage
+    const std::string n_up = "upsample" + sg, n_conv = "resblock_conv" + sg, n_act = "snake_aa" + sg;
+    for (int r = 0; r < s.s; ++r) G(n_up.c_str(), p->ups[i][r], s.phase[r]);
     tg *= s.s;
     const int C = s.cout, cp = pad64(C);
     for (int j = 0; j < 3; ++j) {
       for (int q = 0; q < 3; ++q) {
-        A(s.act[j][2 * q], q == 0 ? p->y32 : p->xr32, tg, p->a16, cp, true);
-        G("resblock_conv", p->c1[i][j][q], s.conv1[j][q]);
-        A(s.act[j][2 * q + 1], p->h32, tg, p->a16, cp, true);
-        G("resblock_conv", p->c2[i][j][q], s.conv2[j][q]);
+        A(n_act.c_str(), s.act[j][2 * q], q == 0 ? p->y32 : p->xr32, tg, p->a16, cp, true);
+        G(n_conv.c_str(), p->c1[i][j][q], s.conv1[j][q]);
+        A(n_act.c_str(), s.act[j][2 * q + 1], p->h32, tg, p->a16, cp, true);
+        G(n_conv.c_str(), p->c2[i][j][q], s.conv2[j][q]);
       }
       // The last mean also writes in16, the next upsampler's operand (its
       // input channel padding pad64(C) is this stage's cp).
@@ -678,7 +680,7 @@ void Vocoder::enqueue(Plan* p, std::vector<KernelTiming>* prof) {
       });
     }
   }
-  A(post_act_, p->acc32, tg, p->h32, 24, false);
+  A("snake_aa.post", post_act_, p->acc32, tg, p->h32, 24, false);
   P.run("conv_post", 2.0 * tg * 24 * 7, tg * (24.0 * 4 + 4.0), [&] {
     conv_post_kernel<<<(tg + 255) / 256, 256, 0, stream_>>>(p->h32, tg, post_w_, p->wave);
     check(cudaGetLastError(), "conv_post");
