@@ -344,6 +344,8 @@ def main():
     ap.add_argument("--batched", type=int, default=64,
                     help="also time a padded batch of this many utterances per GPU (0 = skip)")
     ap.add_argument("--vocoder", type=int, default=1, help="also time the BigVGAN vocoder (0 = skip)")
+    ap.add_argument("--vocoder-only", action="store_true",
+                    help="time only the BigVGAN vocoder and print its line (profiling aid)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -378,10 +380,21 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    cfg = workloads.CONFIGS[args.workload]
+    if args.vocoder_only:
+        peaks, _ = measured_peaks()
+        v = vocoder_line(args, cfg, rank, world, local, barrier, max_over_ranks,
+                         float(peaks.get("bf16_tflops", 1590.0)), float(peaks.get("hbm_gbs", 6546.0)))
+        if rank == 0:
+            print(json.dumps(dict(v, n_gpus=world, higher_is_better=True, scaling="weak", data="synthetic",
+                                  dtype="f16", config={"workload": f"BigVGAN vocoder on the {v['T']} generated mel "
+                                                                   f"rows of a config-{args.workload} utterance"})))
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
     if rank == 0 or world == 1:
         mit2.make_dit_bundle(BUNDLE_DIR, seed=0, init="baseline")
     barrier()
-    cfg = workloads.CONFIGS[args.workload]
     B = args.utts or (1 if args.workload == 2 else 64)
     utts = workloads.config_utterances(args.workload, n=B, seed_offset=rank * 1000)
     T = cfg["T"]

@@ -60,17 +60,22 @@ __device__ __forceinline__ float snake(float u, float a, float ib) {
   return fmaf(s * s, ib, u);
 }
 
+// The two 12-tap filters travel by value (kernel parameters live in the
+// constant bank, which FMAs read as an operand without a load).
+struct SnakeFilters {
+  float up[12];
+  float down[12];
+};
+
 // Output columns [C, cw) (the f16 operand's channel padding) are written as 0;
 // a block whose 32 channels are all padding only writes those zeros.
 template <bool F16OUT>
 __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__ x, int ldx, int T, int C, int cw,
                                                        const float* __restrict__ alpha,
-                                                       const float* __restrict__ inv_beta,
-                                                       const float* __restrict__ up, const float* __restrict__ down,
+                                                       const float* __restrict__ inv_beta, const SnakeFilters f,
                                                        void* __restrict__ out, int ldo) {
   __shared__ float xs[kActTT + 12][kActCC];  // xs[i] = x[clamp(t0 - 6 + i)]
   __shared__ float vs[kActPos][kActCC];      // vs[i] = v(clamp(2 t0 - 6 + i))
-  __shared__ float fu[12], fd[12];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int t0 = blockIdx.x * kActTT;
   const int c = blockIdx.y * kActCC + lane;
@@ -83,8 +88,6 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
     }
     return;
   }
-  if (threadIdx.x < 12) fu[threadIdx.x] = up[threadIdx.x];
-  if (threadIdx.x >= 32 && threadIdx.x < 44) fd[threadIdx.x - 32] = down[threadIdx.x - 32];
   for (int i = w; i < kActTT + 12; i += 8) {
     int r = t0 - 6 + i;
     r = r < 0 ? 0 : (r > T - 1 ? T - 1 : r);
@@ -97,13 +100,13 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
   auto u_even = [&](int xi) {  // u(2m), xi = index of row m + 2
     float acc = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * fu[2 * i + 1];
+    for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * f.up[2 * i + 1];
     return 2.0f * acc;
   };
   auto u_odd = [&](int xi) {  // u(2m + 1), xi = index of row m + 3
     float acc = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * fu[2 * i];
+    for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * f.up[2 * i];
     return 2.0f * acc;
   };
   for (int q = w; q < kActPos / 2; q += 8) {
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
     if (t >= T) break;
     float acc = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 12; ++k) acc += win[2 * o + k] * fd[k];
+    for (int k = 0; k < 12; ++k) acc += win[2 * o + k] * f.down[k];
     if (!cok) acc = 0.0f;
     if constexpr (F16OUT) {
       static_cast<__half*>(out)[static_cast<size_t>(t) * ldo + c] = __float2half_rn(acc);
@@ -280,7 +283,7 @@ struct Pending {
 };
 struct PendingAct {
   VocAct* act;
-  size_t a_off, b_off, u_off, d_off;
+  size_t a_off, b_off;
 };
 
 }  // namespace
@@ -379,8 +382,11 @@ void Vocoder::load(const std::string& bundle_dir, bool verify_sha256) {
       be[i] = 1.0f / (std::exp(be[i]) + 1e-9f);
     }
     a->c = c;
-    pacts.push_back({a, ar.add(al), ar.add(be), ar.add(vec_of(b, prefix + ".upsample.filter", 12)),
-                     ar.add(vec_of(b, prefix + ".downsample.lowpass.filter", 12))});
+    const std::vector<float> fu = vec_of(b, prefix + ".upsample.filter", 12);
+    const std::vector<float> fd = vec_of(b, prefix + ".downsample.lowpass.filter", 12);
+    std::memcpy(a->up, fu.data(), sizeof(a->up));
+    std::memcpy(a->down, fd.data(), sizeof(a->down));
+    pacts.push_back({a, ar.add(al), ar.add(be)});
   };
   conv1d(&pre_, "bigvgan.conv_pre", 80, 1536, 7, 1, true);
   for (int i = 0; i < 6; ++i) {
@@ -436,8 +442,6 @@ void Vocoder::load(const std::string& bundle_dir, bool verify_sha256) {
   for (auto& p : pacts) {
     p.act->alpha = reinterpret_cast<const float*>(base + p.a_off);
     p.act->inv_beta = reinterpret_cast<const float*>(base + p.b_off);
-    p.act->up = reinterpret_cast<const float*>(base + p.u_off);
-    p.act->down = reinterpret_cast<const float*>(base + p.d_off);
   }
   post_w_ = reinterpret_cast<const float*>(base + post_off);
 }
@@ -640,11 +644,14 @@ void Vocoder::enqueue(Plan* p, std::vector<KernelTiming>* prof) {
     const int cw = f16 ? ldo : a.c;  // columns written (the f16 operand's padding as zeros)
     const dim3 grid((tg + kActTT - 1) / kActTT, (cw + kActCC - 1) / kActCC);
     const double bytes = static_cast<double>(tg) * a.c * (4.0 + (f16 ? 2.0 : 4.0));
+    SnakeFilters filt;
+    std::memcpy(filt.up, a.up, sizeof(filt.up));
+    std::memcpy(filt.down, a.down, sizeof(filt.down));
     P.run(name, 0.0, bytes, [&] {
       if (f16) {
-        snake_aa_kernel<true><<<grid, 256, 0, stream_>>>(x, a.c, tg, a.c, cw, a.alpha, a.inv_beta, a.up, a.down, out, ldo);
+        snake_aa_kernel<true><<<grid, 256, 0, stream_>>>(x, a.c, tg, a.c, cw, a.alpha, a.inv_beta, filt, out, ldo);
       } else {
-        snake_aa_kernel<false><<<grid, 256, 0, stream_>>>(x, a.c, tg, a.c, cw, a.alpha, a.inv_beta, a.up, a.down, out, ldo);
+        snake_aa_kernel<false><<<grid, 256, 0, stream_>>>(x, a.c, tg, a.c, cw, a.alpha, a.inv_beta, filt, out, ldo);
       }
       check(cudaGetLastError(), "snake activation");
     });

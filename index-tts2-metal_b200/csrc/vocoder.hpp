@@ -38,8 +38,8 @@ struct VocConv {
 struct VocAct {
   const float* alpha = nullptr;     // [C] exp(alpha_log)
   const float* inv_beta = nullptr;  // [C] 1 / (exp(beta_log) + 1e-9)
-  const float* up = nullptr;        // [12]
-  const float* down = nullptr;      // [12]
+  float up[12] = {};                // anti-aliasing filters (host copies, passed to the kernel by value)
+  float down[12] = {};
   int c = 0;
 };
 
