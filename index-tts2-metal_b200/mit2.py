@@ -342,6 +342,50 @@ def make_vocoder_bundle(out_dir: str | Path, seed: int = 0) -> Path:
     return out
 
 
+LR_PREFIX = "s2mel.net.length_regulator."
+
+
+def length_regulator_tensor_specs() -> list[tuple[str, tuple[int, ...], str]]:
+    """(full name, shape, kind) of the length-regulator tensors
+    (runtime/impl/gpt.cpp:5271-5317): content_in_proj (1024 -> 512), four
+    {k=3 conv, one-group GroupNorm} blocks (model.0/1 .. 9/10), model.12 (k=1)."""
+    s = [(LR_PREFIX + "content_in_proj.weight", (512, 1024), "w"), (LR_PREFIX + "content_in_proj.bias", (512,), "b")]
+    for conv, norm in ((0, 1), (3, 4), (6, 7), (9, 10)):
+        s += [(f"{LR_PREFIX}model.{conv}.weight", (512, 512, 3), "w"), (f"{LR_PREFIX}model.{conv}.bias", (512,), "b"),
+              (f"{LR_PREFIX}model.{norm}.weight", (512,), "gamma"), (f"{LR_PREFIX}model.{norm}.bias", (512,), "b")]
+    s += [(LR_PREFIX + "model.12.weight", (512, 512, 1), "w"), (LR_PREFIX + "model.12.bias", (512,), "b")]
+    return s
+
+
+def make_length_regulator_tensors(seed: int) -> list[tuple[str, np.ndarray]]:
+    """Deterministic synthetic length-regulator weights (f16): weights
+    N(0, 1/fan_in), biases N(0, 0.02), GroupNorm gamma 1 + N(0, 0.1)."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for name, shape, kind in length_regulator_tensor_specs():
+        if kind == "w":
+            arr = rng.standard_normal(shape, dtype=np.float32) / math.sqrt(int(np.prod(shape[1:])))
+        elif kind == "b":
+            arr = rng.standard_normal(shape, dtype=np.float32) * 0.02
+        else:
+            arr = 1.0 + rng.standard_normal(shape, dtype=np.float32) * 0.1
+        out.append((name, arr.astype(np.float16)))
+    return out
+
+
+def make_condition_bundle(out_dir: str | Path, seed: int = 0) -> Path:
+    """Write the synthetic length-regulator bundle; skips work when an identical one exists."""
+    out = Path(out_dir)
+    stamp = out / ".synthetic"
+    key = f"length_regulator seed={seed} v1"
+    if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():
+        return out
+    write_bundle(out, make_length_regulator_tensors(seed),
+                 metadata={"synthetic": True, "seed": seed, "model": "length_regulator"})
+    stamp.write_text(key)
+    return out
+
+
 def bundle_f32(bundle_dir: str | Path) -> dict[str, np.ndarray]:
     """All estimator tensors decoded to contiguous float32 (f16 decoding is exact)."""
     return {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in read_bundle(bundle_dir).items()}

@@ -78,6 +78,9 @@ static const float* VW(const voc_model* m, const char* name, size_t want) {
   return NULL;
 }
 
+/* Tensor lookup for the other stage oracles sharing this table. */
+const float* voc_lookup(const voc_model* m, const char* name, size_t want) { return VW(m, name, want); }
+
 static int v_err = 0;
 int voc_last_error(void) { return v_err; }
 

@@ -162,6 +162,45 @@ class VocoderOracle:
         return out
 
 
+class ConditionOracle:
+    """fp32 CPU restatement of the reference's length regulator and condition
+    merge (oracle/condition_oracle.c), over s2mel.net.length_regulator.* tensors."""
+
+    def __init__(self, tensors: dict[str, np.ndarray], lib_path: Path = PORT_LIB):
+        self.lib = C.CDLL(str(lib_path))
+        L = self.lib
+        L.voc_model_new.restype = C.c_void_p
+        L.voc_model_free.argtypes = [C.c_void_p]
+        L.voc_model_set.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]
+        L.cond_length_regulator.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.cond_assemble.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        self._keep = {k: _f32(v) for k, v in tensors.items() if k.startswith("s2mel.net.length_regulator.")}
+        self.m = C.c_void_p(L.voc_model_new())
+        for k, v in self._keep.items():
+            L.voc_model_set(self.m, k.encode(), _p(v), v.size)
+
+    def __del__(self):
+        try:
+            self.lib.voc_model_free(self.m)
+        except Exception:
+            pass
+
+    def length_regulator(self, x, n_out: int):
+        x = _f32(x)
+        out = np.empty((n_out, 512), np.float32)
+        if self.lib.cond_length_regulator(self.m, _p(x), x.shape[0], int(n_out), _p(out)):
+            raise RuntimeError(f"oracle length regulator failed (line {self.lib.cond_last_error()})")
+        return out
+
+    def assemble(self, x, prompt, G: int):
+        x, prompt = _f32(x), _f32(prompt)
+        P = prompt.shape[0]
+        out = np.empty((P + G, 512), np.float32)
+        if self.lib.cond_assemble(self.m, _p(x), x.shape[0], _p(prompt), P, int(G), _p(out)):
+            raise RuntimeError(f"oracle condition assembly failed (line {self.lib.cond_last_error()})")
+        return out
+
+
 def ref_available() -> bool:
     return REF_LIB.exists()
 
@@ -185,6 +224,7 @@ class RefOracle:
         L.ref_timestep_embed.argtypes = [C.c_char_p, C.c_float, C.c_int, C.c_void_p]
         L.ref_noise.argtypes = [C.c_uint32, C.c_uint32, C.c_uint64, C.c_float, C.c_void_p]
         L.ref_bigvgan_vocoder.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_void_p]
+        L.ref_length_regulator.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
         L.ref_bigvgan_activation.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
 
     def _ok(self, rc):
@@ -239,6 +279,12 @@ class RefOracle:
     def noise(self, T, C_, seed, temperature=1.0):
         out = np.empty((T, C_), np.float32)
         self._ok(self.lib.ref_noise(T, C_, seed, temperature, _p(out)))
+        return out
+
+    def length_regulator(self, x, n_out: int):
+        x = _f32(x)
+        out = np.empty((n_out, 512), np.float32)
+        self._ok(self.lib.ref_length_regulator(self.dir, _p(x), x.shape[0], int(n_out), _p(out)))
         return out
 
     def vocoder(self, mel):

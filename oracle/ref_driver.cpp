@@ -32,6 +32,8 @@ std::vector<float> run_timestep_embedder_cpu(const mit2::Bundle& bundle, const s
 std::vector<float> make_deterministic_normal_noise(uint32_t tokens, uint32_t channels, uint64_t seed,
                                                    float temperature);
 std::vector<float> run_bigvgan_vocoder_cpu(const mit2::Bundle& bundle, std::vector<float> mel, uint32_t tokens);
+std::vector<float> run_length_regulator_full_cpu(const mit2::Bundle& bundle, const std::vector<float>& input,
+                                                 uint32_t in_tokens, uint32_t out_tokens);
 std::vector<float> run_bigvgan_activation_cpu(const mit2::Bundle& bundle, const std::string& prefix,
                                               const std::vector<float>& x, uint32_t tokens, uint32_t channels);
 
@@ -143,6 +145,15 @@ int ref_timestep_embed(const char* bundle_dir, float t, int which, float* out) {
 int ref_noise(uint32_t T, uint32_t C, uint64_t seed, float temperature, float* out) {
   return guard([&] {
     auto v = make_deterministic_normal_noise(T, C, seed, temperature);
+    std::memcpy(out, v.data(), v.size() * sizeof(float));
+  });
+}
+
+// run_length_regulator_full_cpu: s_infer [n_in,1024] -> [n_out,512].
+int ref_length_regulator(const char* bundle_dir, const float* x, uint32_t n_in, uint32_t n_out, float* out) {
+  return guard([&] {
+    mit2::Bundle b(bundle_dir);
+    auto v = run_length_regulator_full_cpu(b, vec(x, static_cast<size_t>(n_in) * 1024), n_in, n_out);
     std::memcpy(out, v.data(), v.size() * sizeof(float));
   });
 }

@@ -80,6 +80,18 @@ def port_vocoder(vocoder_tensors):
     return oracle.VocoderOracle(vocoder_tensors)
 
 
+@pytest.fixture(scope="session")
+def condition_bundle() -> Path:
+    return mit2.make_condition_bundle(BUNDLE_ROOT / "length_regulator_seed0", seed=0)
+
+
+@pytest.fixture(scope="session")
+def port_condition(condition_bundle):
+    import oracle
+
+    return oracle.ConditionOracle(mit2.bundle_f32(condition_bundle))
+
+
 def _gpu_ctx(bundle):
     import itts_cfm
 

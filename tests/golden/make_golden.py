@@ -23,7 +23,11 @@ Cases (inputs follow the reference's self-tests where it has them):
                     and two anti-aliased SnakeBeta activations (768 and 24
                     channels) on seeded inputs, synthetic vocoder bundle seed 0
 
-    python tests/golden/make_golden.py [--only bigvgan]
+  kat_length_regulator  run_length_regulator_full_cpu on its self-test input
+                    (run_length_regulator_full_test: 7 -> 11 frames) and on a
+                    seeded 40 -> 63 case, synthetic length-regulator bundle seed 0
+
+    python tests/golden/make_golden.py [--only bigvgan|lr]
 """
 from __future__ import annotations
 
@@ -86,12 +90,30 @@ def bigvgan_cases():
                         weights_sha256=weights_sha(voc))
 
 
+def length_regulator_cases():
+    lrb = mit2.make_condition_bundle(ROOT / "length_regulator_seed0", seed=0)
+    r = oracle.RefOracle(lrb)
+    # run_length_regulator_full_test inputs (runtime/impl/gpt.cpp:5382-5390)
+    i = np.arange(7 * 1024, dtype=np.float32)
+    x7 = f32(np.sin(i * np.float32(0.017)) * np.float32(0.1) +
+             np.cos((np.arange(7 * 1024) % 131).astype(np.float32) * np.float32(0.013)) * np.float32(0.2)).reshape(7, 1024)
+    x40 = f32(np.random.default_rng(12).standard_normal((40, 1024)))
+    np.savez_compressed(HERE / "kat_length_regulator.npz", x7=x7, out7_11=r.length_regulator(x7, 11), x40=x40,
+                        out40_63=r.length_regulator(x40, 63), bundle_seed=0, weights_sha256=weights_sha(lrb))
+
+
 def main():
-    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "bigvgan":
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only == "bigvgan":
         bigvgan_cases()
         print("golden vectors written to", HERE)
         return
+    if only == "lr":
+        length_regulator_cases()
+        print("golden vectors written to", HERE)
+        return
     bigvgan_cases()
+    length_regulator_cases()
     unit = mit2.make_dit_bundle(ROOT / "seed0_unit", seed=0, init="unit")
     base = mit2.make_dit_bundle(ROOT / "seed0_baseline", seed=0, init="baseline")
     ru, rb = oracle.RefOracle(unit), oracle.RefOracle(base)

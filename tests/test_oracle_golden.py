@@ -1,4 +1,5 @@
-"""Pin the CPU oracles (oracle/dit_oracle.c, oracle/bigvgan_oracle.c) to the reference's own CPU
+"""Pin the CPU oracles (oracle/dit_oracle.c, oracle/bigvgan_oracle.c,
+oracle/condition_oracle.c) to the reference's own CPU
 functions through the committed golden vectors (tests/golden/, made by
 tests/golden/make_golden.py from oracle/_ref). fp32 vs fp32 with a different
 summation order: the reference's own unit tolerance ladder applies (1e-4
@@ -132,3 +133,22 @@ def test_bigvgan_oracle_detects_planted_error(vocoder_tensors):
     bad[k][5] *= -1.0
     with pytest.raises(AssertionError):
         _close(g["wave"], O.VocoderOracle(bad).vocoder(g["mel"]))
+
+
+def test_length_regulator_bundle_matches_golden_generator(condition_bundle):
+    assert _sha(condition_bundle) == str(_load("kat_length_regulator")["weights_sha256"])
+
+
+def test_length_regulator(port_condition):
+    g = _load("kat_length_regulator")
+    _close(g["out7_11"], port_condition.length_regulator(g["x7"], 11))
+    _close(g["out40_63"], port_condition.length_regulator(g["x40"], 63))
+
+
+def test_condition_merge_places_prompt_rows_first(port_condition):
+    g = _load("kat_length_regulator")
+    prompt = np.random.default_rng(5).standard_normal((4, 512)).astype(np.float32)
+    cond = port_condition.assemble(g["x7"], prompt, 11)
+    assert cond.shape == (15, 512)
+    assert np.array_equal(cond[:4], prompt)
+    _close(g["out7_11"], cond[4:])
