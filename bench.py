@@ -44,6 +44,8 @@ UNIT = "mel frames/s"
 BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_seed0_baseline"
 VOC_BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_bigvgan_seed0"
 VOC_REF_FRAMES = 4  # mel frames per reference CPU vocoder call in the baseline sample
+COND_BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_length_regulator_seed0"
+COND_SEM_PER_MEL = 175 / 600  # semantic frames per generated mel frame in the condition workload
 REF_SAMPLE_FRAMES = 32
 
 
@@ -284,6 +286,81 @@ def vocoder_line(args, cfg, rank, world, local, barrier, max_over_ranks, peak, h
             "kernels": [kernel_row(d, 2) for d in prof]}
 
 
+def condition_line(args, cfg, rank, world, local, barrier, max_over_ranks):
+    """Condition assembly (length regulator + merge) for this rank's utterance:
+    s_infer of round(G * 175/600) semantic frames -> G = T - P generated rows
+    after the P prompt rows. Device-timed graph replays, e2e through
+    itts_cond_assemble, and the reference CPU length regulator."""
+    import ctypes as C
+
+    import torch
+
+    import itts_cfm
+
+    if rank == 0 or world == 1:
+        mit2.make_condition_bundle(COND_BUNDLE_DIR, seed=0)
+    barrier()
+    P, G = cfg["P"], cfg["T"] - cfg["P"]
+    n_in = max(1, round(G * COND_SEM_PER_MEL))
+    rng = np.random.default_rng(2000 + rank)
+    s_infer = rng.standard_normal((n_in, 1024)).astype(np.float32)
+    prompt = rng.standard_normal((P, 512)).astype(np.float32)
+    ca = itts_cfm.ConditionAssembler(COND_BUNDLE_DIR, device=local)
+    ca.stage(s_infer, prompt, G)
+    for _ in range(3):
+        ca.launch()
+    ca.fetch()
+    st = torch.cuda.ExternalStream(ca.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nv = 20
+    barrier()
+    e0.record(st)
+    for _ in range(nv):
+        ca.launch()
+    e1.record(st)
+    e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / nv
+    ps = torch.from_numpy(s_infer).pin_memory().numpy()
+    pp = torch.from_numpy(prompt).pin_memory().numpy()
+    out = torch.empty((P + G, 512), dtype=torch.float32).pin_memory().numpy()
+    lib = itts_cfm.load()
+
+    def e2e_once():
+        rc = lib.itts_cond_assemble(ca.h, ps.ctypes.data_as(C.c_void_p), n_in, pp.ctypes.data_as(C.c_void_p), P, G,
+                                    out.ctypes.data_as(C.c_void_p))
+        if rc != 0:
+            raise RuntimeError(lib.itts_cond_last_error(ca.h).decode())
+
+    e2e_once()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(nv):
+        e2e_once()
+    t_e2e = max_over_ranks(time.perf_counter() - t0) / nv
+    launches = ca.launch_kernels()
+    ca.close()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        if oracle.ref_available():
+            ref = oracle.RefOracle(COND_BUNDLE_DIR)
+            g_s, n_s = 64, max(1, round(64 * COND_SEM_PER_MEL))
+            t0 = time.perf_counter()
+            ref.length_regulator(s_infer[:n_s], g_s)
+            dt = time.perf_counter() - t0
+            cpu = {"value": g_s / dt, "unit": "generated mel frames/s", "cores": 1, "kind": "reference",
+                   "sample": f"one run_length_regulator_full_cpu call, {n_s} -> {g_s} frames; {dt:.2f} s"}
+    return {"metric": "condition assembly, generated mel frames/s (length regulator + prompt merge)",
+            "value": G * world / (ms / 1e3), "unit": "generated mel frames/s", "n_in": n_in, "P": P, "G": G,
+            "ms_per_utterance": ms, "tflops": itts_cfm.ConditionAssembler.flops(n_in, G) / (ms / 1e3) / 1e12,
+            "gpu_launches": launches,
+            "e2e": {"value": G * world / t_e2e, "unit": "generated mel frames/s",
+                    "h2d_bytes_per_step": int(s_infer.nbytes + prompt.nbytes), "d2h_bytes_per_step": int(out.nbytes)},
+            "cpu_baseline": cpu}
+
+
 def cpu_reference_rate(u, steps_cfm: int, threads: int, reps: int = 1):
     import oracle
 
@@ -344,6 +421,8 @@ def main():
     ap.add_argument("--batched", type=int, default=64,
                     help="also time a padded batch of this many utterances per GPU (0 = skip)")
     ap.add_argument("--vocoder", type=int, default=1, help="also time the BigVGAN vocoder (0 = skip)")
+    ap.add_argument("--condition", type=int, default=1,
+                    help="also time the condition assembly before the sampler (0 = skip)")
     ap.add_argument("--vocoder-only", action="store_true",
                     help="time only the BigVGAN vocoder and print its line (profiling aid)")
     args = ap.parse_args()
@@ -509,6 +588,10 @@ def main():
                    "gemm_tflops": b_ach, "gemm_frac": b_ach / peak,
                    "kernels": [kernel_row(d, 2) for d in bprof]}
 
+    condition = None
+    if args.condition:
+        condition = condition_line(args, cfg, rank, world, local, barrier, max_over_ranks)
+
     vocoder = None
     if args.vocoder:
         vocoder = vocoder_line(args, cfg, rank, world, local, barrier, max_over_ranks, peak,
@@ -545,6 +628,7 @@ def main():
             "cpu_baseline": cpu,
             "clocks": clk,
             "batched": batched,
+            "condition": condition,
             "vocoder": vocoder,
         }
         print(json.dumps(line))

@@ -260,6 +260,40 @@ int itts_vocoder_profile(itts_vocoder_ctx* ctx, int reps, itts_kernel_stat* out,
 /* Algorithmic FLOPs of one pass over T mel frames (conv MACs x 2). */
 double itts_vocoder_flops(uint32_t T);
 
+/* ------------------------------------------------------------------------
+ * Condition assembly (the step right before the sampler): the S2Mel length
+ * regulator on s_infer [n_in,1024] (GPT layer + VQ embedding, token-major) to
+ * G frames, placed after the voice prompt's P condition rows:
+ * cond [P+G,512] = [prompt_cond ; length_regulator(s_infer, G)]. Replaces
+ * run_length_regulator_full_metal (runtime/impl/gpt.cpp:5319-5357; CPU twin
+ * :5298-5317) followed by MetalContext::hot_condition_merge_f32
+ * (runtime/metal_context.mm:2207-2257; kernel metal/kernels.metal:843-864),
+ * as run at runtime/impl/tts_synthesis/synthesis_pipeline.cpp:1030-1034.
+ * ------------------------------------------------------------------------ */
+typedef struct itts_cond_ctx itts_cond_ctx;
+
+/* Loads the bundle's s2mel.net.length_regulator.* tensors onto `device`. */
+int itts_cond_create(const char* bundle_dir, int device, itts_cond_ctx** out);
+void itts_cond_destroy(itts_cond_ctx* ctx);
+const char* itts_cond_last_error(const itts_cond_ctx* ctx);
+const char* itts_cond_create_error(void);
+
+/* Host s_infer [n_in,1024] f32, prompt_cond [P,512] f32 (may be NULL when
+ * P = 0) -> host cond [P+G,512] f32. The first call for a shape (n_in, P, G)
+ * builds its workspace and CUDA graph. */
+int itts_cond_assemble(itts_cond_ctx* ctx, const float* s_infer, uint32_t n_in, const float* prompt_cond, uint32_t P,
+                       uint32_t G, float* cond);
+
+/* The pieces of itts_cond_assemble for timing (no reference counterpart). */
+int itts_cond_stage(itts_cond_ctx* ctx, const float* s_infer, uint32_t n_in, const float* prompt_cond, uint32_t P,
+                    uint32_t G);
+int itts_cond_launch(itts_cond_ctx* ctx);
+int itts_cond_fetch(itts_cond_ctx* ctx, float* cond);
+void* itts_cond_stream(itts_cond_ctx* ctx);
+int itts_cond_launch_kernels(itts_cond_ctx* ctx);
+/* Algorithmic FLOPs of one length-regulator pass (GEMM MACs x 2). */
+double itts_cond_flops(uint32_t n_in, uint32_t G);
+
 #ifdef __cplusplus
 }
 #endif

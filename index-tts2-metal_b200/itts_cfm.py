@@ -33,6 +33,9 @@ EXPORTED = [
     "itts_vocoder_create", "itts_vocoder_destroy", "itts_vocoder_last_error", "itts_vocoder_create_error",
     "itts_vocoder_run", "itts_vocoder_stage", "itts_vocoder_launch", "itts_vocoder_fetch", "itts_vocoder_stream",
     "itts_vocoder_launch_kernels", "itts_vocoder_profile", "itts_vocoder_flops",
+    "itts_cond_create", "itts_cond_destroy", "itts_cond_last_error", "itts_cond_create_error", "itts_cond_assemble",
+    "itts_cond_stage", "itts_cond_launch", "itts_cond_fetch", "itts_cond_stream", "itts_cond_launch_kernels",
+    "itts_cond_flops",
 ]
 VOCODER_HOP = 256
 VOCODER_MAX_T = 16384
@@ -105,6 +108,17 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_vocoder_launch_kernels": (i32, [vp]),
         "itts_vocoder_profile": (i32, [vp, i32, vp, i32, C.POINTER(i32)]),
         "itts_vocoder_flops": (f64, [u32]),
+        "itts_cond_create": (i32, [C.c_char_p, i32, C.POINTER(vp)]),
+        "itts_cond_destroy": (None, [vp]),
+        "itts_cond_last_error": (C.c_char_p, [vp]),
+        "itts_cond_create_error": (C.c_char_p, []),
+        "itts_cond_assemble": (i32, [vp, vp, u32, vp, u32, u32, vp]),
+        "itts_cond_stage": (i32, [vp, vp, u32, vp, u32, u32]),
+        "itts_cond_launch": (i32, [vp]),
+        "itts_cond_fetch": (i32, [vp, vp]),
+        "itts_cond_stream": (vp, [vp]),
+        "itts_cond_launch_kernels": (i32, [vp]),
+        "itts_cond_flops": (f64, [u32, u32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -357,3 +371,84 @@ class Vocoder:
     @staticmethod
     def flops(T: int) -> float:
         return float(load().itts_vocoder_flops(int(T)))
+
+
+class ConditionAssembler:
+    """Length regulator + condition merge bound to one GPU (itts_cond_create):
+    s_infer [n_in, 1024], prompt_cond [P, 512] -> cond [P + G, 512]."""
+
+    def __init__(self, bundle_dir: str | Path, device: int = 0):
+        self.lib = load()
+        h = C.c_void_p()
+        rc = self.lib.itts_cond_create(str(bundle_dir).encode(), int(device), C.byref(h))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_cond_create_error().decode())
+        self.h = h
+        self.rows = 0
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.itts_cond_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int) -> None:
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_cond_last_error(self.h).decode())
+
+    @staticmethod
+    def _args(s_infer, prompt):
+        s_infer = _f32(s_infer)
+        if s_infer.ndim != 2 or s_infer.shape[1] != 1024:
+            raise ValueError("s_infer must be [n_in, 1024]")
+        prompt = None if prompt is None or len(prompt) == 0 else _f32(prompt)
+        if prompt is not None and (prompt.ndim != 2 or prompt.shape[1] != 512):
+            raise ValueError("prompt_cond must be [P, 512]")
+        return s_infer, prompt, 0 if prompt is None else prompt.shape[0]
+
+    def assemble(self, s_infer, prompt, G: int) -> np.ndarray:
+        s_infer, prompt, P = self._args(s_infer, prompt)
+        out = np.empty((P + int(G), 512), np.float32)
+        self._check(self.lib.itts_cond_assemble(self.h, _ptr(s_infer), s_infer.shape[0], _ptr(prompt), P, int(G),
+                                                _ptr(out)))
+        return out
+
+    def length_regulator(self, s_infer, G: int) -> np.ndarray:
+        return self.assemble(s_infer, None, G)
+
+    def stage(self, s_infer, prompt, G: int) -> None:
+        s_infer, prompt, P = self._args(s_infer, prompt)
+        self._check(self.lib.itts_cond_stage(self.h, _ptr(s_infer), s_infer.shape[0], _ptr(prompt), P, int(G)))
+        self.rows = P + int(G)
+
+    def launch(self) -> None:
+        self._check(self.lib.itts_cond_launch(self.h))
+
+    def fetch(self) -> np.ndarray:
+        out = np.empty((self.rows, 512), np.float32)
+        self._check(self.lib.itts_cond_fetch(self.h, _ptr(out)))
+        return out
+
+    def stream(self) -> int:
+        return int(self.lib.itts_cond_stream(self.h) or 0)
+
+    def launch_kernels(self) -> int:
+        n = int(self.lib.itts_cond_launch_kernels(self.h))
+        if n < 0:
+            raise IttsError(n, "nothing staged")
+        return n
+
+    @staticmethod
+    def flops(n_in: int, G: int) -> float:
+        return float(load().itts_cond_flops(int(n_in), int(G)))

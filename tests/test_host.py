@@ -155,3 +155,20 @@ def test_bigvgan_tensor_specs_complete():
     assert "bigvgan.resblocks.17.convs2.2.weight_v" in names and "bigvgan.conv_post.weight_v" in names
     f = mit2.kaiser_sinc_lowpass(0.25, 0.3)
     assert f.shape == (12,) and abs(float(f.sum()) - 1.0) < 1e-6 and np.allclose(f, f[::-1])
+
+
+def test_condition_create_fails_loudly_without_gpu_or_bundle(tmp_path):
+    import itts_cfm
+
+    with pytest.raises(itts_cfm.IttsError) as e:
+        itts_cfm.ConditionAssembler(tmp_path / "missing", device=0)
+    assert e.value.code in (itts_cfm.ITTS_ECUDA, itts_cfm.ITTS_ENODEV, itts_cfm.ITTS_EBUNDLE)
+
+
+def test_condition_flops_and_specs():
+    import itts_cfm
+
+    assert itts_cfm.ConditionAssembler.flops(175, 600) == 2.0 * (175 * 1024 * 512 + 4 * 600 * 512 * 512 * 3 + 600 * 512 * 512)
+    names = [n for n, _, _ in mit2.length_regulator_tensor_specs()]
+    assert len(names) == len(set(names)) == 20
+    assert names[0] == "s2mel.net.length_regulator.content_in_proj.weight"
