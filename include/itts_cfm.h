@@ -294,6 +294,36 @@ int itts_cond_launch_kernels(itts_cond_ctx* ctx);
 /* Algorithmic FLOPs of one length-regulator pass (GEMM MACs x 2). */
 double itts_cond_flops(uint32_t n_in, uint32_t G);
 
+/* ------------------------------------------------------------------------
+ * Bundle contract gates and the cached-voice loader (host only, no GPU, no
+ * context). Replace the reference's --inspect-voice-bundle / --inspect-model-
+ * bundle gates (inspect_voice_bundle_contract / inspect_model_bundle_contract,
+ * runtime/impl/tokenizer_tests.cpp:5699, 4776; rules docs/native_bundle.md:
+ * 55-112) and the voice reads of the synthesis pipeline
+ * (runtime/impl/tts_synthesis/synthesis_pipeline.cpp:1060-1084). Return ITTS_OK
+ * or ITTS_EBUNDLE; the gates write a JSON report ("ok": true/false, integrity
+ * counters, the required tensors or the error) into `report` (cap bytes, may
+ * be NULL).
+ * ------------------------------------------------------------------------ */
+#define ITTS_COMPONENT_CFM 0x1u              /* s2mel.net.cfm.estimator.* */
+#define ITTS_COMPONENT_LENGTH_REGULATOR 0x2u /* s2mel.net.length_regulator.* */
+#define ITTS_COMPONENT_BIGVGAN 0x4u          /* bigvgan.* */
+#define ITTS_COMPONENT_ALL 0x7u
+
+/* Voice gate: every payload's SHA-256 present and verified; f32 component=voice
+ * spk_cond_emb [1,S>0,1024], s2mel_style [1,192], s2mel_prompt [1,P>0,512],
+ * mel [1,80,P]. */
+int itts_inspect_voice_bundle(const char* bundle_dir, char* report, uint32_t cap);
+/* Model gate: every payload's SHA-256 present and verified; the sentinel
+ * tensors (name, shape, component) of each stage in `components`. */
+int itts_inspect_model_bundle(const char* bundle_dir, uint32_t components, char* report, uint32_t cap);
+/* Reads a voice bundle (after the voice gate's shape rules): *P_out = the
+ * prompt rows used (prompt_tokens, or all of the voice's when 0); then, for
+ * each non-NULL buffer, prompt_cond [P,512] (s2mel_prompt rows), style [192]
+ * and prompt_mel [P,80] (mel transposed from [1,80,T_voice]). */
+int itts_voice_load(const char* bundle_dir, uint32_t prompt_tokens, uint32_t* P_out, float* prompt_cond, float* style,
+                    float* prompt_mel, char* err, uint32_t err_cap);
+
 #ifdef __cplusplus
 }
 #endif

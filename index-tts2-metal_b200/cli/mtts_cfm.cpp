@@ -8,6 +8,10 @@
 //   mtts_cfm --cfm BUNDLE T P STEPS CFG IN_PREFIX OUT.f32 [DEVICE]
 //       reads IN_PREFIX.{noise,prompt,cond,style}.f32 (raw little-endian
 //       float32), writes the mel [T,80] to OUT.f32.
+//   mtts_cfm --inspect-model-bundle DIR [cfm,length_regulator,bigvgan]
+//   mtts_cfm --inspect-voice-bundle DIR
+//       the bundle contract gates (reference: runtime/main.cpp:2688-2691);
+//       print the JSON report, exit 0 when the contract holds, 1 otherwise.
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -83,8 +87,27 @@ int main(int argc, char** argv) {
                        static_cast<uint32_t>(std::strtoul(argv[5], nullptr, 10)), argc > 6 ? std::atoi(argv[6]) : 0);
     }
     if (argc >= 2 && std::strcmp(argv[1], "--cfm") == 0) return run_cfm(argc, argv);
+    if (argc >= 3 && (std::strcmp(argv[1], "--inspect-model-bundle") == 0 ||
+                      std::strcmp(argv[1], "--inspect-voice-bundle") == 0)) {
+      std::string report(1 << 16, '\0');
+      int rc;
+      if (argv[1][10] == 'v') {
+        rc = itts_inspect_voice_bundle(argv[2], &report[0], static_cast<uint32_t>(report.size()));
+      } else {
+        uint32_t mask = 0;
+        const std::string comps = argc > 3 ? argv[3] : "cfm";
+        if (comps.find("cfm") != std::string::npos) mask |= ITTS_COMPONENT_CFM;
+        if (comps.find("length_regulator") != std::string::npos) mask |= ITTS_COMPONENT_LENGTH_REGULATOR;
+        if (comps.find("bigvgan") != std::string::npos) mask |= ITTS_COMPONENT_BIGVGAN;
+        rc = itts_inspect_model_bundle(argv[2], mask, &report[0], static_cast<uint32_t>(report.size()));
+      }
+      std::printf("%s\n", report.c_str());
+      return rc == ITTS_OK ? 0 : 1;
+    }
     std::fprintf(stderr, "usage: mtts_cfm --bench-cfm BUNDLE T STEPS ITERS [DEVICE]\n"
-                         "       mtts_cfm --cfm BUNDLE T P STEPS CFG IN_PREFIX OUT.f32 [DEVICE]\n");
+                         "       mtts_cfm --cfm BUNDLE T P STEPS CFG IN_PREFIX OUT.f32 [DEVICE]\n"
+                         "       mtts_cfm --inspect-model-bundle DIR [cfm,length_regulator,bigvgan]\n"
+                         "       mtts_cfm --inspect-voice-bundle DIR\n");
     return 2;
   } catch (const std::exception& e) {
     std::fprintf(stderr, "error: %s\n", e.what());

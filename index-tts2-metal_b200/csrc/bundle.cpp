@@ -339,6 +339,8 @@ Mit2Bundle::Mit2Bundle(const std::string& dir, bool verify_sha256) : dir_(dir) {
     throw std::runtime_error("bundle: unsupported endianness '" + endian->str + "'");
   const uint64_t alignment = as_u64(root.get("alignment"), "alignment");
   if (alignment == 0) throw std::runtime_error("bundle: alignment must be non-zero");
+  version_ = static_cast<uint32_t>(version);
+  alignment_ = alignment;
   std::string wname = "weights.bin";
   if (const JVal* wf = root.get("weights_file")) wname = as_str(wf, "weights_file");
 
@@ -370,6 +372,7 @@ Mit2Bundle::Mit2Bundle(const std::string& dir, bool verify_sha256) : dir_(dir) {
     t.offset = as_u64(o.get("offset"), "offset");
     t.nbytes = as_u64(o.get("nbytes"), "nbytes");
     if (const JVal* h = o.get("sha256")) t.sha256 = as_str(h, "sha256");
+    if (const JVal* c = o.get("component")) t.component = as_str(c, "component");
     if (by_name_.count(t.name)) throw std::runtime_error("bundle: duplicate tensor " + t.name);
     if (t.nbytes == 0) throw std::runtime_error("bundle: zero-byte tensor " + t.name);
     if (t.offset % alignment != 0) throw std::runtime_error("bundle: unaligned tensor offset for " + t.name);

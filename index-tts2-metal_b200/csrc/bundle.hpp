@@ -21,6 +21,7 @@ struct TensorRec {
   uint64_t offset = 0;
   uint64_t nbytes = 0;
   std::string sha256;
+  std::string component;  // manifest "component" (gpt, semantic_codec, s2mel, bigvgan, voice, ...), may be empty
 };
 
 class Mit2Bundle {
@@ -42,6 +43,9 @@ class Mit2Bundle {
   // Raw f16 payload (throws if the tensor is not f16).
   const uint16_t* as_f16(const std::string& name, size_t* count) const;
   const std::vector<TensorRec>& tensors() const { return tensors_; }
+  uint32_t version() const { return version_; }
+  uint64_t alignment() const { return alignment_; }
+  size_t weights_bytes() const { return size_; }
 
  private:
   std::string dir_;
@@ -50,6 +54,8 @@ class Mit2Bundle {
   size_t size_ = 0;
   std::vector<TensorRec> tensors_;
   std::unordered_map<std::string, size_t> by_name_;
+  uint32_t version_ = 0;
+  uint64_t alignment_ = 0;
 };
 
 // FIPS 180-4 SHA-256, lower-case hex digest.

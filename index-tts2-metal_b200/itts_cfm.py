@@ -35,8 +35,12 @@ EXPORTED = [
     "itts_vocoder_launch_kernels", "itts_vocoder_profile", "itts_vocoder_flops",
     "itts_cond_create", "itts_cond_destroy", "itts_cond_last_error", "itts_cond_create_error", "itts_cond_assemble",
     "itts_cond_stage", "itts_cond_launch", "itts_cond_fetch", "itts_cond_stream", "itts_cond_launch_kernels",
-    "itts_cond_flops",
+    "itts_cond_flops", "itts_inspect_voice_bundle", "itts_inspect_model_bundle", "itts_voice_load",
 ]
+ITTS_COMPONENT_CFM = 0x1
+ITTS_COMPONENT_LENGTH_REGULATOR = 0x2
+ITTS_COMPONENT_BIGVGAN = 0x4
+ITTS_COMPONENT_ALL = 0x7
 VOCODER_HOP = 256
 VOCODER_MAX_T = 16384
 
@@ -119,6 +123,9 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_cond_stream": (vp, [vp]),
         "itts_cond_launch_kernels": (i32, [vp]),
         "itts_cond_flops": (f64, [u32, u32]),
+        "itts_inspect_voice_bundle": (i32, [C.c_char_p, C.c_char_p, u32]),
+        "itts_inspect_model_bundle": (i32, [C.c_char_p, u32, C.c_char_p, u32]),
+        "itts_voice_load": (i32, [C.c_char_p, u32, C.POINTER(u32), vp, vp, vp, C.c_char_p, u32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -452,3 +459,39 @@ class ConditionAssembler:
     @staticmethod
     def flops(n_in: int, G: int) -> float:
         return float(load().itts_cond_flops(int(n_in), int(G)))
+
+
+def inspect_voice_bundle(bundle_dir: str | Path) -> tuple[int, dict]:
+    """The voice-bundle contract gate (host only): (status, JSON report)."""
+    import json
+
+    buf = C.create_string_buffer(1 << 16)
+    rc = load().itts_inspect_voice_bundle(str(bundle_dir).encode(), buf, len(buf))
+    return rc, json.loads(buf.value.decode())
+
+
+def inspect_model_bundle(bundle_dir: str | Path, components: int = ITTS_COMPONENT_CFM) -> tuple[int, dict]:
+    """The model-bundle contract gate for `components` (host only): (status, JSON report)."""
+    import json
+
+    buf = C.create_string_buffer(1 << 16)
+    rc = load().itts_inspect_model_bundle(str(bundle_dir).encode(), int(components), buf, len(buf))
+    return rc, json.loads(buf.value.decode())
+
+
+def voice_load(bundle_dir: str | Path, prompt_tokens: int = 0) -> dict:
+    """prompt_cond [P,512], style [192] and prompt_mel [P,80] of a voice bundle."""
+    lib = load()
+    P = C.c_uint32(0)
+    err = C.create_string_buffer(512)
+    rc = lib.itts_voice_load(str(bundle_dir).encode(), int(prompt_tokens), C.byref(P), None, None, None, err, len(err))
+    if rc != ITTS_OK:
+        raise IttsError(rc, err.value.decode())
+    pc = np.empty((P.value, 512), np.float32)
+    st = np.empty(192, np.float32)
+    pm = np.empty((P.value, 80), np.float32)
+    rc = lib.itts_voice_load(str(bundle_dir).encode(), int(prompt_tokens), C.byref(P), _ptr(pc), _ptr(st), _ptr(pm),
+                             err, len(err))
+    if rc != ITTS_OK:
+        raise IttsError(rc, err.value.decode())
+    return {"prompt_cond": pc, "style": st, "prompt_mel": pm, "P": P.value}

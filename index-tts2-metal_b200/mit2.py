@@ -45,6 +45,21 @@ _DTYPES = {
 _NP = {v: k for k, v in _DTYPES.items()}
 
 
+VOICE_TENSORS = ("spk_cond_emb", "s2mel_style", "s2mel_prompt", "mel")
+
+
+def component_of(name: str) -> str:
+    """The manifest `component` of a tensor, by its name (the reference's
+    bundle writer groups tensors the same way: gpt, semantic_codec, s2mel,
+    bigvgan; the four cached-voice tensors are component voice)."""
+    if name in VOICE_TENSORS:
+        return "voice"
+    for prefix in ("gpt", "semantic_codec", "s2mel", "bigvgan", "campplus"):
+        if name.startswith(prefix + "."):
+            return prefix
+    return "s2mel"
+
+
 def write_bundle(out_dir: str | Path, tensors: Iterable[tuple[str, np.ndarray]], metadata: dict | None = None) -> dict:
     """Write ``(name, array)`` pairs as an MIT2 bundle; returns the manifest."""
     out = Path(out_dir)
@@ -70,7 +85,7 @@ def write_bundle(out_dir: str | Path, tensors: Iterable[tuple[str, np.ndarray]],
                     "nbytes": len(payload),
                     "sha256": hashlib.sha256(payload).hexdigest(),
                     "layout": "row_major",
-                    "component": "s2mel",
+                    "component": component_of(name),
                 }
             )
     manifest = {
@@ -334,7 +349,7 @@ def make_vocoder_bundle(out_dir: str | Path, seed: int = 0) -> Path:
     """Write the synthetic BigVGAN bundle; skips work when an identical one exists."""
     out = Path(out_dir)
     stamp = out / ".synthetic"
-    key = f"bigvgan seed={seed} v1"
+    key = f"bigvgan seed={seed} v2"
     if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():
         return out
     write_bundle(out, make_bigvgan_tensors(seed), metadata={"synthetic": True, "seed": seed, "model": "bigvgan"})
@@ -382,6 +397,30 @@ def make_condition_bundle(out_dir: str | Path, seed: int = 0) -> Path:
         return out
     write_bundle(out, make_length_regulator_tensors(seed),
                  metadata={"synthetic": True, "seed": seed, "model": "length_regulator"})
+    stamp.write_text(key)
+    return out
+
+
+def make_voice_tensors(seed: int, prompt_tokens: int = 200, spk_tokens: int = 170) -> list[tuple[str, np.ndarray]]:
+    """A synthetic cached-voice profile in the reference's voice-bundle layout
+    (f32, component voice): spk_cond_emb [1, S, 1024], s2mel_style [1, 192],
+    s2mel_prompt [1, P, 512] and the prompt mel [1, 80, P]."""
+    rng = np.random.default_rng(seed)
+    return [("spk_cond_emb", rng.standard_normal((1, spk_tokens, 1024), dtype=np.float32)),
+            ("s2mel_style", rng.standard_normal((1, 192), dtype=np.float32)),
+            ("s2mel_prompt", rng.standard_normal((1, prompt_tokens, 512), dtype=np.float32)),
+            ("mel", rng.standard_normal((1, 80, prompt_tokens), dtype=np.float32))]
+
+
+def make_voice_bundle(out_dir: str | Path, seed: int = 0, prompt_tokens: int = 200) -> Path:
+    """Write a synthetic voice bundle; skips work when an identical one exists."""
+    out = Path(out_dir)
+    stamp = out / ".synthetic"
+    key = f"voice seed={seed} P={prompt_tokens} v1"
+    if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():
+        return out
+    write_bundle(out, make_voice_tensors(seed, prompt_tokens), metadata={"synthetic": True, "seed": seed,
+                                                                        "model": "voice"})
     stamp.write_text(key)
     return out
 
