@@ -361,6 +361,42 @@ def condition_line(args, cfg, rank, world, local, barrier, max_over_ranks):
             "cpu_baseline": cpu}
 
 
+def pipeline_line(cfg, rank, world, local, barrier, max_over_ranks):
+    """End to end from semantic features to waveform through
+    itts_pipeline_synthesize (voice profile -> condition assembly -> CFM
+    sampler -> vocoder), host buffers in and out, for this rank's utterance of
+    the workload's shape; wall-clock per call, max over ranks."""
+    import itts_cfm
+
+    voice_dir = Path(tempfile.gettempdir()) / f"itts_bench_voice_P{cfg['P']}"
+    if rank == 0 or world == 1:
+        mit2.make_dit_bundle(BUNDLE_DIR, seed=0, init="baseline")
+        mit2.make_condition_bundle(COND_BUNDLE_DIR, seed=0)
+        mit2.make_vocoder_bundle(VOC_BUNDLE_DIR, seed=0)
+        mit2.make_voice_bundle(voice_dir, seed=0, prompt_tokens=cfg["P"])
+    barrier()
+    P, G = cfg["P"], cfg["T"] - cfg["P"]
+    n_in = max(1, round(G * COND_SEM_PER_MEL))
+    rng = np.random.default_rng(3000 + rank)
+    s_infer = rng.standard_normal((n_in, 1024)).astype(np.float32)
+    noise = rng.standard_normal((P + G, 80)).astype(np.float32)
+    pipe = itts_cfm.Pipeline(BUNDLE_DIR, COND_BUNDLE_DIR, VOC_BUNDLE_DIR, device=local)
+    pipe.synthesize(voice_dir, s_infer, G, noise, cfg["steps"], cfg["cfg"])
+    nv = 5
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(nv):
+        pipe.synthesize(voice_dir, s_infer, G, noise, cfg["steps"], cfg["cfg"])
+    dt = max_over_ranks(time.perf_counter() - t0) / nv
+    pipe.close()
+    audio_s = G * 256 / 22050.0
+    return {"metric": "generated mel frames/s end to end (semantic features + voice -> waveform)",
+            "value": G * world / dt, "unit": "generated mel frames/s", "P": P, "G": G, "n_in": n_in,
+            "steps_cfm": cfg["steps"], "ms_per_utterance": 1e3 * dt,
+            "real_time_factor": dt / audio_s, "audio_seconds_per_second": world * audio_s / dt,
+            "timing": "host wall clock around itts_pipeline_synthesize (host buffers in and out)"}
+
+
 def cpu_reference_rate(u, steps_cfm: int, threads: int, reps: int = 1):
     import oracle
 
@@ -423,6 +459,8 @@ def main():
     ap.add_argument("--vocoder", type=int, default=1, help="also time the BigVGAN vocoder (0 = skip)")
     ap.add_argument("--condition", type=int, default=1,
                     help="also time the condition assembly before the sampler (0 = skip)")
+    ap.add_argument("--pipeline", type=int, default=1,
+                    help="also time the whole semantic-features-to-waveform chain (0 = skip)")
     ap.add_argument("--vocoder-only", action="store_true",
                     help="time only the BigVGAN vocoder and print its line (profiling aid)")
     args = ap.parse_args()
@@ -592,6 +630,10 @@ def main():
     if args.condition:
         condition = condition_line(args, cfg, rank, world, local, barrier, max_over_ranks)
 
+    pipeline = None
+    if args.pipeline:
+        pipeline = pipeline_line(cfg, rank, world, local, barrier, max_over_ranks)
+
     vocoder = None
     if args.vocoder:
         vocoder = vocoder_line(args, cfg, rank, world, local, barrier, max_over_ranks, peak,
@@ -630,6 +672,7 @@ def main():
             "batched": batched,
             "condition": condition,
             "vocoder": vocoder,
+            "pipeline": pipeline,
         }
         print(json.dumps(line))
     if dist is not None:

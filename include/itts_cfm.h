@@ -324,6 +324,32 @@ int itts_inspect_model_bundle(const char* bundle_dir, uint32_t components, char*
 int itts_voice_load(const char* bundle_dir, uint32_t prompt_tokens, uint32_t* P_out, float* prompt_cond, float* style,
                     float* prompt_mel, char* err, uint32_t err_cap);
 
+/* ------------------------------------------------------------------------
+ * The S2Mel-to-waveform chain of the reference's hot synthesis path
+ * (synthesize_hot_condition_vectors_wav_shared,
+ * runtime/impl/tts_synthesis/synthesis_pipeline.cpp:1030-1034, 1060-1089),
+ * from the semantic features on: voice profile -> condition assembly -> CFM
+ * sampler -> vocoder on the generated rows. Holds one context of each stage
+ * on one GPU.
+ * ------------------------------------------------------------------------ */
+typedef struct itts_pipeline itts_pipeline;
+
+/* The three bundle directories may be the same (a full model bundle). */
+int itts_pipeline_create(const char* cfm_bundle_dir, const char* regulator_bundle_dir, const char* vocoder_bundle_dir,
+                         int device, itts_pipeline** out);
+void itts_pipeline_destroy(itts_pipeline* p);
+const char* itts_pipeline_last_error(const itts_pipeline* p);
+const char* itts_pipeline_create_error(void);
+
+/* voice_bundle_dir: a cached voice (itts_inspect_voice_bundle contract);
+ * prompt_tokens: prompt rows P taken from it (0 = all). s_infer [n_in,1024]
+ * (GPT layer + VQ embedding), G generated frames, noise [(P+G),80], steps,
+ * cfg_rate -> wave [256 G] (and, if full_mel is non-NULL, the sampler's
+ * mel [(P+G),80]). */
+int itts_pipeline_synthesize(itts_pipeline* p, const char* voice_bundle_dir, uint32_t prompt_tokens,
+                             const float* s_infer, uint32_t n_in, uint32_t G, const float* noise, uint32_t steps,
+                             float cfg_rate, float* wave, float* full_mel);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,6 +36,8 @@ EXPORTED = [
     "itts_cond_create", "itts_cond_destroy", "itts_cond_last_error", "itts_cond_create_error", "itts_cond_assemble",
     "itts_cond_stage", "itts_cond_launch", "itts_cond_fetch", "itts_cond_stream", "itts_cond_launch_kernels",
     "itts_cond_flops", "itts_inspect_voice_bundle", "itts_inspect_model_bundle", "itts_voice_load",
+    "itts_pipeline_create", "itts_pipeline_destroy", "itts_pipeline_last_error", "itts_pipeline_create_error",
+    "itts_pipeline_synthesize",
 ]
 ITTS_COMPONENT_CFM = 0x1
 ITTS_COMPONENT_LENGTH_REGULATOR = 0x2
@@ -126,6 +128,11 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_inspect_voice_bundle": (i32, [C.c_char_p, C.c_char_p, u32]),
         "itts_inspect_model_bundle": (i32, [C.c_char_p, u32, C.c_char_p, u32]),
         "itts_voice_load": (i32, [C.c_char_p, u32, C.POINTER(u32), vp, vp, vp, C.c_char_p, u32]),
+        "itts_pipeline_create": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.POINTER(vp)]),
+        "itts_pipeline_destroy": (None, [vp]),
+        "itts_pipeline_last_error": (C.c_char_p, [vp]),
+        "itts_pipeline_create_error": (C.c_char_p, []),
+        "itts_pipeline_synthesize": (i32, [vp, C.c_char_p, u32, vp, u32, u32, vp, u32, f32, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -495,3 +502,41 @@ def voice_load(bundle_dir: str | Path, prompt_tokens: int = 0) -> dict:
     if rc != ITTS_OK:
         raise IttsError(rc, err.value.decode())
     return {"prompt_cond": pc, "style": st, "prompt_mel": pm, "P": P.value}
+
+
+class Pipeline:
+    """Voice profile -> condition assembly -> CFM sampler -> vocoder on one GPU
+    (itts_pipeline_create / itts_pipeline_synthesize)."""
+
+    def __init__(self, cfm_bundle: str | Path, regulator_bundle: str | Path, vocoder_bundle: str | Path,
+                 device: int = 0):
+        self.lib = load()
+        h = C.c_void_p()
+        rc = self.lib.itts_pipeline_create(str(cfm_bundle).encode(), str(regulator_bundle).encode(),
+                                           str(vocoder_bundle).encode(), int(device), C.byref(h))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_pipeline_create_error().decode())
+        self.h = h
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.itts_pipeline_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def synthesize(self, voice_bundle: str | Path, s_infer, G: int, noise, steps: int, cfg: float,
+                   prompt_tokens: int = 0) -> tuple[np.ndarray, np.ndarray]:
+        s_infer, noise = _f32(s_infer), _f32(noise)
+        wave = np.empty(int(G) * VOCODER_HOP, np.float32)
+        mel = np.empty_like(noise)
+        rc = self.lib.itts_pipeline_synthesize(self.h, str(voice_bundle).encode(), int(prompt_tokens), _ptr(s_infer),
+                                               s_infer.shape[0], int(G), _ptr(noise), int(steps), float(cfg),
+                                               _ptr(wave), _ptr(mel))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_pipeline_last_error(self.h).decode())
+        return wave, mel
