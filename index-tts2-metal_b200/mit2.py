@@ -425,6 +425,58 @@ def make_voice_bundle(out_dir: str | Path, seed: int = 0, prompt_tokens: int = 2
     return out
 
 
+GPT_LAYERS, GPT_WIDTH, GPT_MLP, GPT_VOCAB, GPT_POSITIONS = 24, 1280, 5120, 8194, 1818
+
+
+def gpt_tensor_specs() -> list[tuple[str, tuple[int, ...], str]]:
+    """(name, shape, kind) of the GPT mel-code decoder tensors the reference's
+    cached decode reads (runtime/impl/gpt.cpp:1060-1210, 1545-1554, 1877-1909):
+    24 GPT-2 blocks (Conv1D weights stored [in, out]), ln_f, final_norm, the
+    mel head, the mel-code and position embeddings."""
+    s: list[tuple[str, tuple[int, ...], str]] = []
+    W, M = GPT_WIDTH, GPT_MLP
+    for l in range(GPT_LAYERS):
+        p = f"gpt.gpt.h.{l}."
+        s += [(p + "ln_1.weight", (W,), "gamma"), (p + "ln_1.bias", (W,), "b"),
+              (p + "attn.c_attn.weight", (W, 3 * W), "w"), (p + "attn.c_attn.bias", (3 * W,), "b"),
+              (p + "attn.c_proj.weight", (W, W), "w"), (p + "attn.c_proj.bias", (W,), "b"),
+              (p + "ln_2.weight", (W,), "gamma"), (p + "ln_2.bias", (W,), "b"),
+              (p + "mlp.c_fc.weight", (W, M), "w"), (p + "mlp.c_fc.bias", (M,), "b"),
+              (p + "mlp.c_proj.weight", (M, W), "w"), (p + "mlp.c_proj.bias", (W,), "b")]
+    s += [("gpt.gpt.ln_f.weight", (W,), "gamma"), ("gpt.gpt.ln_f.bias", (W,), "b"),
+          ("gpt.final_norm.weight", (W,), "gamma"), ("gpt.final_norm.bias", (W,), "b"),
+          ("gpt.mel_head.weight", (GPT_VOCAB, W), "w"), ("gpt.mel_head.bias", (GPT_VOCAB,), "b"),
+          ("gpt.mel_embedding.weight", (GPT_VOCAB, W), "emb"),
+          ("gpt.mel_pos_embedding.emb.weight", (GPT_POSITIONS, W), "emb")]
+    return s
+
+
+def make_gpt_tensors(seed: int) -> list[tuple[str, np.ndarray]]:
+    """Deterministic synthetic GPT decoder weights (f16): linear weights and
+    embeddings N(0, 0.02) (GPT-2's initialisation scale), biases N(0, 0.02),
+    LayerNorm gammas 1 + N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for name, shape, kind in gpt_tensor_specs():
+        a = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+        if kind == "gamma":
+            a += np.float32(1.0)
+        out.append((name, a.astype(np.float16)))
+    return out
+
+
+def make_gpt_bundle(out_dir: str | Path, seed: int = 0) -> Path:
+    """Write the synthetic GPT decoder bundle (about 1 GB); skips work when an identical one exists."""
+    out = Path(out_dir)
+    stamp = out / ".synthetic"
+    key = f"gpt seed={seed} v1"
+    if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():
+        return out
+    write_bundle(out, make_gpt_tensors(seed), metadata={"synthetic": True, "seed": seed, "model": "gpt"})
+    stamp.write_text(key)
+    return out
+
+
 def bundle_f32(bundle_dir: str | Path) -> dict[str, np.ndarray]:
     """All estimator tensors decoded to contiguous float32 (f16 decoding is exact)."""
     return {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in read_bundle(bundle_dir).items()}

@@ -1,0 +1,98 @@
+"""TEST INFRASTRUCTURE — numpy restatement of the reference's cached greedy
+GPT mel-code decoder (fp32), used only by tests/ as the checker; the product
+never imports it. Pinned to the reference's own compiled CPU decoder
+(oracle/_ref) through tests/golden/kat_gpt_decode.npz.
+
+Reference functions restated (paths inside raoqu/index-tts2-metal):
+  cpu_layernorm                      runtime/impl/tokenizer_tests.cpp:2992-3010
+  cpu_gelu_new                       runtime/impl/tokenizer_tests.cpp:3931-3945
+  cpu_attention_single_head_causal / cpu_attention_single_query
+                                     runtime/impl/tokenizer_tests.cpp:4003-4061
+  transpose_gpt_conv1d_weight        runtime/impl/gpt.cpp:208-216
+  run_gpt_transformer_block_cpu_layer runtime/impl/gpt.cpp:658-711
+  run_gpt_layer_qkv_cpu, KV cache, cached attention/block
+                                     runtime/impl/gpt.cpp:1060-1210
+  argmax_row                         runtime/impl/gpt.cpp:1297-1308
+  build_gpt_greedy_current_cpu       runtime/impl/gpt.cpp:1545-1554
+  run_gpt_kv_prefill_cpu             runtime/impl/gpt.cpp:1796-1806
+  run_gpt_kv_greedy_cpu              runtime/impl/gpt.cpp:1877-1909 (hf_generate_positions = false)
+"""
+from __future__ import annotations
+
+import numpy as np
+
+START, STOP, VOCAB, W, HEADS, HD, LAYERS = 8192, 8193, 8194, 1280, 20, 64, 24
+
+
+def _ln(x, g, b, eps=1e-5):
+    x = x.astype(np.float32)
+    m = x.mean(axis=-1, keepdims=True, dtype=np.float32)
+    v = ((x - m) ** 2).mean(axis=-1, keepdims=True, dtype=np.float32)
+    return ((x - m) / np.sqrt(v + np.float32(eps))) * g + b
+
+
+def _gelu_new(x):
+    c = np.float32(0.7978845608028654)
+    y = np.float32(0.5) * x * (np.float32(1.0) + np.tanh(c * (x + np.float32(0.044715) * x * x * x)))
+    return np.where(x > 10.0, x, np.where(x < -10.0, np.float32(0.0), y)).astype(np.float32)
+
+
+class GptOracle:
+    def __init__(self, tensors: dict[str, np.ndarray]):
+        f = {k: np.asarray(v, np.float32) for k, v in tensors.items() if k.startswith("gpt.")}
+        self.t = f
+        self.layers = []
+        for l in range(LAYERS):
+            p = f"gpt.gpt.h.{l}."
+            self.layers.append({
+                "ln1": (f[p + "ln_1.weight"], f[p + "ln_1.bias"]),
+                "attn": (f[p + "attn.c_attn.weight"], f[p + "attn.c_attn.bias"]),  # [in, out]: x @ W
+                "proj": (f[p + "attn.c_proj.weight"], f[p + "attn.c_proj.bias"]),
+                "ln2": (f[p + "ln_2.weight"], f[p + "ln_2.bias"]),
+                "fc": (f[p + "mlp.c_fc.weight"], f[p + "mlp.c_fc.bias"]),
+                "mproj": (f[p + "mlp.c_proj.weight"], f[p + "mlp.c_proj.bias"]),
+            })
+
+    @staticmethod
+    def _attend(q, k, v):
+        """q [H,64] against keys/values [L,H,64] -> [H*64]."""
+        s = np.einsum("hd,lhd->hl", q, k) * np.float32(1.0 / np.sqrt(np.float32(HD)))
+        s = np.exp(s - s.max(axis=1, keepdims=True))
+        p = s / s.sum(axis=1, keepdims=True)
+        return np.einsum("hl,lhd->hd", p, v).reshape(-1).astype(np.float32)
+
+    def _block_current(self, L, x, cache_k, cache_v):
+        """One token through layer L with its KV cache (appended in place)."""
+        qkv = _ln(x, *L["ln1"]) @ L["attn"][0] + L["attn"][1]
+        q, k, v = qkv[:W].reshape(HEADS, HD), qkv[W:2 * W].reshape(HEADS, HD), qkv[2 * W:].reshape(HEADS, HD)
+        cache_k.append(k)
+        cache_v.append(v)
+        a = self._attend(q, np.stack(cache_k), np.stack(cache_v))
+        h = x + (a @ L["proj"][0] + L["proj"][1])
+        m = _gelu_new(_ln(h, *L["ln2"]) @ L["fc"][0] + L["fc"][1])
+        return (h + (m @ L["mproj"][0] + L["mproj"][1])).astype(np.float32)
+
+    def greedy(self, prefix, steps: int):
+        """(predicted codes, logits of each step) as run_gpt_kv_greedy_cpu;
+        the prefix is processed token by token (the causal full-sequence
+        prefill of the reference computes the same values)."""
+        prefix = np.asarray(prefix, np.float32)
+        caches = [([], []) for _ in range(LAYERS)]
+        for x in prefix:
+            for L, (ck, cv) in zip(self.layers, caches):
+                x = self._block_current(L, x, ck, cv)
+        emb, pos = self.t["gpt.mel_embedding.weight"], self.t["gpt.mel_pos_embedding.emb.weight"]
+        tok, out, logits = START, [], []
+        for step in range(steps):
+            x = emb[tok] + pos[step]
+            for L, (ck, cv) in zip(self.layers, caches):
+                x = self._block_current(L, x, ck, cv)
+            h = _ln(_ln(x, self.t["gpt.gpt.ln_f.weight"], self.t["gpt.gpt.ln_f.bias"]),
+                    self.t["gpt.final_norm.weight"], self.t["gpt.final_norm.bias"])
+            lg = (self.t["gpt.mel_head.weight"] @ h + self.t["gpt.mel_head.bias"]).astype(np.float32)
+            logits.append(lg)
+            tok = int(np.argmax(lg))
+            out.append(tok)
+            if tok == STOP:
+                break
+        return out, logits

@@ -225,6 +225,8 @@ class RefOracle:
         L.ref_noise.argtypes = [C.c_uint32, C.c_uint32, C.c_uint64, C.c_float, C.c_void_p]
         L.ref_bigvgan_vocoder.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_void_p]
         L.ref_length_regulator.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
+        L.ref_gpt_kv_greedy.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p,
+                                        C.POINTER(C.c_uint32), C.c_void_p, C.POINTER(C.c_int)]
         L.ref_bigvgan_activation.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
 
     def _ok(self, rc):
@@ -280,6 +282,17 @@ class RefOracle:
         out = np.empty((T, C_), np.float32)
         self._ok(self.lib.ref_noise(T, C_, seed, temperature, _p(out)))
         return out
+
+    def gpt_greedy(self, prefix, steps: int):
+        """run_gpt_kv_greedy_cpu: (codes, logits of the last step, first stop step)."""
+        prefix = _f32(prefix)
+        toks = np.zeros(steps, np.uint32)
+        n = C.c_uint32(0)
+        stop = C.c_int(-1)
+        logits = np.zeros(8194, np.float32)
+        self._ok(self.lib.ref_gpt_kv_greedy(self.dir, _p(prefix), prefix.shape[0], int(steps), _p(toks), C.byref(n),
+                                            _p(logits), C.byref(stop)))
+        return toks[: n.value].tolist(), logits, stop.value
 
     def length_regulator(self, x, n_out: int):
         x = _f32(x)

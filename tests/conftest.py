@@ -92,6 +92,18 @@ def port_condition(condition_bundle):
     return oracle.ConditionOracle(mit2.bundle_f32(condition_bundle))
 
 
+@pytest.fixture(scope="session")
+def gpt_bundle() -> Path:
+    return mit2.make_gpt_bundle(BUNDLE_ROOT / "gpt_seed0", seed=0)
+
+
+@pytest.fixture(scope="session")
+def gpt_oracle(gpt_bundle):
+    import gpt_oracle as G
+
+    return G.GptOracle(mit2.bundle_f32(gpt_bundle))
+
+
 def _gpu_ctx(bundle):
     import itts_cfm
 

@@ -27,7 +27,10 @@ Cases (inputs follow the reference's self-tests where it has them):
                     (run_length_regulator_full_test: 7 -> 11 frames) and on a
                     seeded 40 -> 63 case, synthetic length-regulator bundle seed 0
 
-    python tests/golden/make_golden.py [--only bigvgan|lr]
+  kat_gpt_decode    run_gpt_kv_greedy_cpu (cached greedy mel-code decode, 24 layers)
+                    on a seeded 4-row prefix for 3 steps, synthetic GPT bundle seed 0
+
+    python tests/golden/make_golden.py [--only bigvgan|lr|gpt]
 """
 from __future__ import annotations
 
@@ -102,8 +105,21 @@ def length_regulator_cases():
                         out40_63=r.length_regulator(x40, 63), bundle_seed=0, weights_sha256=weights_sha(lrb))
 
 
+def gpt_cases():
+    gb = mit2.make_gpt_bundle(ROOT / "gpt_seed0", seed=0)
+    r = oracle.RefOracle(gb)
+    prefix = f32(np.random.default_rng(7).standard_normal((4, 1280)))
+    toks, logits, stop = r.gpt_greedy(prefix, 3)
+    np.savez_compressed(HERE / "kat_gpt_decode.npz", prefix=prefix, codes=np.array(toks, np.uint32),
+                        last_logits=logits, first_stop=np.int32(stop), bundle_seed=0, weights_sha256=weights_sha(gb))
+
+
 def main():
     only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only == "gpt":
+        gpt_cases()
+        print("golden vectors written to", HERE)
+        return
     if only == "bigvgan":
         bigvgan_cases()
         print("golden vectors written to", HERE)
@@ -114,6 +130,7 @@ def main():
         return
     bigvgan_cases()
     length_regulator_cases()
+    gpt_cases()
     unit = mit2.make_dit_bundle(ROOT / "seed0_unit", seed=0, init="unit")
     base = mit2.make_dit_bundle(ROOT / "seed0_baseline", seed=0, init="baseline")
     ru, rb = oracle.RefOracle(unit), oracle.RefOracle(base)

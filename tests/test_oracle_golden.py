@@ -1,5 +1,5 @@
 """Pin the CPU oracles (oracle/dit_oracle.c, oracle/bigvgan_oracle.c,
-oracle/condition_oracle.c) to the reference's own CPU
+oracle/condition_oracle.c, oracle/gpt_oracle.py) to the reference's own CPU
 functions through the committed golden vectors (tests/golden/, made by
 tests/golden/make_golden.py from oracle/_ref). fp32 vs fp32 with a different
 summation order: the reference's own unit tolerance ladder applies (1e-4
@@ -152,3 +152,14 @@ def test_condition_merge_places_prompt_rows_first(port_condition):
     assert cond.shape == (15, 512)
     assert np.array_equal(cond[:4], prompt)
     _close(g["out7_11"], cond[4:])
+
+
+def test_gpt_bundle_matches_golden_generator(gpt_bundle):
+    assert _sha(gpt_bundle) == str(_load("kat_gpt_decode")["weights_sha256"])
+
+
+def test_gpt_greedy_decode(gpt_oracle):
+    g = _load("kat_gpt_decode")
+    codes, logits = gpt_oracle.greedy(g["prefix"], 3)
+    assert codes == g["codes"].tolist()
+    _close(g["last_logits"], logits[-1])
