@@ -47,6 +47,8 @@ VOC_REF_FRAMES = 4  # mel frames per reference CPU vocoder call in the baseline 
 COND_BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_length_regulator_seed0"
 COND_SEM_PER_MEL = 175 / 600  # semantic frames per generated mel frame in the condition workload
 REF_SAMPLE_FRAMES = 32
+GPT_BUNDLE_DIR = Path(tempfile.gettempdir()) / "itts_bench_bundle_gpt_seed0"
+GPT_PREFIX, GPT_STEPS = 100, 175  # prefix rows; mel codes for 600 mel frames at 175 codes per 600 frames
 
 
 def step_flops_total(B: int, T: int, cfg: dict) -> float:
@@ -361,6 +363,63 @@ def condition_line(args, cfg, rank, world, local, barrier, max_over_ranks):
             "cpu_baseline": cpu}
 
 
+def gpt_line(args, rank, world, local, barrier, max_over_ranks, hbm_peak):
+    """GPT mel-code decoder for this rank's utterance: a GPT_PREFIX-row prefix,
+    then GPT_STEPS greedy decode steps (random weights never predict the stop
+    code, so every step runs). Device-timed prefill and decode from the
+    decoder's own events, e2e = wall clock of itts_gpt_generate with the prefix
+    in and the codes and logits out; the dominant cost is streaming the f16
+    weights once per token, so the roofline is HBM bytes per token."""
+    import itts_cfm
+
+    if rank == 0 or world == 1:
+        mit2.make_gpt_bundle(GPT_BUNDLE_DIR, seed=0)
+    barrier()
+    rng = np.random.default_rng(3000 + rank)
+    prefix = rng.standard_normal((GPT_PREFIX, 1280)).astype(np.float32)
+    dec = itts_cfm.GptDecoder(GPT_BUNDLE_DIR, device=local)
+    dec.generate(prefix, 16)
+    runs, pre, dcd, wall = 3, [], [], []
+    for _ in range(runs):
+        barrier()
+        t0 = time.perf_counter()
+        codes, _ = dec.generate(prefix, GPT_STEPS)
+        wall.append(time.perf_counter() - t0)
+        p_ms, d_ms = dec.timing()
+        pre.append(p_ms)
+        dcd.append(d_ms)
+    n = len(codes)
+    pre_ms, dec_ms, t_e2e = (max_over_ranks(float(np.median(v))) for v in (pre, dcd, wall))
+    launches = dec.launch_kernels()
+    dec.close()
+    wb = itts_cfm.GptDecoder.weight_bytes_per_token()
+    kv = 24 * 1280 * 2 * 4 * (GPT_PREFIX + 0.5 * (n + 1))  # fp32 K and V rows read per token, mean over the run
+    gbs = (wb + kv) / (dec_ms / n / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import gpt_oracle
+        import threadpoolctl
+
+        o = gpt_oracle.GptOracle(mit2.bundle_f32(GPT_BUNDLE_DIR))
+        th = threadpoolctl.threadpool_info()
+        cores = max([int(i.get("num_threads", 1)) for i in th if i.get("user_api") == "blas"] or [1])
+        ps, ss = 16, 8
+        t0 = time.perf_counter()
+        o.greedy(prefix[:ps], ss)
+        dt = time.perf_counter() - t0
+        cpu = {"value": (ps + ss) / dt, "unit": "tokens/s (prefix rows + decode steps)", "cores": cores, "kind": "port",
+               "sample": f"oracle/gpt_oracle.py greedy, {ps} prefix rows + {ss} steps, numpy BLAS; {dt:.2f} s"}
+    return {"metric": "GPT mel-code decode, tokens/s (cached greedy, one utterance per GPU)",
+            "value": n * world / (dec_ms / 1e3), "unit": "tokens/s", "prefix_rows": GPT_PREFIX, "steps": n,
+            "ms_per_token": dec_ms / n, "prefill_ms": pre_ms, "prefill_ms_per_row": pre_ms / GPT_PREFIX,
+            "gpu_launches": launches * n + launches * GPT_PREFIX,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "bytes_per_token": wb + kv, "note": "f16 weights once per token + mean fp32 KV-cache reads"},
+            "e2e": {"value": n * world / t_e2e, "unit": "tokens/s (prefill included)",
+                    "h2d_bytes_per_step": int(prefix.nbytes), "d2h_bytes_per_step": int(n * 4 + 8194 * 4)},
+            "cpu_baseline": cpu}
+
+
 def pipeline_line(cfg, rank, world, local, barrier, max_over_ranks):
     """End to end from semantic features to waveform through
     itts_pipeline_synthesize (voice profile -> condition assembly -> CFM
@@ -461,6 +520,7 @@ def main():
                     help="also time the condition assembly before the sampler (0 = skip)")
     ap.add_argument("--pipeline", type=int, default=1,
                     help="also time the whole semantic-features-to-waveform chain (0 = skip)")
+    ap.add_argument("--gpt", type=int, default=1, help="also time the GPT mel-code decoder (0 = skip)")
     ap.add_argument("--vocoder-only", action="store_true",
                     help="time only the BigVGAN vocoder and print its line (profiling aid)")
     args = ap.parse_args()
@@ -639,6 +699,10 @@ def main():
         vocoder = vocoder_line(args, cfg, rank, world, local, barrier, max_over_ranks, peak,
                                float(peaks.get("hbm_gbs", 6546.0)))
 
+    gpt = None
+    if args.gpt:
+        gpt = gpt_line(args, rank, world, local, barrier, max_over_ranks, float(peaks.get("hbm_gbs", 6546.0)))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
@@ -673,6 +737,7 @@ def main():
             "condition": condition,
             "vocoder": vocoder,
             "pipeline": pipeline,
+            "gpt": gpt,
         }
         print(json.dumps(line))
     if dist is not None:

@@ -350,6 +350,42 @@ int itts_pipeline_synthesize(itts_pipeline* p, const char* voice_bundle_dir, uin
                              const float* s_infer, uint32_t n_in, uint32_t G, const float* noise, uint32_t steps,
                              float cfg_rate, float* wave, float* full_mel);
 
+/* ------------------------------------------------------------------------
+ * GPT mel-code decoder: cached greedy decode of mel codes (24 GPT-2 blocks,
+ * width 1280, 20 heads, vocabulary 8194; start code 8192, stop code 8193)
+ * from a prefix of input embeddings. Replaces run_gpt_kv_greedy_cpu
+ * (runtime/impl/gpt.cpp:1877-1909, its GptGreedyOutputs :1857-1863 as codes
+ * plus last_logits; hf_generate_positions = false) and the Metal cached decode
+ * it stands for. f16 weights, fp32 activations and KV cache.
+ * ------------------------------------------------------------------------ */
+typedef struct itts_gpt_ctx itts_gpt_ctx;
+
+#define ITTS_GPT_WIDTH 1280u
+#define ITTS_GPT_VOCAB 8194u
+#define ITTS_GPT_START 8192u
+#define ITTS_GPT_STOP 8193u
+#define ITTS_GPT_MAX_STEPS 1818u /* rows of gpt.mel_pos_embedding */
+#define ITTS_GPT_MAX_LEN 4096u   /* prefix rows + steps held in the KV cache */
+
+/* Loads the bundle's gpt.* decoder tensors onto `device`. */
+int itts_gpt_create(const char* bundle_dir, int device, itts_gpt_ctx** out);
+void itts_gpt_destroy(itts_gpt_ctx* ctx);
+const char* itts_gpt_last_error(const itts_gpt_ctx* ctx);
+const char* itts_gpt_create_error(void);
+
+/* prefix [P,1280] f32 (may be NULL when P = 0), at most `steps` decode steps
+ * -> codes [steps] (the predicted codes; the stop code, when predicted, is the
+ * last one), *n_codes = how many, last_logits [8194] (may be NULL) = the last
+ * step's logits. Needs 1 <= steps <= ITTS_GPT_MAX_STEPS and
+ * P + steps <= ITTS_GPT_MAX_LEN. */
+int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t* codes,
+                      uint32_t* n_codes, float* last_logits);
+/* Device time (ms) of the last generate's prefill and decode (no reference
+ * counterpart); kernels one decode step launches; f16 weight bytes it streams. */
+int itts_gpt_timing(const itts_gpt_ctx* ctx, float* prefill_ms, float* decode_ms);
+int itts_gpt_launch_kernels(const itts_gpt_ctx* ctx);
+double itts_gpt_weight_bytes_per_token(void);
+
 #ifdef __cplusplus
 }
 #endif

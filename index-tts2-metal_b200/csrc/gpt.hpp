@@ -1,0 +1,84 @@
+// GPT mel-code decoder: cached greedy decode of mel codes from a prefix of
+// input embeddings.
+//
+// Follows run_gpt_kv_greedy_cpu (runtime/impl/gpt.cpp:1877-1909) and its
+// pieces (:1060-1210, 1545-1554, 1796-1806): 24 GPT-2 blocks (LayerNorm ->
+// c_attn 1280 -> 3840 -> 20-head attention over the KV cache -> c_proj +
+// residual; LayerNorm -> c_fc 1280 -> 5120 -> gelu_new -> c_proj + residual),
+// ln_f, final_norm, mel head (8194 codes), argmax; the next input is the
+// code's mel embedding plus the step's position embedding; start code 8192,
+// stop code 8193.
+//
+// One token at a time is bandwidth-bound (about 1 GB of f16 weights per
+// token), so every projection is a GEMV kernel over f16 weights with fp32
+// activations and accumulation (LayerNorm fused into its prologue); the KV
+// cache is fp32. A CUDA graph per token (prefill row or decode step) reads
+// the row, the cache length, the step and the current code from device
+// memory, so the host only synchronises once per chunk of steps.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+namespace itts {
+
+class GptDecoder {
+ public:
+  GptDecoder(const std::string& bundle_dir, int device, bool verify_sha256);
+  ~GptDecoder();
+  GptDecoder(const GptDecoder&) = delete;
+  GptDecoder& operator=(const GptDecoder&) = delete;
+
+  // prefix [P,1280] (host) -> up to max_steps codes (host); stops after the
+  // stop code (included, as the reference's predicted tokens). Returns the
+  // number of codes; last_logits (optional, host [8194]) of the last step.
+  int generate(const float* prefix, int P, int max_steps, uint32_t* codes, float* last_logits);
+  // Device time of the last generate call's prefill and decode parts (ms).
+  float last_prefill_ms() const { return prefill_ms_; }
+  float last_decode_ms() const { return decode_ms_; }
+  int last_steps() const { return steps_; }
+  int kernels_per_token() const { return decode_kernels_; }
+  cudaStream_t stream() const { return stream_; }
+  int device() const { return device_; }
+  // f16 weight bytes one decode step streams (all projections and the head).
+  static double weight_bytes_per_token();
+
+  static constexpr int kLayers = 24, kW = 1280, kQkv = 3840, kMlp = 5120, kVocab = 8194, kPositions = 1818;
+  static constexpr int kHeads = 20, kHd = 64, kStart = 8192, kStop = 8193;
+  static constexpr int kMaxLen = 4096;  // prefix rows + decode steps held in the KV cache
+
+ private:
+  struct Layer {
+    const float *ln1_g, *ln1_b, *b_attn, *b_proj, *ln2_g, *ln2_b, *b_fc, *b_mproj;
+    const __half *w_attn, *w_proj, *w_fc, *w_mproj;  // [out][in]
+  };
+  void check(cudaError_t e, const char* what);
+  void enqueue_layers();
+  void build_graphs();
+
+  int device_ = 0;
+  cudaStream_t stream_ = nullptr;
+  cudaEvent_t ev_[3] = {nullptr, nullptr, nullptr};
+  void* arena_ = nullptr;
+  void* state_ = nullptr;
+  Layer L_[kLayers];
+  const float *lnf_g_ = nullptr, *lnf_b_ = nullptr, *fn_g_ = nullptr, *fn_b_ = nullptr, *b_head_ = nullptr;
+  const __half* w_head_ = nullptr;
+  const float *emb_ = nullptr, *pos_ = nullptr;  // [8194][1280], [1818][1280] (fp32)
+  // device state
+  float *x_ = nullptr, *h_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *m_ = nullptr, *logits_ = nullptr;
+  float *kc_ = nullptr, *vc_ = nullptr;  // [24][kMaxLen][1280]
+  float* prefix_ = nullptr;              // [kMaxLen][1280]
+  // [0] cache length, [1] prefill row, [2] step, [3] current code, [4] stopped, [5] max steps
+  int* ctl_ = nullptr;
+  uint32_t* codes_ = nullptr;  // [kPositions]
+  cudaGraphExec_t g_prefill_ = nullptr, g_decode_ = nullptr;
+  int decode_kernels_ = 0;
+  float prefill_ms_ = 0.0f, decode_ms_ = 0.0f;
+  int steps_ = 0;
+};
+
+}  // namespace itts

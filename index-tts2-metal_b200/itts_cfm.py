@@ -38,7 +38,15 @@ EXPORTED = [
     "itts_cond_flops", "itts_inspect_voice_bundle", "itts_inspect_model_bundle", "itts_voice_load",
     "itts_pipeline_create", "itts_pipeline_destroy", "itts_pipeline_last_error", "itts_pipeline_create_error",
     "itts_pipeline_synthesize",
+    "itts_gpt_create", "itts_gpt_destroy", "itts_gpt_last_error", "itts_gpt_create_error", "itts_gpt_generate",
+    "itts_gpt_timing", "itts_gpt_launch_kernels", "itts_gpt_weight_bytes_per_token",
 ]
+GPT_WIDTH = 1280
+GPT_VOCAB = 8194
+GPT_START = 8192
+GPT_STOP = 8193
+GPT_MAX_STEPS = 1818
+GPT_MAX_LEN = 4096
 ITTS_COMPONENT_CFM = 0x1
 ITTS_COMPONENT_LENGTH_REGULATOR = 0x2
 ITTS_COMPONENT_BIGVGAN = 0x4
@@ -133,6 +141,14 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_pipeline_last_error": (C.c_char_p, [vp]),
         "itts_pipeline_create_error": (C.c_char_p, []),
         "itts_pipeline_synthesize": (i32, [vp, C.c_char_p, u32, vp, u32, u32, vp, u32, f32, vp, vp]),
+        "itts_gpt_create": (i32, [C.c_char_p, i32, C.POINTER(vp)]),
+        "itts_gpt_destroy": (None, [vp]),
+        "itts_gpt_last_error": (C.c_char_p, [vp]),
+        "itts_gpt_create_error": (C.c_char_p, []),
+        "itts_gpt_generate": (i32, [vp, vp, u32, u32, vp, C.POINTER(u32), vp]),
+        "itts_gpt_timing": (i32, [vp, C.POINTER(f32), C.POINTER(f32)]),
+        "itts_gpt_launch_kernels": (i32, [vp]),
+        "itts_gpt_weight_bytes_per_token": (f64, []),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -540,3 +556,60 @@ class Pipeline:
         if rc != ITTS_OK:
             raise IttsError(rc, self.lib.itts_pipeline_last_error(self.h).decode())
         return wave, mel
+
+
+class GptDecoder:
+    """Cached greedy mel-code decoder bound to one GPU (itts_gpt_create):
+    prefix [P, 1280] -> predicted codes (the stop code last when predicted)
+    and the last step's logits, as run_gpt_kv_greedy_cpu."""
+
+    def __init__(self, bundle_dir: str | Path, device: int = 0):
+        self.lib = load()
+        h = C.c_void_p()
+        rc = self.lib.itts_gpt_create(str(bundle_dir).encode(), int(device), C.byref(h))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_gpt_create_error().decode())
+        self.h = h
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.itts_gpt_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def generate(self, prefix, steps: int) -> tuple[list[int], np.ndarray]:
+        prefix = None if prefix is None or len(prefix) == 0 else _f32(prefix)
+        if prefix is not None and (prefix.ndim != 2 or prefix.shape[1] != GPT_WIDTH):
+            raise ValueError("prefix must be [P, 1280]")
+        P = 0 if prefix is None else prefix.shape[0]
+        codes = np.zeros(max(int(steps), 1), np.uint32)
+        logits = np.empty(GPT_VOCAB, np.float32)
+        n = C.c_uint32(0)
+        rc = self.lib.itts_gpt_generate(self.h, _ptr(prefix), P, int(steps), _ptr(codes), C.byref(n), _ptr(logits))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_gpt_last_error(self.h).decode())
+        return [int(c) for c in codes[:n.value]], logits
+
+    def timing(self) -> tuple[float, float]:
+        """Device ms of the last generate's (prefill, decode)."""
+        a, b = C.c_float(0.0), C.c_float(0.0)
+        self.lib.itts_gpt_timing(self.h, C.byref(a), C.byref(b))
+        return a.value, b.value
+
+    def launch_kernels(self) -> int:
+        return int(self.lib.itts_gpt_launch_kernels(self.h))
+
+    @staticmethod
+    def weight_bytes_per_token() -> float:
+        return float(load().itts_gpt_weight_bytes_per_token())

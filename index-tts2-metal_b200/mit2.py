@@ -451,28 +451,31 @@ def gpt_tensor_specs() -> list[tuple[str, tuple[int, ...], str]]:
     return s
 
 
-def make_gpt_tensors(seed: int) -> list[tuple[str, np.ndarray]]:
+def make_gpt_tensors(seed: int, stop_bias: float | None = None) -> list[tuple[str, np.ndarray]]:
     """Deterministic synthetic GPT decoder weights (f16): linear weights and
     embeddings N(0, 0.02) (GPT-2's initialisation scale), biases N(0, 0.02),
-    LayerNorm gammas 1 + N(0, 0.02)."""
+    LayerNorm gammas 1 + N(0, 0.02). stop_bias, when given, replaces the mel
+    head's bias of the stop code (8193), to make the decode stop early."""
     rng = np.random.default_rng(seed)
     out = []
     for name, shape, kind in gpt_tensor_specs():
         a = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
         if kind == "gamma":
             a += np.float32(1.0)
+        if name == "gpt.mel_head.bias" and stop_bias is not None:
+            a[GPT_VOCAB - 1] = np.float32(stop_bias)
         out.append((name, a.astype(np.float16)))
     return out
 
 
-def make_gpt_bundle(out_dir: str | Path, seed: int = 0) -> Path:
+def make_gpt_bundle(out_dir: str | Path, seed: int = 0, stop_bias: float | None = None) -> Path:
     """Write the synthetic GPT decoder bundle (about 1 GB); skips work when an identical one exists."""
     out = Path(out_dir)
     stamp = out / ".synthetic"
-    key = f"gpt seed={seed} v1"
+    key = f"gpt seed={seed} v1" + ("" if stop_bias is None else f" stop_bias={float(stop_bias)!r}")
     if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():
         return out
-    write_bundle(out, make_gpt_tensors(seed), metadata={"synthetic": True, "seed": seed, "model": "gpt"})
+    write_bundle(out, make_gpt_tensors(seed, stop_bias), metadata={"synthetic": True, "seed": seed, "model": "gpt"})
     stamp.write_text(key)
     return out
 

@@ -172,3 +172,21 @@ def test_condition_flops_and_specs():
     names = [n for n, _, _ in mit2.length_regulator_tensor_specs()]
     assert len(names) == len(set(names)) == 20
     assert names[0] == "s2mel.net.length_regulator.content_in_proj.weight"
+
+
+def test_gpt_create_fails_loudly_without_gpu_or_bundle(tmp_path):
+    import itts_cfm
+
+    with pytest.raises(itts_cfm.IttsError) as e:
+        itts_cfm.GptDecoder(tmp_path / "missing", device=0)
+    assert e.value.code in (itts_cfm.ITTS_ECUDA, itts_cfm.ITTS_ENODEV, itts_cfm.ITTS_EBUNDLE)
+
+
+def test_gpt_specs_and_weight_bytes():
+    import itts_cfm
+
+    specs = mit2.gpt_tensor_specs()
+    names = [n for n, _, _ in specs]
+    assert len(names) == len(set(names)) == 24 * 12 + 8
+    w = sum(int(np.prod(s)) for n, s, k in specs if k == "w")
+    assert itts_cfm.GptDecoder.weight_bytes_per_token() == 2.0 * w  # every linear weight once per token
