@@ -12,6 +12,8 @@
 #include <vector>
 
 #include "bundle.hpp"
+#include "launch.cuh"
+#include "ptx.cuh"
 
 namespace itts {
 
@@ -19,24 +21,31 @@ namespace {
 
 constexpr int kW = GptDecoder::kW;
 constexpr int kMaxLen = GptDecoder::kMaxLen;
-constexpr int kDecodeChunk = 8;  // decode steps per host check of the stop flag
+constexpr int kHeads = GptDecoder::kHeads;
+constexpr int kDecodeChunk = 8;   // decode steps per host check of the stop flag
+constexpr int kSplits = 7;        // key ranges per head in the attention (7 x 20 heads = 140 CTAs)
+constexpr int kPart = 66;         // per (head, range) partial: max, sum, 64 accumulators
+constexpr int kSplitKeys = (kMaxLen + kSplits - 1) / kSplits + 1;  // longest key range
 
-enum { kProPlain = 0, kProLn = 1, kProLn2 = 2 };
+enum { kProPlain = 0, kProLn = 1, kProLn2 = 2, kProAttn = 3 };
 enum { kEpiBias = 0, kEpiGelu = 1, kEpiResid = 2 };
 
 struct GemvArgs {
-  const float* x;  // [K] input row
+  const float* x;                  // [K] input row (kProAttn: the attention partials)
   const float *g1, *b1, *g2, *b2;  // LayerNorm(s) of the prologue
-  const __half* w;     // [N][K] f16
-  const float* bias;   // [N]
-  const float* resid;  // [N] (kEpiResid)
-  float* y;            // [N]
-  int n;
-  const int* stopped;  // nonzero: the decode has ended, do nothing
+  const __half* w;                 // [N][K] f16
+  const float* bias;               // [N]
+  const float* resid;              // [N] (kEpiResid)
+  float* y;                        // [N]
+  int n;                           // rows
+  int rpc;                         // rows per CTA
+  const int* ctl;                  // ctl[4] nonzero: the decode has ended, do nothing
+  unsigned int* status;            // bounded-wait failures
 };
 
-// Sum of one value per thread over a 256-thread block, returned to every
+// Sum of one value per thread over an NT-thread block, returned to every
 // thread (fixed reduction tree: deterministic).
+template <int NT>
 __device__ __forceinline__ float block_sum_all(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -44,11 +53,12 @@ __device__ __forceinline__ float block_sum_all(float v, float* red) {
   __syncthreads();
   float t = 0.0f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) t += red[w];
+  for (int w = 0; w < NT / 32; ++w) t += red[w];
   __syncthreads();
   return t;
 }
 
+template <int NT>
 __device__ __forceinline__ float block_max_all(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -56,7 +66,7 @@ __device__ __forceinline__ float block_max_all(float v, float* red) {
   __syncthreads();
   float t = red[0];
 #pragma unroll
-  for (int w = 1; w < 8; ++w) t = fmaxf(t, red[w]);
+  for (int w = 1; w < NT / 32; ++w) t = fmaxf(t, red[w]);
   __syncthreads();
   return t;
 }
@@ -64,20 +74,20 @@ __device__ __forceinline__ float block_max_all(float v, float* red) {
 // cpu_layernorm (runtime/impl/tokenizer_tests.cpp:2992-3010) on the row held
 // in shared memory: mean, biased variance, (x - mean) * (1 / sqrt(var + 1e-5))
 // * gamma + beta.
-template <int K>
+template <int K, int NT>
 __device__ __forceinline__ void layer_norm_smem(float* xs, const float* __restrict__ g, const float* __restrict__ b,
                                                 float* red) {
   float s = 0.0f;
-  for (int i = threadIdx.x; i < K; i += 256) s += xs[i];
-  const float mean = block_sum_all(s, red) / static_cast<float>(K);
+  for (int i = threadIdx.x; i < K; i += NT) s += xs[i];
+  const float mean = block_sum_all<NT>(s, red) / static_cast<float>(K);
   float v = 0.0f;
-  for (int i = threadIdx.x; i < K; i += 256) {
+  for (int i = threadIdx.x; i < K; i += NT) {
     const float d = xs[i] - mean;
     v += d * d;
   }
-  const float var = block_sum_all(v, red) / static_cast<float>(K);
+  const float var = block_sum_all<NT>(v, red) / static_cast<float>(K);
   const float inv = 1.0f / sqrtf(var + 1e-5f);
-  for (int i = threadIdx.x; i < K; i += 256) xs[i] = (xs[i] - mean) * inv * g[i] + b[i];
+  for (int i = threadIdx.x; i < K; i += NT) xs[i] = (xs[i] - mean) * inv * g[i] + b[i];
   __syncthreads();
 }
 
@@ -88,16 +98,6 @@ __device__ __forceinline__ float gelu_new(float x) {
   if (x < -10.0f) return 0.0f;
   const float c = 0.7978845608028654f;
   return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
-}
-
-// Streaming 16-byte load (evict-first). Volatile so that the compiler keeps
-// every load of a row batch ahead of the first multiply.
-__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.global.cs.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
 }
 
 __device__ __forceinline__ float dot8(const uint4 w, const float* xs) {
@@ -118,88 +118,171 @@ __device__ __forceinline__ float dot8(const uint4 w, const float* xs) {
   return s;
 }
 
-// y[n] = epilogue(W[n,:] . prologue(x) + bias[n]) for the R rows of each of
-// the block's 8 warps. A warp streams its rows' f16 weights in 16-byte chunks
-// (lane l takes chunks l, l+32, ...: 512 contiguous bytes per warp load),
-// every load of the rows issued before the first multiply; fp32 products,
-// fp32 accumulation, a fixed butterfly across the warp.
-template <int K, int R, int PRO, int EPI>
-__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
-  if (*a.stopped) return;
-  __shared__ __align__(16) float xs[K];
-  __shared__ float red[8];
-  for (int i = threadIdx.x; i < K; i += 256) xs[i] = a.x[i];
-  __syncthreads();
-  if (PRO >= kProLn) layer_norm_smem<K>(xs, a.g1, a.b1, red);
-  if (PRO == kProLn2) layer_norm_smem<K>(xs, a.g2, a.b2, red);
-  constexpr int C = K / 256;  // 16-byte chunks per lane per row
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = (blockIdx.x * 8 + warp) * R;
-  uint4 wv[R][C];
+// Merges the attention's per-range partials into the heads' outputs
+// (1280 values in xs): M = max_r m_r, out = sum_r acc_r e^(m_r - M) /
+// sum_r l_r e^(m_r - M), ranges in index order.
+template <int NT>
+__device__ __forceinline__ void attn_combine_smem(const float* __restrict__ part, float* xs) {
+  for (int i = threadIdx.x; i < kW; i += NT) {
+    const int h = i >> 6, d = i & 63;
+    const float* p = part + static_cast<size_t>(h) * kSplits * kPart;
+    float M = -INFINITY;
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int n = row0 + r;
-    const uint4* wr = reinterpret_cast<const uint4*>(a.w + static_cast<size_t>(n < a.n ? n : 0) * K);
+    for (int r = 0; r < kSplits; ++r)
+      if (p[r * kPart + 1] > 0.0f) M = fmaxf(M, p[r * kPart]);
+    float L = 0.0f, A = 0.0f;
 #pragma unroll
-    for (int c = 0; c < C; ++c) wv[r][c] = ld_stream(wr + lane + 32 * c);
+    for (int r = 0; r < kSplits; ++r) {
+      const float l = p[r * kPart + 1];
+      if (l > 0.0f) {
+        const float e = expf(p[r * kPart] - M);
+        L = fmaf(l, e, L);
+        A = fmaf(p[r * kPart + 2 + d], e, A);
+      }
+    }
+    xs[i] = A / L;
   }
-  asm volatile("" ::: "memory");  // the shared-memory reads of x stay behind the weight loads
-  float acc[R];
+  __syncthreads();
+}
+
+// Weight load that bypasses L1 (each weight byte is read once per token).
+// Volatile: every weight load of the kernel stays ahead of the dependency
+// wait that follows them.
+__device__ __forceinline__ uint4 ldg_weights(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+constexpr int kGemvThreads = 512;
+
+// y[n] = epilogue(W[n,:] . prologue(x) + bias[n]). The work is cut into
+// tasks (row, segment of K / SEG columns); warp w of CTA b takes tasks
+// b * tpc + w + 16 i (i < RW). Every weight load of the CTA's tasks (f16,
+// 16 bytes per lane, 512 contiguous bytes per warp load) and the biases are
+// issued BEFORE the kernel waits on its predecessor (programmatic dependent
+// launch), so the weight stream overlaps the previous kernel's tail and the
+// prologue; then the input row is read (and normalised, or the attention
+// partials merged) into shared memory and each warp reduces its tasks from
+// registers: fp32 products and accumulation, a fixed butterfly, segments
+// summed in order.
+template <int K, int SEG, int RW, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) gemv_stream_kernel(GemvArgs a) {
+  constexpr int NT = kGemvThreads, NW = NT / 32;
+  constexpr int KS = K / SEG;  // columns per task
+  constexpr int C = KS / 256;  // 16-byte loads per lane per task
+  static_assert(KS % 256 == 0, "segment width");
+  __shared__ __align__(16) float xs[K];
+  __shared__ float red[NW];
+  __shared__ float part[SEG > 1 ? NW * RW : 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * a.rpc;  // rpc = tasks per CTA here (a multiple of SEG)
+  const int tend = min(t0 + a.rpc, a.n * SEG);
+  uint4 wv[RW][C];
+  float bias[RW];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
+  for (int i = 0; i < RW; ++i) {
+    int t = t0 + warp + NW * i;
+    if (t >= tend) t = t0;  // a valid row; the result is discarded
+    const int row = t / SEG, seg = t - row * SEG;
+    const uint4* wr = reinterpret_cast<const uint4*>(a.w + static_cast<size_t>(row) * K + seg * KS);
+#pragma unroll
+    for (int c = 0; c < C; ++c) wv[i][c] = ldg_weights(wr + lane + 32 * c);
+    bias[i] = a.bias[row];
+  }
+  griddep_launch();
+  griddep_wait();
+  if (a.ctl[4]) return;
+  if (PRO == kProAttn) {
+    attn_combine_smem<NT>(a.x, xs);
+  } else {
+    for (int i = threadIdx.x; i < K; i += NT) xs[i] = a.x[i];
+    __syncthreads();
+    if (PRO >= kProLn) layer_norm_smem<K, NT>(xs, a.g1, a.b1, red);
+    if (PRO == kProLn2) layer_norm_smem<K, NT>(xs, a.g2, a.b2, red);
+  }
+#pragma unroll
+  for (int i = 0; i < RW; ++i) {
+    const int t = t0 + warp + NW * i;
+    const int row = t / SEG, seg = t - row * SEG;
     float s = 0.0f;
 #pragma unroll
-    for (int c = 0; c < C; ++c) s += dot8(wv[r][c], xs + (lane + 32 * c) * 8);
+    for (int c = 0; c < C; ++c) s += dot8(wv[i][c], xs + seg * KS + (lane + 32 * c) * 8);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    acc[r] = s;
+    if (lane == 0 && t < tend) {
+      if (SEG == 1) {
+        float v = s + bias[i];
+        if (EPI == kEpiGelu) v = gelu_new(v);
+        if (EPI == kEpiResid) v = a.resid[row] + v;
+        a.y[row] = v;
+      } else {
+        part[warp + NW * i] = s;  // task index within the CTA
+      }
+    }
   }
-  if (lane == 0) {
+  if (SEG > 1) {
+    __syncthreads();
+    for (int j = threadIdx.x * SEG; j < tend - t0; j += NT * SEG) {
+      const int row = (t0 + j) / SEG;
+      float s = 0.0f;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int n = row0 + r;
-      if (n >= a.n) break;
-      float v = acc[r] + a.bias[n];
+      for (int q = 0; q < SEG; ++q) s += part[j + q];
+      float v = s + a.bias[row];
       if (EPI == kEpiGelu) v = gelu_new(v);
-      if (EPI == kEpiResid) v = a.resid[n] + v;
-      a.y[n] = v;
+      if (EPI == kEpiResid) v = a.resid[row] + v;
+      a.y[row] = v;
     }
   }
 }
 
-// One head of the cached single-query attention
+// One key range of one head of the cached single-query attention
 // (cpu_attention_single_query, runtime/impl/tokenizer_tests.cpp:4034-4061,
-// over the cache of runtime/impl/gpt.cpp:1060-1210): appends this token's K
-// and V at row len of the layer's cache, then scores = q . k * (1/8) over the
-// len + 1 keys, p = exp(s - max) / sum, out = sum_j p_j v_j.
+// over the cache of runtime/impl/gpt.cpp:1060-1210). The len + 1 keys (the
+// cache plus this token's, read straight from qkv) are cut into kSplits
+// ranges; range r of head h writes its partial (m = max score, l = sum
+// e^(s - m), acc = sum e^(s - m) v) for the combine in the next projection.
+// Range 0 also appends this token's K and V at row len of the layer's cache.
 __global__ void __launch_bounds__(256) gpt_attn_kernel(const float* __restrict__ qkv, float* __restrict__ kc,
-                                                       float* __restrict__ vc, float* __restrict__ out,
+                                                       float* __restrict__ vc, float* __restrict__ part,
                                                        const int* __restrict__ ctl) {
-  if (ctl[4]) return;
-  extern __shared__ float s[];  // [len + 1] scores, then probabilities
+  __shared__ float s[kSplitKeys];
   __shared__ __align__(16) float q[64];
   __shared__ float red[8];
-  __shared__ float part[8][64];
-  const int h = blockIdx.x, tid = threadIdx.x;
+  __shared__ float acc_w[8][64];
+  griddep_launch();
+  griddep_wait();
+  if (ctl[4]) return;
+  const int r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int len = ctl[0], n = len + 1;
-  const size_t cur = static_cast<size_t>(len) * kW + h * 64;
-  if (tid < 64) {
-    q[tid] = qkv[h * 64 + tid];
-    kc[cur + tid] = qkv[kW + h * 64 + tid];
-  } else if (tid < 128) {
-    vc[cur + tid - 64] = qkv[2 * kW + h * 64 + tid - 64];
+  const int chunk = (n + kSplits - 1) / kSplits;
+  const int j0 = r * chunk, j1 = min(n, j0 + chunk);
+  const float* kcur = qkv + kW + h * 64;
+  const float* vcur = qkv + 2 * kW + h * 64;
+  if (r == 0) {
+    const size_t cur = static_cast<size_t>(len) * kW + h * 64;
+    if (tid < 64) kc[cur + tid] = kcur[tid];
+    else if (tid < 128) vc[cur + tid - 64] = vcur[tid - 64];
   }
+  float* out = part + (static_cast<size_t>(h) * kSplits + r) * kPart;
+  if (j0 >= j1) {  // empty range (short caches)
+    if (tid < kPart) out[tid] = tid == 0 ? -INFINITY : 0.0f;
+    return;
+  }
+  if (tid < 64) q[tid] = qkv[h * 64 + tid];
   __syncthreads();
-  // scores: 16 lanes per key (a float4 of the 64 dims each), 4 keys in flight
+  // scores: 16 lanes per key (a float4 of the 64 dims each), 4 keys in flight per group
   const int g = tid >> 4, l = tid & 15;
   const float4 qv = reinterpret_cast<const float4*>(q)[l];
-  const float* kh = kc + h * 64 + 4 * l;
-  for (int base = 0; base < n; base += 64) {
+  for (int base = j0; base < j1; base += 64) {
     float4 kv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int j = base + g + 16 * u;
-      kv[u] = j < n ? *reinterpret_cast<const float4*>(kh + static_cast<size_t>(j) * kW) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float* kp = j == len ? kcur : kc + static_cast<size_t>(j) * kW + h * 64;
+      kv[u] = j < j1 ? *reinterpret_cast<const float4*>(kp + 4 * l) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -210,49 +293,52 @@ __global__ void __launch_bounds__(256) gpt_attn_kernel(const float* __restrict__
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
       const int j = base + g + 16 * u;
-      if (l == 0 && j < n) s[j] = d * 0.125f;
+      if (l == 0 && j < j1) s[j - j0] = d * 0.125f;
     }
   }
   __syncthreads();
-  float mx = -FLT_MAX;
-  for (int j = tid; j < n; j += 256) mx = fmaxf(mx, s[j]);
-  mx = block_max_all(mx, red);
+  const int cnt = j1 - j0;
+  float mx = -INFINITY;
+  for (int j = tid; j < cnt; j += 256) mx = fmaxf(mx, s[j]);
+  mx = block_max_all<256>(mx, red);
   float den = 0.0f;
-  for (int j = tid; j < n; j += 256) {
+  for (int j = tid; j < cnt; j += 256) {
     const float e = expf(s[j] - mx);
     s[j] = e;
     den += e;
   }
-  den = block_sum_all(den, red);
-  for (int j = tid; j < n; j += 256) s[j] = s[j] / den;
-  __syncthreads();
-  // out: warp w takes keys w, w+8, ...; lane l dims 2l, 2l+1
+  den = block_sum_all<256>(den, red);  // also orders the writes of s before the reads below
+  // acc: warp w takes keys w, w+8, ...; lane dims 2 lane, 2 lane + 1
   const int w = tid >> 5, lane = tid & 31;
-  const float* vh = vc + h * 64 + 2 * lane;
   float2 acc = make_float2(0.f, 0.f);
-  for (int base = 0; base < n; base += 32) {
+  for (int base = 0; base < cnt; base += 32) {
     float2 vv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int j = base + w + 8 * u;
-      vv[u] = j < n ? *reinterpret_cast<const float2*>(vh + static_cast<size_t>(j) * kW) : make_float2(0.f, 0.f);
+      const int jj = j0 + j;
+      const float* vp = jj == len ? vcur : vc + static_cast<size_t>(jj) * kW + h * 64;
+      vv[u] = j < cnt ? *reinterpret_cast<const float2*>(vp + 2 * lane) : make_float2(0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int j = base + w + 8 * u;
-      const float p = j < n ? s[j] : 0.0f;
+      const float p = j < cnt ? s[j] : 0.0f;
       acc.x = fmaf(p, vv[u].x, acc.x);
       acc.y = fmaf(p, vv[u].y, acc.y);
     }
   }
-  part[w][2 * lane] = acc.x;
-  part[w][2 * lane + 1] = acc.y;
+  acc_w[w][2 * lane] = acc.x;
+  acc_w[w][2 * lane + 1] = acc.y;
   __syncthreads();
   if (tid < 64) {
     float o = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o += part[i][tid];
-    out[h * 64 + tid] = o;
+    for (int i = 0; i < 8; ++i) o += acc_w[i][tid];
+    out[2 + tid] = o;
+  } else if (tid == 64) {
+    out[0] = mx;
+    out[1] = den;
   }
 }
 
@@ -260,6 +346,8 @@ __global__ void __launch_bounds__(256) gpt_attn_kernel(const float* __restrict__
 // 1545-1554): mel_embedding[code] + mel_pos_embedding[step].
 __global__ void __launch_bounds__(256) gpt_embed_kernel(const float* __restrict__ emb, const float* __restrict__ pos,
                                                         float* __restrict__ x, const int* __restrict__ ctl) {
+  griddep_launch();
+  griddep_wait();
   if (ctl[4]) return;
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i < kW) x[i] = emb[static_cast<size_t>(ctl[3]) * kW + i] + pos[static_cast<size_t>(ctl[2]) * kW + i];
@@ -268,11 +356,15 @@ __global__ void __launch_bounds__(256) gpt_embed_kernel(const float* __restrict_
 // Prefill input: prefix row ctl[1].
 __global__ void __launch_bounds__(256) gpt_prefix_row_kernel(const float* __restrict__ prefix, float* __restrict__ x,
                                                              const int* __restrict__ ctl) {
+  griddep_launch();
+  griddep_wait();
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i < kW) x[i] = prefix[static_cast<size_t>(ctl[1]) * kW + i];
 }
 
 __global__ void gpt_prefill_advance_kernel(int* ctl) {
+  griddep_launch();
+  griddep_wait();
   ctl[0] += 1;
   ctl[1] += 1;
 }
@@ -282,8 +374,10 @@ __global__ void gpt_prefill_advance_kernel(int* ctl) {
 // the cache, and stops after the stop code or the last allowed step.
 __global__ void __launch_bounds__(1024) gpt_argmax_kernel(const float* __restrict__ logits, int n,
                                                           uint32_t* __restrict__ codes, int* __restrict__ ctl) {
-  if (ctl[4]) return;
   __shared__ float bv_s[32];
+  griddep_launch();
+  griddep_wait();
+  if (ctl[4]) return;
   __shared__ int bi_s[32];
   float bv = -INFINITY;
   int bi = INT_MAX;
@@ -325,10 +419,14 @@ __global__ void __launch_bounds__(1024) gpt_argmax_kernel(const float* __restric
   }
 }
 
-template <int K, int R, int PRO, int EPI>
-void launch_gemv(const GemvArgs& a, cudaStream_t st) {
-  const int rows_per_block = 8 * R;
-  gemv_kernel<K, R, PRO, EPI><<<(a.n + rows_per_block - 1) / rows_per_block, 256, 0, st>>>(a);
+// Grid of a projection: tasks (row, segment) in CTAs of 16 warps x RW tasks.
+template <int K, int SEG, int RW, int PRO, int EPI>
+cudaError_t launch_gemv(GemvArgs a, cudaStream_t st) {
+  const int tpc = kGemvThreads / 32 * RW;
+  static_assert((kGemvThreads / 32 * RW) % SEG == 0, "rows must not straddle CTAs");
+  a.rpc = tpc;
+  const int grid = (a.n * SEG + tpc - 1) / tpc;
+  return launch_pdl(gemv_stream_kernel<K, SEG, RW, PRO, EPI>, dim3(grid), dim3(kGemvThreads), 0, st, a);
 }
 
 // Transposes a [rows][cols] f16 payload to [cols][rows] (32x32 tiles).
@@ -457,11 +555,11 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
     off += (bytes + 255) & ~size_t(255);
     return o;
   };
-  const size_t o_x = carve(kW * 4), o_h = carve(kW * 4), o_qkv = carve(kQkv * 4), o_attn = carve(kW * 4),
+  const size_t o_x = carve(kW * 4), o_h = carve(kW * 4), o_qkv = carve(kQkv * 4), o_part = carve(static_cast<size_t>(kHeads) * kSplits * kPart * 4),
                o_m = carve(kMlp * 4), o_logits = carve(kVocab * 4),
                o_kc = carve(static_cast<size_t>(kLayers) * kMaxLen * kW * 4),
                o_vc = carve(static_cast<size_t>(kLayers) * kMaxLen * kW * 4),
-               o_prefix = carve(static_cast<size_t>(kMaxLen) * kW * 4), o_ctl = carve(8 * 4),
+               o_prefix = carve(static_cast<size_t>(kMaxLen) * kW * 4), o_ctl = carve(8 * 4), o_status = carve(4),
                o_codes = carve(static_cast<size_t>(kPositions) * 4);
   check(cudaMalloc(&state_, off), "gpt state cudaMalloc");
   check(cudaMemset(state_, 0, off), "gpt state memset");
@@ -469,18 +567,18 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
   x_ = reinterpret_cast<float*>(s + o_x);
   h_ = reinterpret_cast<float*>(s + o_h);
   qkv_ = reinterpret_cast<float*>(s + o_qkv);
-  attn_ = reinterpret_cast<float*>(s + o_attn);
+  part_ = reinterpret_cast<float*>(s + o_part);
   m_ = reinterpret_cast<float*>(s + o_m);
   logits_ = reinterpret_cast<float*>(s + o_logits);
   kc_ = reinterpret_cast<float*>(s + o_kc);
   vc_ = reinterpret_cast<float*>(s + o_vc);
   prefix_ = reinterpret_cast<float*>(s + o_prefix);
   ctl_ = reinterpret_cast<int*>(s + o_ctl);
+  status_ = reinterpret_cast<unsigned int*>(s + o_status);
   codes_ = reinterpret_cast<uint32_t*>(s + o_codes);
   check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   for (auto& e : ev_) check(cudaEventCreate(&e), "cudaEventCreate");
-  check(cudaFuncSetAttribute(gpt_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxLen * 4),
-        "attention shared memory");
+  check(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device), "SM count");
   build_graphs();
 }
 
@@ -501,22 +599,25 @@ GptDecoder::~GptDecoder() {
 // the cache with this token appended; h = x + c_proj(a); m = gelu_new(c_fc(
 // ln_2(h))); x = h + mlp.c_proj(m).
 void GptDecoder::enqueue_layers() {
-  const int* stopped = ctl_ + 4;
   for (int l = 0; l < kLayers; ++l) {
     const Layer& L = L_[l];
     float* kc = kc_ + static_cast<size_t>(l) * kMaxLen * kW;
     float* vc = vc_ + static_cast<size_t>(l) * kMaxLen * kW;
-    launch_gemv<kW, 2, kProLn, kEpiBias>({x_, L.ln1_g, L.ln1_b, nullptr, nullptr, L.w_attn, L.b_attn, nullptr, qkv_, kQkv, stopped},
-                                         stream_);
-    gpt_attn_kernel<<<kHeads, 256, kMaxLen * 4, stream_>>>(qkv_, kc, vc, attn_, ctl_);
-    launch_gemv<kW, 1, kProPlain, kEpiResid>({attn_, nullptr, nullptr, nullptr, nullptr, L.w_proj, L.b_proj, x_, h_, kW, stopped},
-                                             stream_);
-    launch_gemv<kW, 2, kProLn, kEpiGelu>({h_, L.ln2_g, L.ln2_b, nullptr, nullptr, L.w_fc, L.b_fc, nullptr, m_, kMlp, stopped},
-                                         stream_);
-    launch_gemv<kMlp, 1, kProPlain, kEpiResid>({m_, nullptr, nullptr, nullptr, nullptr, L.w_mproj, L.b_mproj, h_, x_, kW, stopped},
-                                               stream_);
+    check(launch_gemv<kW, 1, 4, kProLn, kEpiBias>(
+              {x_, L.ln1_g, L.ln1_b, nullptr, nullptr, L.w_attn, L.b_attn, nullptr, qkv_, kQkv, 0, ctl_, status_}, stream_),
+          "c_attn");
+    check(launch_pdl(gpt_attn_kernel, dim3(kSplits, kHeads), dim3(256), 0, stream_, qkv_, kc, vc, part_, ctl_),
+          "attention");
+    check(launch_gemv<kW, 1, 2, kProAttn, kEpiResid>(
+              {part_, nullptr, nullptr, nullptr, nullptr, L.w_proj, L.b_proj, x_, h_, kW, 0, ctl_, status_}, stream_),
+          "attn.c_proj");
+    check(launch_gemv<kW, 1, 4, kProLn, kEpiGelu>(
+              {h_, L.ln2_g, L.ln2_b, nullptr, nullptr, L.w_fc, L.b_fc, nullptr, m_, kMlp, 0, ctl_, status_}, stream_),
+          "c_fc");
+    check(launch_gemv<kMlp, 2, 1, kProPlain, kEpiResid>(
+              {m_, nullptr, nullptr, nullptr, nullptr, L.w_mproj, L.b_mproj, h_, x_, kW, 0, ctl_, status_}, stream_),
+          "mlp.c_proj");
   }
-  check(cudaGetLastError(), "layer launches");
 }
 
 void GptDecoder::build_graphs() {
@@ -548,21 +649,21 @@ void GptDecoder::build_graphs() {
   };
   capture(
       [&] {
-        gpt_prefix_row_kernel<<<kW / 256, 256, 0, stream_>>>(prefix_, x_, ctl_);
+        check(launch_pdl(gpt_prefix_row_kernel, dim3(kW / 256), dim3(256), 0, stream_, prefix_, x_, ctl_),
+              "prefix row");
         enqueue_layers();
-        gpt_prefill_advance_kernel<<<1, 1, 0, stream_>>>(ctl_);
-        check(cudaGetLastError(), "prefill launches");
+        check(launch_pdl(gpt_prefill_advance_kernel, dim3(1), dim3(1), 0, stream_, ctl_), "prefill advance");
       },
       &g_prefill_, nullptr);
   capture(
       [&] {
-        gpt_embed_kernel<<<kW / 256, 256, 0, stream_>>>(emb_, pos_, x_, ctl_);
+        check(launch_pdl(gpt_embed_kernel, dim3(kW / 256), dim3(256), 0, stream_, emb_, pos_, x_, ctl_), "embed");
         enqueue_layers();
         // ln_f then final_norm (runtime/impl/gpt.cpp:1901-1902), the mel head, argmax
-        launch_gemv<kW, 2, kProLn2, kEpiBias>(
-            {x_, lnf_g_, lnf_b_, fn_g_, fn_b_, w_head_, b_head_, nullptr, logits_, kVocab, ctl_ + 4}, stream_);
-        gpt_argmax_kernel<<<1, 1024, 0, stream_>>>(logits_, kVocab, codes_, ctl_);
-        check(cudaGetLastError(), "decode launches");
+        check(launch_gemv<kW, 1, 4, kProLn2, kEpiBias>(
+                  {x_, lnf_g_, lnf_b_, fn_g_, fn_b_, w_head_, b_head_, nullptr, logits_, kVocab, 0, ctl_, status_}, stream_),
+              "mel head");
+        check(launch_pdl(gpt_argmax_kernel, dim3(1), dim3(1024), 0, stream_, logits_, kVocab, codes_, ctl_), "argmax");
       },
       &g_decode_, &decode_kernels_);
 }
@@ -594,6 +695,12 @@ int GptDecoder::generate(const float* prefix, int P, int max_steps, uint32_t* co
   int ctl[8];
   check(cudaMemcpyAsync(ctl, ctl_, sizeof(ctl), cudaMemcpyDeviceToHost, stream_), "gpt control read");
   check(cudaStreamSynchronize(stream_), "gpt sync");
+  unsigned int st = 0;
+  check(cudaMemcpy(&st, status_, sizeof(st), cudaMemcpyDeviceToHost), "gpt status read");
+  if (st != 0) {
+    check(cudaMemset(status_, 0, sizeof(st)), "gpt status clear");
+    throw std::runtime_error("timeout: a GPT kernel abandoned a bounded wait (device status " + std::to_string(st) + ")");
+  }
   const int n = ctl[2];
   if (n < 1 || n > max_steps) throw std::runtime_error("cuda: gpt: decoder produced an invalid step count");
   check(cudaMemcpyAsync(codes, codes_, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, stream_), "codes read");

@@ -10,11 +10,15 @@
 // stop code 8193.
 //
 // One token at a time is bandwidth-bound (about 1 GB of f16 weights per
-// token), so every projection is a GEMV kernel over f16 weights with fp32
-// activations and accumulation (LayerNorm fused into its prologue); the KV
-// cache is fp32. A CUDA graph per token (prefill row or decode step) reads
-// the row, the cache length, the step and the current code from device
-// memory, so the host only synchronises once per chunk of steps.
+// token), so every projection is a weight-streaming GEMV: one CTA per SM
+// bulk-copies its rows of the f16 weight matrix into shared memory before it
+// waits on the previous kernel (programmatic dependent launch), so the weight
+// streams of consecutive projections overlap the dependent chain; fp32
+// activations and accumulation, LayerNorm (and the attention's split-softmax
+// combine) in the prologue. The attention splits each head's keys over 7
+// CTAs. The KV cache is fp32. A CUDA graph per token (prefill row or decode
+// step) reads the row, the cache length, the step and the current code from
+// device memory, so the host only synchronises once per chunk of steps.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -69,12 +73,15 @@ class GptDecoder {
   const __half* w_head_ = nullptr;
   const float *emb_ = nullptr, *pos_ = nullptr;  // [8194][1280], [1818][1280] (fp32)
   // device state
-  float *x_ = nullptr, *h_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *m_ = nullptr, *logits_ = nullptr;
+  float *x_ = nullptr, *h_ = nullptr, *qkv_ = nullptr, *m_ = nullptr, *logits_ = nullptr;
+  float* part_ = nullptr;  // attention partials [20 heads][key ranges][max, sum, 64 accumulators]
   float *kc_ = nullptr, *vc_ = nullptr;  // [24][kMaxLen][1280]
   float* prefix_ = nullptr;              // [kMaxLen][1280]
   // [0] cache length, [1] prefill row, [2] step, [3] current code, [4] stopped, [5] max steps
   int* ctl_ = nullptr;
   uint32_t* codes_ = nullptr;  // [kPositions]
+  unsigned int* status_ = nullptr;  // nonzero: a kernel abandoned a bounded wait
+  int sms_ = 148;
   cudaGraphExec_t g_prefill_ = nullptr, g_decode_ = nullptr;
   int decode_kernels_ = 0;
   float prefill_ms_ = 0.0f, decode_ms_ = 0.0f;

@@ -21,6 +21,7 @@ enum DevStatusCode : unsigned int {
   kDevTimeoutEmpty = 2,  // producer waited too long for a free stage
   kDevTimeoutAccum = 3,  // epilogue waited too long for the accumulator
   kDevTimeoutProbe = 6,  // the bounded-wait self-test gave up (as it should)
+  kDevTimeoutBulk = 8,   // a GEMV waited too long for its weight rows (bulk copy)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -88,6 +89,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// Untiled bulk copy global -> shared::cta completing on `bar` (both addresses
+// 16-byte aligned, bytes a multiple of 16; no multicast).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // 3-D tiled TMA load: the box spans several 64-column k-blocks of a row-major
