@@ -412,7 +412,8 @@ def gpt_line(args, rank, world, local, barrier, max_over_ranks, hbm_peak):
     return {"metric": "GPT mel-code decode, tokens/s (cached greedy, one utterance per GPU)",
             "value": n * world / (dec_ms / 1e3), "unit": "tokens/s", "prefix_rows": GPT_PREFIX, "steps": n,
             "ms_per_token": dec_ms / n, "prefill_ms": pre_ms, "prefill_ms_per_row": pre_ms / GPT_PREFIX,
-            "gpu_launches": launches * n + launches * GPT_PREFIX,
+            "gpu_launches": launches,
+            "path": "graphs per token" if os.environ.get("ITTS_GPT_MODE") == "graph" else "one persistent kernel per call",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                          "bytes_per_token": wb + kv, "note": "f16 weights once per token + mean fp32 KV-cache reads"},
             "e2e": {"value": n * world / t_e2e, "unit": "tokens/s (prefill included)",

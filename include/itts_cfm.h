@@ -308,7 +308,8 @@ double itts_cond_flops(uint32_t n_in, uint32_t G);
 #define ITTS_COMPONENT_CFM 0x1u              /* s2mel.net.cfm.estimator.* */
 #define ITTS_COMPONENT_LENGTH_REGULATOR 0x2u /* s2mel.net.length_regulator.* */
 #define ITTS_COMPONENT_BIGVGAN 0x4u          /* bigvgan.* */
-#define ITTS_COMPONENT_ALL 0x7u
+#define ITTS_COMPONENT_GPT 0x8u              /* gpt.* (the mel-code decoder's tensors) */
+#define ITTS_COMPONENT_ALL 0xfu
 
 /* Voice gate: every payload's SHA-256 present and verified; f32 component=voice
  * spk_cond_emb [1,S>0,1024], s2mel_style [1,192], s2mel_prompt [1,P>0,512],
@@ -381,7 +382,8 @@ const char* itts_gpt_create_error(void);
 int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t* codes,
                       uint32_t* n_codes, float* last_logits);
 /* Device time (ms) of the last generate's prefill and decode (no reference
- * counterpart); kernels one decode step launches; f16 weight bytes it streams. */
+ * counterpart); kernel launches of the last generate (1: the whole call is one
+ * persistent kernel); f16 weight bytes one decode step streams. */
 int itts_gpt_timing(const itts_gpt_ctx* ctx, float* prefill_ms, float* decode_ms);
 int itts_gpt_launch_kernels(const itts_gpt_ctx* ctx);
 double itts_gpt_weight_bytes_per_token(void);

@@ -8,7 +8,7 @@
 //   mtts_cfm --cfm BUNDLE T P STEPS CFG IN_PREFIX OUT.f32 [DEVICE]
 //       reads IN_PREFIX.{noise,prompt,cond,style}.f32 (raw little-endian
 //       float32), writes the mel [T,80] to OUT.f32.
-//   mtts_cfm --inspect-model-bundle DIR [cfm,length_regulator,bigvgan]
+//   mtts_cfm --inspect-model-bundle DIR [cfm,length_regulator,bigvgan,gpt]
 //   mtts_cfm --inspect-voice-bundle DIR
 //       the bundle contract gates (reference: runtime/main.cpp:2688-2691);
 //       print the JSON report, exit 0 when the contract holds, 1 otherwise.
@@ -99,6 +99,7 @@ int main(int argc, char** argv) {
         if (comps.find("cfm") != std::string::npos) mask |= ITTS_COMPONENT_CFM;
         if (comps.find("length_regulator") != std::string::npos) mask |= ITTS_COMPONENT_LENGTH_REGULATOR;
         if (comps.find("bigvgan") != std::string::npos) mask |= ITTS_COMPONENT_BIGVGAN;
+        if (comps.find("gpt") != std::string::npos) mask |= ITTS_COMPONENT_GPT;
         rc = itts_inspect_model_bundle(argv[2], mask, &report[0], static_cast<uint32_t>(report.size()));
       }
       std::printf("%s\n", report.c_str());
@@ -106,7 +107,7 @@ int main(int argc, char** argv) {
     }
     std::fprintf(stderr, "usage: mtts_cfm --bench-cfm BUNDLE T STEPS ITERS [DEVICE]\n"
                          "       mtts_cfm --cfm BUNDLE T P STEPS CFG IN_PREFIX OUT.f32 [DEVICE]\n"
-                         "       mtts_cfm --inspect-model-bundle DIR [cfm,length_regulator,bigvgan]\n"
+                         "       mtts_cfm --inspect-model-bundle DIR [cfm,length_regulator,bigvgan,gpt]\n"
                          "       mtts_cfm --inspect-voice-bundle DIR\n");
     return 2;
   } catch (const std::exception& e) {

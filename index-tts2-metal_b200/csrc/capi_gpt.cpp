@@ -21,6 +21,7 @@ int gclassify(const std::exception& e) {
   if (dynamic_cast<const std::invalid_argument*>(&e)) return ITTS_EINVAL_SHAPE;
   const std::string m = e.what();
   if (m.rfind("bundle", 0) == 0 || m.rfind("manifest", 0) == 0 || m.rfind("gpt weights", 0) == 0) return ITTS_EBUNDLE;
+  if (m.rfind("timeout", 0) == 0) return ITTS_ETIMEOUT;
   if (m.rfind("device id", 0) == 0 || m.rfind("this build targets", 0) == 0) return ITTS_ENODEV;
   return ITTS_ECUDA;
 }
@@ -80,7 +81,9 @@ int itts_gpt_timing(const itts_gpt_ctx* ctx, float* prefill_ms, float* decode_ms
   return ITTS_OK;
 }
 
-int itts_gpt_launch_kernels(const itts_gpt_ctx* ctx) { return ctx ? ctx->dec->kernels_per_token() : ITTS_EINVAL_SHAPE; }
+int itts_gpt_launch_kernels(const itts_gpt_ctx* ctx) {
+  return ctx ? static_cast<int>(ctx->dec->last_launches()) : ITTS_EINVAL_SHAPE;
+}
 
 double itts_gpt_weight_bytes_per_token(void) { return itts::GptDecoder::weight_bytes_per_token(); }
 

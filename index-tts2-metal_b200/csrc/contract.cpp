@@ -174,6 +174,17 @@ std::vector<Required> required_for(uint32_t components) {
     r.push_back({"bigvgan.activation_post.upsample.filter", "bigvgan", {1, 1, 12}});
     r.push_back({"bigvgan.conv_post.weight_v", "bigvgan", {1, 24, 7}});
   }
+  if (components & ITTS_COMPONENT_GPT) {  // Conv1D weights are stored [in, out]
+    r.push_back({"gpt.gpt.h.0.attn.c_attn.weight", "gpt", {1280, 3840}});
+    r.push_back({"gpt.gpt.h.12.ln_1.weight", "gpt", {1280}});
+    r.push_back({"gpt.gpt.h.23.mlp.c_fc.weight", "gpt", {1280, 5120}});
+    r.push_back({"gpt.gpt.h.23.mlp.c_proj.weight", "gpt", {5120, 1280}});
+    r.push_back({"gpt.gpt.ln_f.weight", "gpt", {1280}});
+    r.push_back({"gpt.final_norm.weight", "gpt", {1280}});
+    r.push_back({"gpt.mel_head.weight", "gpt", {8194, 1280}});
+    r.push_back({"gpt.mel_embedding.weight", "gpt", {8194, 1280}});
+    r.push_back({"gpt.mel_pos_embedding.emb.weight", "gpt", {1818, 1280}});
+  }
   return r;
 }
 
@@ -223,6 +234,7 @@ int itts_inspect_model_bundle(const char* bundle_dir, uint32_t components, char*
     if (components & ITTS_COMPONENT_CFM) comps += "\"cfm_estimator\"";
     if (components & ITTS_COMPONENT_LENGTH_REGULATOR) comps += std::string(comps.empty() ? "" : ", ") + "\"length_regulator\"";
     if (components & ITTS_COMPONENT_BIGVGAN) comps += std::string(comps.empty() ? "" : ", ") + "\"bigvgan\"";
+    if (components & ITTS_COMPONENT_GPT) comps += std::string(comps.empty() ? "" : ", ") + "\"gpt\"";
     put_report(report, cap,
                head_json("model_bundle_contract", dir, b, in) + ", \"components\": [" + comps +
                    "], \"required_tensors\": [" + list + "]}");

@@ -6,6 +6,7 @@
 #include <cfloat>
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -561,6 +562,10 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
                o_vc = carve(static_cast<size_t>(kLayers) * kMaxLen * kW * 4),
                o_prefix = carve(static_cast<size_t>(kMaxLen) * kW * 4), o_ctl = carve(8 * 4), o_status = carve(4),
                o_codes = carve(static_cast<size_t>(kPositions) * 4);
+  check(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device), "SM count");
+  const size_t o_layers = carve(sizeof(GptLayerPtrs) * kLayers), o_cval = carve(static_cast<size_t>(sms_) * 4),
+               o_cidx = carve(static_cast<size_t>(sms_) * 4), o_bar = carve(4), o_out = carve(16),
+               o_times = carve(4 * 8);
   check(cudaMalloc(&state_, off), "gpt state cudaMalloc");
   check(cudaMemset(state_, 0, off), "gpt state memset");
   uint8_t* s = static_cast<uint8_t*>(state_);
@@ -576,9 +581,21 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
   ctl_ = reinterpret_cast<int*>(s + o_ctl);
   status_ = reinterpret_cast<unsigned int*>(s + o_status);
   codes_ = reinterpret_cast<uint32_t*>(s + o_codes);
+  layers_dev_ = reinterpret_cast<GptLayerPtrs*>(s + o_layers);
+  cand_val_ = reinterpret_cast<float*>(s + o_cval);
+  cand_idx_ = reinterpret_cast<int*>(s + o_cidx);
+  barrier_ = reinterpret_cast<unsigned int*>(s + o_bar);
+  out_ = reinterpret_cast<int*>(s + o_out);
+  times_ = reinterpret_cast<unsigned long long*>(s + o_times);
+  check(cudaMemcpy(layers_dev_, L_, sizeof(GptLayerPtrs) * kLayers, cudaMemcpyHostToDevice), "gpt layer table upload");
   check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   for (auto& e : ev_) check(cudaEventCreate(&e), "cudaEventCreate");
-  check(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device), "SM count");
+  const char* mode = std::getenv("ITTS_GPT_MODE");
+  persistent_ = mode && std::string(mode) == "persistent";
+  if (persistent_) {
+    if (sms_ < gpt_persist_min_grid()) throw std::runtime_error("gpt: too few SMs for the persistent decoder");
+    check(gpt_persist_prepare(), "persistent decoder shared memory");
+  }
   build_graphs();
 }
 
@@ -654,7 +671,7 @@ void GptDecoder::build_graphs() {
         enqueue_layers();
         check(launch_pdl(gpt_prefill_advance_kernel, dim3(1), dim3(1), 0, stream_, ctl_), "prefill advance");
       },
-      &g_prefill_, nullptr);
+      &g_prefill_, &prefill_kernels_);
   capture(
       [&] {
         check(launch_pdl(gpt_embed_kernel, dim3(kW / 256), dim3(256), 0, stream_, emb_, pos_, x_, ctl_), "embed");
@@ -674,12 +691,81 @@ int GptDecoder::generate(const float* prefix, int P, int max_steps, uint32_t* co
   if (P > 0 && !prefix) throw std::invalid_argument("gpt: prefix must be non-null when P > 0");
   if (!codes) throw std::invalid_argument("gpt: codes must be non-null");
   check(cudaSetDevice(device_), "cudaSetDevice");
-  static_assert(kStart == 8192, "start code");
-  const int ctl0[8] = {0, 0, 0, kStart, 0, max_steps, 0, 0};
-  check(cudaMemcpyAsync(ctl_, ctl0, sizeof(ctl0), cudaMemcpyHostToDevice, stream_), "gpt control upload");
   if (P > 0)
     check(cudaMemcpyAsync(prefix_, prefix, static_cast<size_t>(P) * kW * 4, cudaMemcpyHostToDevice, stream_),
           "gpt prefix upload");
+  const int n = persistent_ ? generate_persistent(P, max_steps) : generate_graphs(P, max_steps);
+  unsigned int st = 0;
+  check(cudaMemcpy(&st, status_, sizeof(st), cudaMemcpyDeviceToHost), "gpt status read");
+  if (st != 0) {
+    check(cudaMemset(status_, 0, sizeof(st)), "gpt status clear");
+    throw std::runtime_error("timeout: a GPT kernel abandoned a bounded wait (device status " + std::to_string(st) + ")");
+  }
+  if (n < 1 || n > max_steps) throw std::runtime_error("cuda: gpt: decoder produced an invalid step count");
+  check(cudaMemcpyAsync(codes, codes_, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, stream_), "codes read");
+  if (last_logits)
+    check(cudaMemcpyAsync(last_logits, logits_, kVocab * 4, cudaMemcpyDeviceToHost, stream_), "logits read");
+  check(cudaStreamSynchronize(stream_), "gpt sync");
+  steps_ = n;
+  return n;
+}
+
+// One cooperative launch for the whole call; the prefill / decode split of
+// the device time comes from the kernel's global-timer stamps.
+int GptDecoder::generate_persistent(int P, int max_steps) {
+  GptPersistParams p;
+  p.layers = layers_dev_;
+  p.lnf_g = lnf_g_;
+  p.lnf_b = lnf_b_;
+  p.fn_g = fn_g_;
+  p.fn_b = fn_b_;
+  p.b_head = b_head_;
+  p.w_head = w_head_;
+  p.emb = emb_;
+  p.pos = pos_;
+  p.prefix = prefix_;
+  p.x = x_;
+  p.h = h_;
+  p.qkv = qkv_;
+  p.m = m_;
+  p.logits = logits_;
+  p.kc = kc_;
+  p.vc = vc_;
+  p.part = part_;
+  p.cand_val = cand_val_;
+  p.cand_idx = cand_idx_;
+  p.codes = codes_;
+  p.out = out_;
+  p.barrier = barrier_;
+  p.status = status_;
+  p.times = times_;
+  p.P = P;
+  p.max_steps = max_steps;
+  check(cudaMemsetAsync(barrier_, 0, sizeof(unsigned int), stream_), "grid barrier reset");
+  check(cudaMemsetAsync(out_, 0, 16, stream_), "gpt output reset");
+  check(cudaEventRecord(ev_[0], stream_), "event");
+  check(gpt_persist_launch(p, sms_, stream_), "persistent decoder launch");
+  check(cudaEventRecord(ev_[2], stream_), "event");
+  int n = 0;
+  unsigned long long t[3] = {0, 0, 0};
+  check(cudaMemcpyAsync(&n, out_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "gpt step count read");
+  check(cudaMemcpyAsync(t, times_, sizeof(t), cudaMemcpyDeviceToHost, stream_), "gpt timer read");
+  check(cudaStreamSynchronize(stream_), "gpt sync");
+  float total = 0.0f;
+  check(cudaEventElapsedTime(&total, ev_[0], ev_[2]), "event time");
+  const double pre = t[1] >= t[0] ? (t[1] - t[0]) * 1e-6 : 0.0;
+  prefill_ms_ = static_cast<float>(pre);
+  decode_ms_ = total - prefill_ms_;
+  launches_ = 1;
+  return n;
+}
+
+// The per-kernel path: a graph per prefill row, a graph per decode step,
+// the stop flag read once per chunk of steps.
+int GptDecoder::generate_graphs(int P, int max_steps) {
+  static_assert(kStart == 8192, "start code");
+  const int ctl0[8] = {0, 0, 0, kStart, 0, max_steps, 0, 0};
+  check(cudaMemcpyAsync(ctl_, ctl0, sizeof(ctl0), cudaMemcpyHostToDevice, stream_), "gpt control upload");
   check(cudaEventRecord(ev_[0], stream_), "event");
   for (int r = 0; r < P; ++r) check(cudaGraphLaunch(g_prefill_, stream_), "prefill graph launch");
   check(cudaEventRecord(ev_[1], stream_), "event");
@@ -695,22 +781,10 @@ int GptDecoder::generate(const float* prefix, int P, int max_steps, uint32_t* co
   int ctl[8];
   check(cudaMemcpyAsync(ctl, ctl_, sizeof(ctl), cudaMemcpyDeviceToHost, stream_), "gpt control read");
   check(cudaStreamSynchronize(stream_), "gpt sync");
-  unsigned int st = 0;
-  check(cudaMemcpy(&st, status_, sizeof(st), cudaMemcpyDeviceToHost), "gpt status read");
-  if (st != 0) {
-    check(cudaMemset(status_, 0, sizeof(st)), "gpt status clear");
-    throw std::runtime_error("timeout: a GPT kernel abandoned a bounded wait (device status " + std::to_string(st) + ")");
-  }
-  const int n = ctl[2];
-  if (n < 1 || n > max_steps) throw std::runtime_error("cuda: gpt: decoder produced an invalid step count");
-  check(cudaMemcpyAsync(codes, codes_, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, stream_), "codes read");
-  if (last_logits)
-    check(cudaMemcpyAsync(last_logits, logits_, kVocab * 4, cudaMemcpyDeviceToHost, stream_), "logits read");
-  check(cudaStreamSynchronize(stream_), "gpt sync");
   check(cudaEventElapsedTime(&prefill_ms_, ev_[0], ev_[1]), "event time");
   check(cudaEventElapsedTime(&decode_ms_, ev_[1], ev_[2]), "event time");
-  steps_ = n;
-  return n;
+  launches_ = static_cast<long long>(P) * prefill_kernels_ + static_cast<long long>(launched) * decode_kernels_;
+  return ctl[2];
 }
 
 }  // namespace itts

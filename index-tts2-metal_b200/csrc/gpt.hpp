@@ -9,16 +9,16 @@
 // code's mel embedding plus the step's position embedding; start code 8192,
 // stop code 8193.
 //
-// One token at a time is bandwidth-bound (about 1 GB of f16 weights per
-// token), so every projection is a weight-streaming GEMV: one CTA per SM
-// bulk-copies its rows of the f16 weight matrix into shared memory before it
-// waits on the previous kernel (programmatic dependent launch), so the weight
-// streams of consecutive projections overlap the dependent chain; fp32
-// activations and accumulation, LayerNorm (and the attention's split-softmax
-// combine) in the prologue. The attention splits each head's keys over 7
-// CTAs. The KV cache is fp32. A CUDA graph per token (prefill row or decode
-// step) reads the row, the cache length, the step and the current code from
-// device memory, so the host only synchronises once per chunk of steps.
+// One token at a time is bandwidth- and latency-bound (about 1 GB of f16
+// weights per token, in a chain of 121 dependent all-to-all steps). The
+// product path is one persistent cooperative kernel per generate call
+// (gpt_persist.cu): the steps are stages separated by grid barriers, and a
+// producer warp per SM streams the weights through a shared-memory ring
+// ahead of them. The per-kernel path (ITTS_GPT_MODE=graph in the
+// environment, a diagnostic) runs the same math as weight-streaming GEMV
+// kernels with programmatic dependent launch, one CUDA graph per token. Both
+// use fp32 activations, accumulation and KV cache, and split each head's
+// keys over 7 ranges with the softmax merged in the next projection.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -26,6 +26,8 @@
 
 #include <cstdint>
 #include <string>
+
+#include "gpt_persist.cuh"
 
 namespace itts {
 
@@ -45,6 +47,9 @@ class GptDecoder {
   float last_decode_ms() const { return decode_ms_; }
   int last_steps() const { return steps_; }
   int kernels_per_token() const { return decode_kernels_; }
+  // Kernel launches of the last generate call (1 for the persistent kernel).
+  long long last_launches() const { return launches_; }
+  bool persistent() const { return persistent_; }
   cudaStream_t stream() const { return stream_; }
   int device() const { return device_; }
   // f16 weight bytes one decode step streams (all projections and the head).
@@ -55,13 +60,12 @@ class GptDecoder {
   static constexpr int kMaxLen = 4096;  // prefix rows + decode steps held in the KV cache
 
  private:
-  struct Layer {
-    const float *ln1_g, *ln1_b, *b_attn, *b_proj, *ln2_g, *ln2_b, *b_fc, *b_mproj;
-    const __half *w_attn, *w_proj, *w_fc, *w_mproj;  // [out][in]
-  };
+  using Layer = GptLayerPtrs;
   void check(cudaError_t e, const char* what);
   void enqueue_layers();
   void build_graphs();
+  int generate_persistent(int P, int max_steps);
+  int generate_graphs(int P, int max_steps);
 
   int device_ = 0;
   cudaStream_t stream_ = nullptr;
@@ -82,8 +86,17 @@ class GptDecoder {
   uint32_t* codes_ = nullptr;  // [kPositions]
   unsigned int* status_ = nullptr;  // nonzero: a kernel abandoned a bounded wait
   int sms_ = 148;
+  // persistent-kernel state
+  bool persistent_ = true;
+  GptLayerPtrs* layers_dev_ = nullptr;
+  float* cand_val_ = nullptr;
+  int* cand_idx_ = nullptr;
+  unsigned int* barrier_ = nullptr;
+  int* out_ = nullptr;
+  unsigned long long* times_ = nullptr;
+  long long launches_ = 0;
   cudaGraphExec_t g_prefill_ = nullptr, g_decode_ = nullptr;
-  int decode_kernels_ = 0;
+  int decode_kernels_ = 0, prefill_kernels_ = 0;
   float prefill_ms_ = 0.0f, decode_ms_ = 0.0f;
   int steps_ = 0;
 };

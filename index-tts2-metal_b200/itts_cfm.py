@@ -50,7 +50,8 @@ GPT_MAX_LEN = 4096
 ITTS_COMPONENT_CFM = 0x1
 ITTS_COMPONENT_LENGTH_REGULATOR = 0x2
 ITTS_COMPONENT_BIGVGAN = 0x4
-ITTS_COMPONENT_ALL = 0x7
+ITTS_COMPONENT_GPT = 0x8
+ITTS_COMPONENT_ALL = 0xF
 VOCODER_HOP = 256
 VOCODER_MAX_T = 16384
 

@@ -95,6 +95,17 @@ def test_model_gate_per_component(unit_bundle, tmp_path):
     assert rc == itts_cfm.ITTS_EBUNDLE and "component mask" in rep["error"]
 
 
+def test_model_gate_gpt(gpt_bundle, unit_bundle):
+    """The GPT decoder's sentinels (Conv1D weights [in, out]) on the
+    synthetic GPT bundle, every payload's SHA-256 verified; missing from the
+    estimator bundle."""
+    rc, rep = itts_cfm.inspect_model_bundle(gpt_bundle, itts_cfm.ITTS_COMPONENT_GPT)
+    assert rc == itts_cfm.ITTS_OK and rep["ok"] and rep["components"] == ["gpt"], rep
+    assert rep["integrity"]["sha256_verified_count"] == rep["tensor_count"] == len(mit2.gpt_tensor_specs())
+    rc, rep = itts_cfm.inspect_model_bundle(unit_bundle, itts_cfm.ITTS_COMPONENT_GPT)
+    assert rc == itts_cfm.ITTS_EBUNDLE and "missing tensor: gpt." in rep["error"]
+
+
 def test_model_gate_bigvgan(vocoder_bundle):
     rc, rep = itts_cfm.inspect_model_bundle(vocoder_bundle, itts_cfm.ITTS_COMPONENT_BIGVGAN)
     assert rc == itts_cfm.ITTS_OK, rep
