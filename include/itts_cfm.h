@@ -381,6 +381,13 @@ const char* itts_gpt_create_error(void);
  * P + steps <= ITTS_GPT_MAX_LEN. */
 int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t* codes,
                       uint32_t* n_codes, float* last_logits);
+/* itts_gpt_generate with flags. ITTS_GPT_HF_POSITIONS = the reference's
+ * hf_generate_positions = true (decode step s > 0 takes position embedding
+ * s + 1; steps <= 1817), which is how its synthesis pipeline calls the decoder
+ * (runtime/impl/tts_synthesis/synthesis_pipeline.cpp:675, 795). */
+#define ITTS_GPT_HF_POSITIONS 0x1u
+int itts_gpt_generate_ex(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t flags,
+                         uint32_t* codes, uint32_t* n_codes, float* last_logits);
 /* Device time (ms) of the last generate's prefill and decode (no reference
  * counterpart); kernel launches of the last generate (1: the whole call is one
  * persistent kernel); f16 weight bytes one decode step streams. */

@@ -56,13 +56,20 @@ const char* itts_gpt_create_error(void) { return g_gpt_create_err.c_str(); }
 
 int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t* codes,
                       uint32_t* n_codes, float* last_logits) {
+  return itts_gpt_generate_ex(ctx, prefix, P, steps, 0u, codes, n_codes, last_logits);
+}
+
+int itts_gpt_generate_ex(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t flags,
+                         uint32_t* codes, uint32_t* n_codes, float* last_logits) {
   if (!ctx) return ITTS_EINVAL_SHAPE;
   try {
     ctx->err.clear();
     if (P > ITTS_GPT_MAX_LEN || steps > ITTS_GPT_MAX_STEPS)
       throw std::invalid_argument("gpt: need 1 <= steps <= 1818 and P + steps <= 4096");
+    if (flags & ~ITTS_GPT_HF_POSITIONS) throw std::invalid_argument("gpt: unknown flag bits");
     cudaSetDevice(ctx->dec->device());
-    const int n = ctx->dec->generate(prefix, static_cast<int>(P), static_cast<int>(steps), codes, last_logits);
+    const int n = ctx->dec->generate(prefix, static_cast<int>(P), static_cast<int>(steps),
+                                     (flags & ITTS_GPT_HF_POSITIONS) != 0, codes, last_logits);
     if (n_codes) *n_codes = static_cast<uint32_t>(n);
     return ITTS_OK;
   } catch (const std::exception& e) {

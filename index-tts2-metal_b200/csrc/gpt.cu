@@ -351,7 +351,8 @@ __global__ void __launch_bounds__(256) gpt_embed_kernel(const float* __restrict_
   griddep_wait();
   if (ctl[4]) return;
   const int i = blockIdx.x * 256 + threadIdx.x;
-  if (i < kW) x[i] = emb[static_cast<size_t>(ctl[3]) * kW + i] + pos[static_cast<size_t>(ctl[2]) * kW + i];
+  const int step = ctl[2], position = ctl[6] && step > 0 ? step + 1 : step;  // ctl[6]: generate-style positions
+  if (i < kW) x[i] = emb[static_cast<size_t>(ctl[3]) * kW + i] + pos[static_cast<size_t>(position) * kW + i];
 }
 
 // Prefill input: prefix row ctl[1].
@@ -685,9 +686,13 @@ void GptDecoder::build_graphs() {
       &g_decode_, &decode_kernels_);
 }
 
-int GptDecoder::generate(const float* prefix, int P, int max_steps, uint32_t* codes, float* last_logits) {
-  if (P < 0 || max_steps < 1 || max_steps > kPositions || P + max_steps > kMaxLen)
-    throw std::invalid_argument("gpt: need 0 <= P, 1 <= max_steps <= 1818 and P + max_steps <= 4096");
+int GptDecoder::generate(const float* prefix, int P, int max_steps, bool hf_positions, uint32_t* codes,
+                         float* last_logits) {
+  const int max_allowed = hf_positions ? kPositions - 1 : kPositions;
+  if (P < 0 || max_steps < 1 || max_steps > max_allowed || P + max_steps > kMaxLen)
+    throw std::invalid_argument("gpt: need 0 <= P, 1 <= max_steps <= 1818 (1817 with generate-style positions) and "
+                                "P + max_steps <= 4096");
+  hf_ = hf_positions;
   if (P > 0 && !prefix) throw std::invalid_argument("gpt: prefix must be non-null when P > 0");
   if (!codes) throw std::invalid_argument("gpt: codes must be non-null");
   check(cudaSetDevice(device_), "cudaSetDevice");
@@ -741,6 +746,7 @@ int GptDecoder::generate_persistent(int P, int max_steps) {
   p.times = times_;
   p.P = P;
   p.max_steps = max_steps;
+  p.hf_positions = hf_ ? 1 : 0;
   check(cudaMemsetAsync(barrier_, 0, sizeof(unsigned int), stream_), "grid barrier reset");
   check(cudaMemsetAsync(out_, 0, 16, stream_), "gpt output reset");
   check(cudaEventRecord(ev_[0], stream_), "event");
@@ -764,7 +770,7 @@ int GptDecoder::generate_persistent(int P, int max_steps) {
 // the stop flag read once per chunk of steps.
 int GptDecoder::generate_graphs(int P, int max_steps) {
   static_assert(kStart == 8192, "start code");
-  const int ctl0[8] = {0, 0, 0, kStart, 0, max_steps, 0, 0};
+  const int ctl0[8] = {0, 0, 0, kStart, 0, max_steps, hf_ ? 1 : 0, 0};
   check(cudaMemcpyAsync(ctl_, ctl0, sizeof(ctl0), cudaMemcpyHostToDevice, stream_), "gpt control upload");
   check(cudaEventRecord(ev_[0], stream_), "event");
   for (int r = 0; r < P; ++r) check(cudaGraphLaunch(g_prefill_, stream_), "prefill graph launch");

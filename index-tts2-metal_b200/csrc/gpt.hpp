@@ -41,7 +41,9 @@ class GptDecoder {
   // prefix [P,1280] (host) -> up to max_steps codes (host); stops after the
   // stop code (included, as the reference's predicted tokens). Returns the
   // number of codes; last_logits (optional, host [8194]) of the last step.
-  int generate(const float* prefix, int P, int max_steps, uint32_t* codes, float* last_logits);
+  // hf_positions: the reference's hf_generate_positions (decode step s > 0
+  // at position s + 1), as its synthesis pipeline calls the decoder.
+  int generate(const float* prefix, int P, int max_steps, bool hf_positions, uint32_t* codes, float* last_logits);
   // Device time of the last generate call's prefill and decode parts (ms).
   float last_prefill_ms() const { return prefill_ms_; }
   float last_decode_ms() const { return decode_ms_; }
@@ -81,7 +83,8 @@ class GptDecoder {
   float* part_ = nullptr;  // attention partials [20 heads][key ranges][max, sum, 64 accumulators]
   float *kc_ = nullptr, *vc_ = nullptr;  // [24][kMaxLen][1280]
   float* prefix_ = nullptr;              // [kMaxLen][1280]
-  // [0] cache length, [1] prefill row, [2] step, [3] current code, [4] stopped, [5] max steps
+  // [0] cache length, [1] prefill row, [2] step, [3] current code, [4] stopped, [5] max steps,
+  // [6] generate-style positions
   int* ctl_ = nullptr;
   uint32_t* codes_ = nullptr;  // [kPositions]
   unsigned int* status_ = nullptr;  // nonzero: a kernel abandoned a bounded wait
@@ -95,6 +98,7 @@ class GptDecoder {
   int* out_ = nullptr;
   unsigned long long* times_ = nullptr;
   long long launches_ = 0;
+  bool hf_ = false;
   cudaGraphExec_t g_prefill_ = nullptr, g_decode_ = nullptr;
   int decode_kernels_ = 0, prefill_kernels_ = 0;
   float prefill_ms_ = 0.0f, decode_ms_ = 0.0f;

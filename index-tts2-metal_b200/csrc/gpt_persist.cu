@@ -517,7 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1) gpt_persist_kernel(GptPersistPara
       // runtime/impl/gpt.cpp:1545-1554) and publishes the CTA's slice of it.
       if (l == 0) {
         const float* e0 = decode ? p.emb + static_cast<size_t>(code) * kW : p.prefix + static_cast<size_t>(tok) * kW;
-        const float* e1 = p.pos + static_cast<size_t>(step) * kW;
+        // gpt_cached_generate_position (runtime/impl/gpt.cpp:1873-1875)
+        const int position = p.hf_positions && step > 0 ? step + 1 : step;
+        const float* e1 = p.pos + static_cast<size_t>(position) * kW;
         const int x0 = static_cast<int>(static_cast<long long>(b) * kW / G);
         const int x1 = static_cast<int>(static_cast<long long>(b + 1) * kW / G);
         for (int i = tid; i < kW; i += kCons) {

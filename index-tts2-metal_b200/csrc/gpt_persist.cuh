@@ -30,6 +30,7 @@ struct GptPersistParams {
   unsigned int* status;       // nonzero: a bounded wait gave up
   unsigned long long* times;  // globaltimer at start, end of prefill, end
   int P, max_steps;
+  int hf_positions;  // nonzero: decode step s > 0 takes position embedding s + 1
 };
 
 // Dynamic shared memory of one CTA; the one-time function attribute; the

@@ -39,6 +39,7 @@ EXPORTED = [
     "itts_pipeline_create", "itts_pipeline_destroy", "itts_pipeline_last_error", "itts_pipeline_create_error",
     "itts_pipeline_synthesize",
     "itts_gpt_create", "itts_gpt_destroy", "itts_gpt_last_error", "itts_gpt_create_error", "itts_gpt_generate",
+    "itts_gpt_generate_ex",
     "itts_gpt_timing", "itts_gpt_launch_kernels", "itts_gpt_weight_bytes_per_token",
 ]
 GPT_WIDTH = 1280
@@ -47,6 +48,7 @@ GPT_START = 8192
 GPT_STOP = 8193
 GPT_MAX_STEPS = 1818
 GPT_MAX_LEN = 4096
+GPT_HF_POSITIONS = 0x1
 ITTS_COMPONENT_CFM = 0x1
 ITTS_COMPONENT_LENGTH_REGULATOR = 0x2
 ITTS_COMPONENT_BIGVGAN = 0x4
@@ -147,6 +149,7 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_gpt_last_error": (C.c_char_p, [vp]),
         "itts_gpt_create_error": (C.c_char_p, []),
         "itts_gpt_generate": (i32, [vp, vp, u32, u32, vp, C.POINTER(u32), vp]),
+        "itts_gpt_generate_ex": (i32, [vp, vp, u32, u32, u32, vp, C.POINTER(u32), vp]),
         "itts_gpt_timing": (i32, [vp, C.POINTER(f32), C.POINTER(f32)]),
         "itts_gpt_launch_kernels": (i32, [vp]),
         "itts_gpt_weight_bytes_per_token": (f64, []),
@@ -589,7 +592,9 @@ class GptDecoder:
         except Exception:
             pass
 
-    def generate(self, prefix, steps: int) -> tuple[list[int], np.ndarray]:
+    def generate(self, prefix, steps: int, hf_positions: bool = False) -> tuple[list[int], np.ndarray]:
+        """hf_positions: the reference's hf_generate_positions (as its
+        synthesis pipeline calls the decoder)."""
         prefix = None if prefix is None or len(prefix) == 0 else _f32(prefix)
         if prefix is not None and (prefix.ndim != 2 or prefix.shape[1] != GPT_WIDTH):
             raise ValueError("prefix must be [P, 1280]")
@@ -597,7 +602,8 @@ class GptDecoder:
         codes = np.zeros(max(int(steps), 1), np.uint32)
         logits = np.empty(GPT_VOCAB, np.float32)
         n = C.c_uint32(0)
-        rc = self.lib.itts_gpt_generate(self.h, _ptr(prefix), P, int(steps), _ptr(codes), C.byref(n), _ptr(logits))
+        rc = self.lib.itts_gpt_generate_ex(self.h, _ptr(prefix), P, int(steps), GPT_HF_POSITIONS if hf_positions else 0,
+                                           _ptr(codes), C.byref(n), _ptr(logits))
         if rc != ITTS_OK:
             raise IttsError(rc, self.lib.itts_gpt_last_error(self.h).decode())
         return [int(c) for c in codes[:n.value]], logits

@@ -15,7 +15,8 @@ Reference functions restated (paths inside raoqu/index-tts2-metal):
   argmax_row                         runtime/impl/gpt.cpp:1297-1308
   build_gpt_greedy_current_cpu       runtime/impl/gpt.cpp:1545-1554
   run_gpt_kv_prefill_cpu             runtime/impl/gpt.cpp:1796-1806
-  run_gpt_kv_greedy_cpu              runtime/impl/gpt.cpp:1877-1909 (hf_generate_positions = false)
+  gpt_cached_generate_position       runtime/impl/gpt.cpp:1873-1875
+  run_gpt_kv_greedy_cpu              runtime/impl/gpt.cpp:1877-1909
 """
 from __future__ import annotations
 
@@ -72,10 +73,12 @@ class GptOracle:
         m = _gelu_new(_ln(h, *L["ln2"]) @ L["fc"][0] + L["fc"][1])
         return (h + (m @ L["mproj"][0] + L["mproj"][1])).astype(np.float32)
 
-    def greedy(self, prefix, steps: int):
+    def greedy(self, prefix, steps: int, hf_positions: bool = False):
         """(predicted codes, logits of each step) as run_gpt_kv_greedy_cpu;
         the prefix is processed token by token (the causal full-sequence
-        prefill of the reference computes the same values)."""
+        prefill of the reference computes the same values). hf_positions:
+        its hf_generate_positions (step s > 0 uses position s + 1, as the
+        synthesis pipeline calls it)."""
         prefix = np.asarray(prefix, np.float32)
         caches = [([], []) for _ in range(LAYERS)]
         for x in prefix:
@@ -84,7 +87,7 @@ class GptOracle:
         emb, pos = self.t["gpt.mel_embedding.weight"], self.t["gpt.mel_pos_embedding.emb.weight"]
         tok, out, logits = START, [], []
         for step in range(steps):
-            x = emb[tok] + pos[step]
+            x = emb[tok] + pos[step + 1 if hf_positions and step > 0 else step]
             for L, (ck, cv) in zip(self.layers, caches):
                 x = self._block_current(L, x, ck, cv)
             h = _ln(_ln(x, self.t["gpt.gpt.ln_f.weight"], self.t["gpt.gpt.ln_f.bias"]),

@@ -225,7 +225,7 @@ class RefOracle:
         L.ref_noise.argtypes = [C.c_uint32, C.c_uint32, C.c_uint64, C.c_float, C.c_void_p]
         L.ref_bigvgan_vocoder.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_void_p]
         L.ref_length_regulator.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
-        L.ref_gpt_kv_greedy.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p,
+        L.ref_gpt_kv_greedy.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_int, C.c_void_p,
                                         C.POINTER(C.c_uint32), C.c_void_p, C.POINTER(C.c_int)]
         L.ref_bigvgan_activation.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
 
@@ -283,14 +283,16 @@ class RefOracle:
         self._ok(self.lib.ref_noise(T, C_, seed, temperature, _p(out)))
         return out
 
-    def gpt_greedy(self, prefix, steps: int):
-        """run_gpt_kv_greedy_cpu: (codes, logits of the last step, first stop step)."""
+    def gpt_greedy(self, prefix, steps: int, hf_positions: bool = False):
+        """run_gpt_kv_greedy_cpu: (codes, logits of the last step, first stop step);
+        hf_positions = its hf_generate_positions argument."""
         prefix = _f32(prefix)
         toks = np.zeros(steps, np.uint32)
         n = C.c_uint32(0)
         stop = C.c_int(-1)
         logits = np.zeros(8194, np.float32)
-        self._ok(self.lib.ref_gpt_kv_greedy(self.dir, _p(prefix), prefix.shape[0], int(steps), _p(toks), C.byref(n),
+        self._ok(self.lib.ref_gpt_kv_greedy(self.dir, _p(prefix), prefix.shape[0], int(steps), int(bool(hf_positions)),
+                                            _p(toks), C.byref(n),
                                             _p(logits), C.byref(stop)))
         return toks[: n.value].tolist(), logits, stop.value
 

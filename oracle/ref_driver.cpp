@@ -35,8 +35,8 @@ std::vector<float> run_bigvgan_vocoder_cpu(const mit2::Bundle& bundle, std::vect
 std::vector<float> run_length_regulator_full_cpu(const mit2::Bundle& bundle, const std::vector<float>& input,
                                                  uint32_t in_tokens, uint32_t out_tokens);
 void ref_glue_gpt_kv_greedy(const mit2::Bundle& bundle, const std::vector<float>& prefix, uint32_t prefix_tokens,
-                            uint32_t steps, std::vector<uint32_t>* tokens, std::vector<float>* last_logits,
-                            int* first_stop);
+                            uint32_t steps, bool hf_generate_positions, std::vector<uint32_t>* tokens,
+                            std::vector<float>* last_logits, int* first_stop);
 std::vector<float> run_bigvgan_activation_cpu(const mit2::Bundle& bundle, const std::string& prefix,
                                               const std::vector<float>& x, uint32_t tokens, uint32_t channels);
 
@@ -153,14 +153,15 @@ int ref_noise(uint32_t T, uint32_t C, uint64_t seed, float temperature, float* o
 }
 
 // run_gpt_kv_greedy_cpu: prefix [P,1280] -> up to `steps` greedy mel codes
-// (stops after the stop code 8193), the logits of the last step [8194].
-int ref_gpt_kv_greedy(const char* bundle_dir, const float* prefix, uint32_t P, uint32_t steps, uint32_t* tokens,
-                      uint32_t* n_tokens, float* last_logits, int* first_stop) {
+// (stops after the stop code 8193), the logits of the last step [8194];
+// hf != 0 selects the generate-style positions (step s > 0 at position s + 1).
+int ref_gpt_kv_greedy(const char* bundle_dir, const float* prefix, uint32_t P, uint32_t steps, int hf,
+                      uint32_t* tokens, uint32_t* n_tokens, float* last_logits, int* first_stop) {
   return guard([&] {
     mit2::Bundle b(bundle_dir);
     std::vector<uint32_t> t;
     std::vector<float> l;
-    ref_glue_gpt_kv_greedy(b, vec(prefix, static_cast<size_t>(P) * 1280), P, steps, &t, &l, first_stop);
+    ref_glue_gpt_kv_greedy(b, vec(prefix, static_cast<size_t>(P) * 1280), P, steps, hf != 0, &t, &l, first_stop);
     std::memcpy(tokens, t.data(), t.size() * sizeof(uint32_t));
     *n_tokens = static_cast<uint32_t>(t.size());
     std::memcpy(last_logits, l.data(), l.size() * sizeof(float));

@@ -29,8 +29,10 @@ Cases (inputs follow the reference's self-tests where it has them):
 
   kat_gpt_decode    run_gpt_kv_greedy_cpu (cached greedy mel-code decode, 24 layers)
                     on a seeded 4-row prefix for 3 steps, synthetic GPT bundle seed 0
+  kat_gpt_decode_hf the same with hf_generate_positions = true (the synthesis
+                    pipeline's call) on a seeded 5-row prefix for 3 steps
 
-    python tests/golden/make_golden.py [--only bigvgan|lr|gpt]
+    python tests/golden/make_golden.py [--only bigvgan|lr|gpt|gpt_hf]
 """
 from __future__ import annotations
 
@@ -114,10 +116,23 @@ def gpt_cases():
                         last_logits=logits, first_stop=np.int32(stop), bundle_seed=0, weights_sha256=weights_sha(gb))
 
 
+def gpt_hf_cases():
+    """The synthesis pipeline's call (hf_generate_positions = true,
+    runtime/impl/tts_synthesis/synthesis_pipeline.cpp:675, 795)."""
+    gb = mit2.make_gpt_bundle(ROOT / "gpt_seed0", seed=0)
+    r = oracle.RefOracle(gb)
+    prefix = f32(np.random.default_rng(8).standard_normal((5, 1280)))
+    toks, logits, stop = r.gpt_greedy(prefix, 3, hf_positions=True)
+    np.savez_compressed(HERE / "kat_gpt_decode_hf.npz", prefix=prefix, codes=np.array(toks, np.uint32),
+                        last_logits=logits, first_stop=np.int32(stop), bundle_seed=0, weights_sha256=weights_sha(gb))
+
+
 def main():
     only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
-    if only == "gpt":
-        gpt_cases()
+    if only in ("gpt", "gpt_hf"):
+        if only == "gpt":
+            gpt_cases()
+        gpt_hf_cases()
         print("golden vectors written to", HERE)
         return
     if only == "bigvgan":
@@ -131,6 +146,7 @@ def main():
     bigvgan_cases()
     length_regulator_cases()
     gpt_cases()
+    gpt_hf_cases()
     unit = mit2.make_dit_bundle(ROOT / "seed0_unit", seed=0, init="unit")
     base = mit2.make_dit_bundle(ROOT / "seed0_baseline", seed=0, init="baseline")
     ru, rb = oracle.RefOracle(unit), oracle.RefOracle(base)

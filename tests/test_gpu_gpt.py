@@ -45,6 +45,20 @@ def test_decode_matches_reference_golden(dec):
     _close(g["last_logits"], logits)
 
 
+def test_decode_hf_positions_matches_reference_golden(dec, gpt_oracle):
+    """The synthesis pipeline's call (hf_generate_positions = true): the
+    reference's own golden, then a longer decode against the oracle."""
+    g = dict(np.load(GOLD / "kat_gpt_decode_hf.npz"))
+    codes, logits = dec.generate(g["prefix"], 3, hf_positions=True)
+    assert codes == [int(c) for c in g["codes"]]
+    _close(g["last_logits"], logits)
+    prefix = np.random.default_rng(11).standard_normal((12, 1280)).astype(np.float32)
+    want, ref = gpt_oracle.greedy(prefix, 10, hf_positions=True)
+    codes, last = dec.generate(prefix, 10, hf_positions=True)
+    assert codes == want
+    _close(ref[-1], last)
+
+
 def test_decode_matches_oracle_longer(dec, gpt_oracle):
     """A 24-row prefix and 12 steps (crosses the 8-step stop-flag chunk)."""
     prefix = np.random.default_rng(5).standard_normal((24, 1280)).astype(np.float32) * np.float32(0.5)

@@ -163,3 +163,14 @@ def test_gpt_greedy_decode(gpt_oracle):
     codes, logits = gpt_oracle.greedy(g["prefix"], 3)
     assert codes == g["codes"].tolist()
     _close(g["last_logits"], logits[-1])
+
+
+def test_gpt_greedy_decode_hf_positions(gpt_oracle):
+    """hf_generate_positions = true, as the synthesis pipeline calls the
+    decoder: step s > 0 takes position embedding s + 1."""
+    g = _load("kat_gpt_decode_hf")
+    codes, logits = gpt_oracle.greedy(g["prefix"], 3, hf_positions=True)
+    assert codes == g["codes"].tolist()
+    _close(g["last_logits"], logits[-1])
+    plain = gpt_oracle.greedy(g["prefix"], 3)[1][-1]
+    assert not np.allclose(plain, logits[-1])  # the flag changes the decode
