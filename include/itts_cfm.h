@@ -394,6 +394,17 @@ int itts_gpt_generate_ex(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uin
 int itts_gpt_timing(const itts_gpt_ctx* ctx, float* prefill_ms, float* decode_ms);
 int itts_gpt_launch_kernels(const itts_gpt_ctx* ctx);
 double itts_gpt_weight_bytes_per_token(void);
+/* Profiling aid (no reference counterpart): with tracing on, the persistent
+ * decoder stamps its first decode token's stages; itts_gpt_stage_trace writes
+ * the microseconds since that token started at each point (the token start,
+ * then per stage: prologue done, weight slots done, compute done, grid
+ * barrier passed; 5 stages
+ * per layer, then the head; 485 values), then every CTA's barrier arrival
+ * ([121 stages][SM count]), then (at the "weight slots done" positions of
+ * the first block) how long CTA 0's first thread waited for its weight slots;
+ * -1 marks points not reached. Returns how many. */
+int itts_gpt_set_tracing(itts_gpt_ctx* ctx, int on);
+int itts_gpt_stage_trace(itts_gpt_ctx* ctx, double* us, uint32_t cap);
 
 #ifdef __cplusplus
 }

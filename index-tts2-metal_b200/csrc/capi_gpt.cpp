@@ -92,6 +92,22 @@ int itts_gpt_launch_kernels(const itts_gpt_ctx* ctx) {
   return ctx ? static_cast<int>(ctx->dec->last_launches()) : ITTS_EINVAL_SHAPE;
 }
 
+int itts_gpt_set_tracing(itts_gpt_ctx* ctx, int on) {
+  if (!ctx) return ITTS_EINVAL_SHAPE;
+  ctx->dec->set_tracing(on != 0);
+  return ITTS_OK;
+}
+
+int itts_gpt_stage_trace(itts_gpt_ctx* ctx, double* us, uint32_t cap) {
+  if (!ctx || !us) return ITTS_EINVAL_SHAPE;
+  try {
+    return ctx->dec->stage_trace(us, static_cast<int>(cap));
+  } catch (const std::exception& e) {
+    ctx->err = e.what();
+    return ITTS_ECUDA;
+  }
+}
+
 double itts_gpt_weight_bytes_per_token(void) { return itts::GptDecoder::weight_bytes_per_token(); }
 
 }  // extern "C"

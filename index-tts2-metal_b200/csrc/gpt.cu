@@ -565,8 +565,8 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
                o_codes = carve(static_cast<size_t>(kPositions) * 4);
   check(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device), "SM count");
   const size_t o_layers = carve(sizeof(GptLayerPtrs) * kLayers), o_cval = carve(static_cast<size_t>(sms_) * 4),
-               o_cidx = carve(static_cast<size_t>(sms_) * 4), o_bar = carve(4), o_out = carve(16),
-               o_times = carve(4 * 8);
+               o_cidx = carve(static_cast<size_t>(sms_) * 4), o_bar = carve(512), o_out = carve(16),
+               o_times = carve(4 * 8), o_trace = carve((2 * static_cast<size_t>(kGptTraceCap) + static_cast<size_t>(kGptTraceStages) * sms_) * 8);
   check(cudaMalloc(&state_, off), "gpt state cudaMalloc");
   check(cudaMemset(state_, 0, off), "gpt state memset");
   uint8_t* s = static_cast<uint8_t*>(state_);
@@ -588,11 +588,12 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
   barrier_ = reinterpret_cast<unsigned int*>(s + o_bar);
   out_ = reinterpret_cast<int*>(s + o_out);
   times_ = reinterpret_cast<unsigned long long*>(s + o_times);
+  trace_ = reinterpret_cast<unsigned long long*>(s + o_trace);
   check(cudaMemcpy(layers_dev_, L_, sizeof(GptLayerPtrs) * kLayers, cudaMemcpyHostToDevice), "gpt layer table upload");
   check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   for (auto& e : ev_) check(cudaEventCreate(&e), "cudaEventCreate");
   const char* mode = std::getenv("ITTS_GPT_MODE");
-  persistent_ = mode && std::string(mode) == "persistent";
+  persistent_ = !(mode && std::string(mode) == "graph");
   if (persistent_) {
     if (sms_ < gpt_persist_min_grid()) throw std::runtime_error("gpt: too few SMs for the persistent decoder");
     check(gpt_persist_prepare(), "persistent decoder shared memory");
@@ -747,7 +748,13 @@ int GptDecoder::generate_persistent(int P, int max_steps) {
   p.P = P;
   p.max_steps = max_steps;
   p.hf_positions = hf_ ? 1 : 0;
-  check(cudaMemsetAsync(barrier_, 0, sizeof(unsigned int), stream_), "grid barrier reset");
+  p.trace = tracing_ ? trace_ : nullptr;
+  if (tracing_)
+    check(cudaMemsetAsync(trace_, 0,
+                          (2 * static_cast<size_t>(kGptTraceCap) + static_cast<size_t>(kGptTraceStages) * sms_) * 8,
+                          stream_),
+          "trace reset");
+  check(cudaMemsetAsync(barrier_, 0, 512, stream_), "grid barrier reset");
   check(cudaMemsetAsync(out_, 0, 16, stream_), "gpt output reset");
   check(cudaEventRecord(ev_[0], stream_), "event");
   check(gpt_persist_launch(p, sms_, stream_), "persistent decoder launch");
@@ -791,6 +798,18 @@ int GptDecoder::generate_graphs(int P, int max_steps) {
   check(cudaEventElapsedTime(&decode_ms_, ev_[1], ev_[2]), "event time");
   launches_ = static_cast<long long>(P) * prefill_kernels_ + static_cast<long long>(launched) * decode_kernels_;
   return ctl[2];
+}
+
+int GptDecoder::stage_trace(double* us, int cap) {
+  if (!tracing_ || !persistent_) return 0;
+  const size_t stamps = static_cast<size_t>(kGptTraceCap) + static_cast<size_t>(kGptTraceStages) * sms_;
+  std::vector<unsigned long long> t(stamps + kGptTraceCap);
+  check(cudaMemcpy(t.data(), trace_, t.size() * 8, cudaMemcpyDeviceToHost), "trace read");
+  int n = 0;
+  for (size_t i = 0; i < stamps && n < cap; ++i, ++n)
+    us[n] = t[i] == 0 || t[0] == 0 ? -1.0 : (static_cast<double>(t[i]) - static_cast<double>(t[0])) * 1e-3;
+  for (size_t i = stamps; i < t.size() && n < cap; ++i, ++n) us[n] = static_cast<double>(t[i]) * 1e-3;  // durations
+  return n;
 }
 
 }  // namespace itts

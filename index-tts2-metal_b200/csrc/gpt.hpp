@@ -52,6 +52,11 @@ class GptDecoder {
   // Kernel launches of the last generate call (1 for the persistent kernel).
   long long last_launches() const { return launches_; }
   bool persistent() const { return persistent_; }
+  // Stage trace of the last persistent generate's first decode token: the
+  // microseconds since the token started at each trace point (see
+  // GptPersistParams::trace); empty unless the decoder traces.
+  int stage_trace(double* us, int cap);
+  void set_tracing(bool on) { tracing_ = on; }
   cudaStream_t stream() const { return stream_; }
   int device() const { return device_; }
   // f16 weight bytes one decode step streams (all projections and the head).
@@ -99,6 +104,8 @@ class GptDecoder {
   unsigned long long* times_ = nullptr;
   long long launches_ = 0;
   bool hf_ = false;
+  bool tracing_ = false;
+  unsigned long long* trace_ = nullptr;  // [kGptTraceCap]
   cudaGraphExec_t g_prefill_ = nullptr, g_decode_ = nullptr;
   int decode_kernels_ = 0, prefill_kernels_ = 0;
   float prefill_ms_ = 0.0f, decode_ms_ = 0.0f;

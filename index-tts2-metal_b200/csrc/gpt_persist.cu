@@ -59,11 +59,12 @@ constexpr size_t kOffRed = kOffBars + 2 * kSlots * 8;
 constexpr size_t kOffTsum = kOffRed + 16 * 4;
 constexpr size_t kOffTv = kOffTsum + kMaxTasks * 4;
 constexpr size_t kOffFlags = kOffTv + kMaxTasks * 4;
-constexpr size_t kSmem = kOffFlags + 16;
+constexpr size_t kOffLayers = kOffFlags + 16;  // the layer pointer table, copied once
+constexpr size_t kSmem = kOffLayers + sizeof(GptLayerPtrs) * kLayers;
 static_assert(kSmem <= 227 * 1024, "shared memory");
-// attention scratch inside xs: scores [0, 600), q [600, 664), 16 x 64 accumulators after
-constexpr int kScrQ = 600, kScrAcc = 664;
-static_assert(kSplitKeys <= kScrQ && kScrAcc + 16 * 64 <= kMlp, "attention scratch");
+// attention scratch inside xs
+constexpr int kScrAcc = 640;  // scores [0, kSplitKeys), 16 x 64 accumulators from here
+static_assert(kSplitKeys <= kScrAcc && kScrAcc + 16 * 64 <= kMlp, "attention scratch");
 
 enum Stage { kSQkv = 0, kSAttn = 1, kSProj = 2, kSFc = 3, kSMproj = 4, kSHead = 5 };
 
@@ -73,9 +74,18 @@ struct ProjDesc {
   int n, k;
 };
 
-__device__ __forceinline__ ProjDesc proj_of(const GptPersistParams& p, int stage, int layer) {
+// Rows and columns of each stage's projection (compile-time, so that loop
+// bounds never wait on a load).
+__host__ __device__ constexpr int stage_n(int stage) {
+  return stage == kSQkv ? kQkv : stage == kSFc ? kMlp : stage == kSHead ? kVocab : kW;
+}
+__host__ __device__ constexpr int stage_k(int stage) { return stage == kSMproj ? kMlp : kW; }
+
+// Weight and bias of a stage; `layers` = the pointer table in shared memory.
+__device__ __forceinline__ ProjDesc proj_of(const GptPersistParams& p, const GptLayerPtrs* layers, int stage,
+                                            int layer) {
   if (stage == kSHead) return {p.w_head, p.b_head, kVocab, kW};
-  const GptLayerPtrs& L = p.layers[layer];
+  const GptLayerPtrs& L = layers[layer];
   switch (stage) {
     case kSQkv: return {L.w_attn, L.b_attn, kQkv, kW};
     case kSProj: return {L.w_proj, L.b_proj, kW, kW};
@@ -131,20 +141,57 @@ __device__ __forceinline__ float cmax(float v, float* red) {
   return t;
 }
 
-// cpu_layernorm (runtime/impl/tokenizer_tests.cpp:2992-3010) on xs[0, kW).
-__device__ __forceinline__ void cons_layer_norm(float* xs, const float* __restrict__ g, const float* __restrict__ b,
-                                                float* red) {
-  float s = 0.0f;
-  for (int i = threadIdx.x; i < kW; i += kCons) s += xs[i];
-  const float mean = csum(s, red) / static_cast<float>(kW);
-  float v = 0.0f;
-  for (int i = threadIdx.x; i < kW; i += kCons) {
-    const float d = xs[i] - mean;
-    v += d * d;
+// A 1280-wide row held 3 values per consumer thread (elements tid, tid + 512,
+// tid + 1024), so that its loads, the LayerNorm parameters' loads and the
+// reductions need one memory round trip.
+constexpr int kPer = (kW + kCons - 1) / kCons;
+
+__device__ __forceinline__ void load_params(const float* __restrict__ g, const float* __restrict__ b, float* gg,
+                                            float* bb) {
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = threadIdx.x + k * kCons;
+    gg[k] = i < kW ? g[i] : 0.0f;
+    bb[k] = i < kW ? b[i] : 0.0f;
   }
-  const float var = csum(v, red) / static_cast<float>(kW);
+}
+
+__device__ __forceinline__ void load_row_cg(const float* src, float* v) {
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = threadIdx.x + k * kCons;
+    v[k] = i < kW ? __ldcg(src + i) : 0.0f;
+  }
+}
+
+// cpu_layernorm (runtime/impl/tokenizer_tests.cpp:2992-3010) on the row in
+// registers: mean, biased variance, (x - mean) * (1 / sqrt(var + 1e-5)) *
+// gamma + beta.
+__device__ __forceinline__ void layer_norm_regs(float* v, const float* gg, const float* bb, float* red) {
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k)
+    if (threadIdx.x + k * kCons < kW) s += v[k];
+  const float mean = csum(s, red) / static_cast<float>(kW);
+  float q = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k)
+    if (threadIdx.x + k * kCons < kW) {
+      const float d = v[k] - mean;
+      q += d * d;
+    }
+  const float var = csum(q, red) / static_cast<float>(kW);
   const float inv = 1.0f / sqrtf(var + 1e-5f);
-  for (int i = threadIdx.x; i < kW; i += kCons) xs[i] = (xs[i] - mean) * inv * g[i] + b[i];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) v[k] = (v[k] - mean) * inv * gg[k] + bb[k];
+}
+
+__device__ __forceinline__ void store_row(const float* v, float* xs) {
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = threadIdx.x + k * kCons;
+    if (i < kW) xs[i] = v[k];
+  }
   cbar();
 }
 
@@ -156,21 +203,20 @@ __device__ __forceinline__ float gelu_new(float x) {
   return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
 }
 
-__device__ __forceinline__ float dot8(const uint4 w, const float* xs) {
-  const float4 xa = *reinterpret_cast<const float4*>(xs);
-  const float4 xb = *reinterpret_cast<const float4*>(xs + 4);
+// dot8 with the eight input values in registers (same order of operations).
+__device__ __forceinline__ float dot8r(const uint4 w, const float* x) {
   const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
   const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
   const float2 w2 = __half22float2(*reinterpret_cast<const __half2*>(&w.z));
   const float2 w3 = __half22float2(*reinterpret_cast<const __half2*>(&w.w));
-  float s = w0.x * xa.x;
-  s = fmaf(w0.y, xa.y, s);
-  s = fmaf(w1.x, xa.z, s);
-  s = fmaf(w1.y, xa.w, s);
-  s = fmaf(w2.x, xb.x, s);
-  s = fmaf(w2.y, xb.y, s);
-  s = fmaf(w3.x, xb.z, s);
-  s = fmaf(w3.y, xb.w, s);
+  float s = w0.x * x[0];
+  s = fmaf(w0.y, x[1], s);
+  s = fmaf(w1.x, x[2], s);
+  s = fmaf(w1.y, x[3], s);
+  s = fmaf(w2.x, x[4], s);
+  s = fmaf(w2.y, x[5], s);
+  s = fmaf(w3.x, x[6], s);
+  s = fmaf(w3.y, x[7], s);
   return s;
 }
 
@@ -183,6 +229,7 @@ struct Smem {
   float* tsum;
   float* tv;
   volatile int* flags;  // [0] done (consumers finished), [1] error, [2] argmax result
+  GptLayerPtrs* layers;  // [24]
 };
 
 __device__ __forceinline__ Smem smem_of(uint8_t* base) {
@@ -195,27 +242,37 @@ __device__ __forceinline__ Smem smem_of(uint8_t* base) {
   s.tsum = reinterpret_cast<float*>(base + kOffTsum);
   s.tv = reinterpret_cast<float*>(base + kOffTv);
   s.flags = reinterpret_cast<volatile int*>(base + kOffFlags);
+  s.layers = reinterpret_cast<GptLayerPtrs*>(base + kOffLayers);
   return s;
 }
 
-// Grid barrier over the consumers of all CTAs: arrival counter, bounded spin.
-// Returns false (and marks the CTA's error flag) when the wait gave up.
-__device__ __forceinline__ bool grid_sync(const GptPersistParams& p, unsigned int target, const Smem& sm) {
+__device__ __forceinline__ void red_add_release(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid barrier k over the consumers of all CTAs: after the CTA barrier,
+// thread 0 adds one to the arrival counter with a release reduction (the
+// CTA's writes, ordered before it by the CTA barrier, are released; nothing
+// waits for the add to return) and polls the counter with acquire loads until
+// all k * G arrivals are in (bounded spin); the CTA barrier then passes the
+// acquired writes on to the CTA. Returns false (and marks the CTA's error
+// flag) when the wait gave up. `arrive`, when non-null, receives the global
+// timer at this CTA's arrival (stage trace).
+__device__ __forceinline__ bool grid_sync(const GptPersistParams& p, unsigned int k, const Smem& sm,
+                                          unsigned long long* arrive) {
   cbar();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(p.barrier, 1u);
+    const unsigned int target = k * gridDim.x;
+    if (arrive) *arrive = globaltimer();
+    red_add_release(p.barrier, 1u);
     const long long start = clock64();
-    bool ok = true;
     while (ld_acquire(p.barrier) < target) {
       if (clock64() - start > kWaitBudgetCycles) {
         atomicCAS(p.status, 0u, kDevTimeoutGrid);
-        ok = false;
+        sm.flags[1] = 1;
         break;
       }
     }
-    __threadfence();
-    if (!ok) sm.flags[1] = 1;
   }
   cbar();
   return sm.flags[1] == 0;
@@ -244,7 +301,7 @@ __device__ void producer(const GptPersistParams& p, const Smem& sm) {
   bool stop = false;
   auto issue = [&](int stage, int layer) {
     if (stop) return;
-    const ProjDesc d = proj_of(p, stage, layer);
+    const ProjDesc d = proj_of(p, sm.layers, stage, layer);
     int r0, r1;
     rows_of(d.n, b, G, r0, r1);
     const uint32_t bytes = static_cast<uint32_t>(r1 - r0) * d.k * 2;
@@ -279,26 +336,62 @@ __device__ void producer(const GptPersistParams& p, const Smem& sm) {
 
 // ---------------------------------------------------------------- consumers
 
+// The epilogue operands of the CTA's rows (one row per consumer thread):
+// bias and residual, loaded before the stage's prologue so that their
+// latency overlaps it. The residual (x for attn.c_proj, h for mlp.c_proj)
+// was written at least one grid barrier earlier.
+template <int STAGE>
+__device__ __forceinline__ void epi_prefetch(const GptPersistParams& p, const Smem& sm, int layer, float& eb,
+                                             float& er) {
+  const ProjDesc d = proj_of(p, sm.layers, STAGE, layer);
+  int r0, r1;
+  rows_of(stage_n(STAGE), blockIdx.x, gridDim.x, r0, r1);
+  const int r = r0 + threadIdx.x;
+  const bool mine = r < r1;
+  eb = mine ? d.bias[r] : 0.0f;
+  er = 0.0f;
+  if (STAGE == kSProj && mine) er = __ldcg(p.x + r);
+  if (STAGE == kSMproj && mine) er = __ldcg(p.h + r);
+}
+
 // The CTA's part of one projection: tasks (row, 1280-column slice) from the
 // ring, then the epilogue per row. `it` = the ring position of the stage's
 // first slot. Returns false when a slot wait gave up.
 template <int STAGE>
-__device__ bool cons_proj(const GptPersistParams& p, const Smem& sm, int layer, uint32_t& it) {
+__device__ bool cons_proj(const GptPersistParams& p, const Smem& sm, int layer, uint32_t& it, float eb, float er,
+                          unsigned long long* slots_done) {
   const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const ProjDesc d = proj_of(p, STAGE, layer);
   int r0, r1;
-  rows_of(d.n, b, G, r0, r1);
-  const int segs = d.k / kTaskCols;
+  rows_of(stage_n(STAGE), b, G, r0, r1);
+  constexpr int segs = stage_k(STAGE) / kTaskCols;
   const int T = (r1 - r0) * segs;
   const int S = (T + kSlotTasks - 1) / kSlotTasks;
   const int wg = warp >> 3, wt = warp & 7;  // warps 0-7 take even slots, 8-15 odd ones
+  // A slot holds 8 tasks and segs divides 8, so a warp always works on the
+  // same 1280-column segment of the input row: its lanes keep their 40 input
+  // values in registers for the whole stage, and only the weights stream
+  // from shared memory.
+  float xr[kTaskCols / 256][8];
+  {
+    const float* xb = sm.xs + (wt % segs) * kTaskCols;
+#pragma unroll
+    for (int c = 0; c < kTaskCols / 256; ++c) {
+      const float4 a = *reinterpret_cast<const float4*>(xb + (lane + 32 * c) * 8);
+      const float4 e = *reinterpret_cast<const float4*>(xb + (lane + 32 * c) * 8 + 4);
+      xr[c][0] = a.x, xr[c][1] = a.y, xr[c][2] = a.z, xr[c][3] = a.w;
+      xr[c][4] = e.x, xr[c][5] = e.y, xr[c][6] = e.z, xr[c][7] = e.w;
+    }
+  }
+  unsigned long long waited = 0;  // stage trace: time thread 0 spent waiting for its slots
   for (int sp = 0; sp < S; sp += 2) {
     const int si = sp + wg;
     if (si < S) {
       const uint32_t ig = it + si;
       const int slot = static_cast<int>(ig % kSlots);
+      const unsigned long long w0 = slots_done ? globaltimer() : 0;
       // warp-uniform outcome, so that the shuffles below see every lane
       const bool got = __all_sync(0xffffffffu, mbar_wait(&sm.full[slot], (ig / kSlots) & 1, p.status, kDevTimeoutSlot));
+      if (slots_done) waited += globaltimer() - w0;
       if (!got) {
         sm.flags[1] = 1;
       } else {
@@ -306,10 +399,9 @@ __device__ bool cons_proj(const GptPersistParams& p, const Smem& sm, int layer, 
         if (task < T) {
           const uint4* wr = reinterpret_cast<const uint4*>(sm.ring + static_cast<size_t>(slot) * kSlotBytes +
                                                           static_cast<size_t>(wt) * kTaskBytes);
-          const float* xb = sm.xs + (task % segs) * kTaskCols;
           float s = 0.0f;
 #pragma unroll
-          for (int c = 0; c < kTaskCols / 256; ++c) s += dot8(wr[lane + 32 * c], xb + (lane + 32 * c) * 8);
+          for (int c = 0; c < kTaskCols / 256; ++c) s += dot8r(wr[lane + 32 * c], xr[c]);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
           if (lane == 0) sm.tsum[task] = s;
@@ -320,20 +412,24 @@ __device__ bool cons_proj(const GptPersistParams& p, const Smem& sm, int layer, 
     }
   }
   it += S;
+  if (slots_done && tid == 0) {
+    *slots_done = globaltimer();
+    slots_done[kGptTraceCap + kGptTraceStages * gridDim.x] = waited;  // stored after the arrivals
+  }
   cbar();
   if (sm.flags[1]) return false;
-  for (int r = tid; r < r1 - r0; r += kCons) {
+  if (tid < r1 - r0) {
     float s = 0.0f;
-    for (int q = 0; q < segs; ++q) s += sm.tsum[r * segs + q];
-    const int n = r0 + r;
-    const float v = s + d.bias[n];
+    for (int q = 0; q < segs; ++q) s += sm.tsum[tid * segs + q];
+    const int n = r0 + tid;
+    const float v = s + eb;
     if (STAGE == kSQkv) p.qkv[n] = v;
-    if (STAGE == kSProj) p.h[n] = __ldcg(p.x + n) + v;
+    if (STAGE == kSProj) p.h[n] = er + v;
     if (STAGE == kSFc) p.m[n] = gelu_new(v);
-    if (STAGE == kSMproj) p.x[n] = __ldcg(p.h + n) + v;
+    if (STAGE == kSMproj) p.x[n] = er + v;
     if (STAGE == kSHead) {
       p.logits[n] = v;
-      sm.tv[r] = v;
+      sm.tv[tid] = v;
     }
   }
   if (STAGE == kSHead) {
@@ -357,7 +453,8 @@ __device__ bool cons_proj(const GptPersistParams& p, const Smem& sm, int layer, 
 // (cpu_attention_single_query, runtime/impl/tokenizer_tests.cpp:4034-4061):
 // partial (max, sum e^(s-max), sum e^(s-max) v) over keys [j0, j1) of the
 // len + 1 keys (this token's K and V read from qkv); range 0 also appends
-// this token's K and V at row len of the layer's cache.
+// this token's K and V at row len of the layer's cache. q, the first keys and
+// the first values are loaded together (one memory round trip).
 __device__ void cons_attention(const GptPersistParams& p, const Smem& sm, int layer, int len) {
   const int b = blockIdx.x, tid = threadIdx.x;
   const int h = b / kSplits, r = b - h * kSplits;
@@ -368,7 +465,6 @@ __device__ void cons_attention(const GptPersistParams& p, const Smem& sm, int la
   const float* kcur = p.qkv + kW + h * 64;
   const float* vcur = p.qkv + 2 * kW + h * 64;
   float* s = sm.xs;
-  float* q = sm.xs + kScrQ;
   float* accw = sm.xs + kScrAcc;
   if (r == 0) {
     const size_t cur = static_cast<size_t>(len) * kW + h * 64;
@@ -380,11 +476,21 @@ __device__ void cons_attention(const GptPersistParams& p, const Smem& sm, int la
     if (tid < kPart) out[tid] = tid == 0 ? -INFINITY : 0.0f;
     return;
   }
-  if (tid < 64) q[tid] = __ldcg(p.qkv + h * 64 + tid);
-  cbar();
-  // scores: 16 lanes per key (a float4 of the 64 dims each), 4 keys in flight per group
+  const int cnt = j1 - j0;
   const int g = tid >> 4, l = tid & 15;
-  const float4 qv = reinterpret_cast<const float4*>(q)[l];
+  const int w = tid >> 5, lane = tid & 31;
+  auto vrow = [&](int j) {  // value row of key j0 + j (this token's from qkv)
+    const int jj = j0 + j;
+    return jj == len ? vcur : vc + static_cast<size_t>(jj) * kW + h * 64;
+  };
+  const float4 qv = __ldcg(reinterpret_cast<const float4*>(p.qkv + h * 64) + l);
+  float2 vv0[4];  // values of keys w, w+16, w+32, w+48 (the first PV block)
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int j = w + 16 * u;
+    vv0[u] = j < cnt ? __ldcg(reinterpret_cast<const float2*>(vrow(j) + 2 * lane)) : make_float2(0.f, 0.f);
+  }
+  // scores: 16 lanes per key (a float4 of the 64 dims each), 4 keys in flight per group
   for (int base = j0; base < j1; base += 128) {
     float4 kv[4];
 #pragma unroll
@@ -406,7 +512,6 @@ __device__ void cons_attention(const GptPersistParams& p, const Smem& sm, int la
     }
   }
   cbar();
-  const int cnt = j1 - j0;
   float mx = -INFINITY;
   for (int j = tid; j < cnt; j += kCons) mx = fmaxf(mx, s[j]);
   mx = cmax(mx, sm.red);
@@ -418,16 +523,14 @@ __device__ void cons_attention(const GptPersistParams& p, const Smem& sm, int la
   }
   den = csum(den, sm.red);  // its barriers also order the writes of s before the reads below
   // acc: warp w takes keys w, w+16, ...; lane dims 2 lane, 2 lane + 1
-  const int w = tid >> 5, lane = tid & 31;
   float2 acc = make_float2(0.f, 0.f);
   for (int base = 0; base < cnt; base += 64) {
     float2 vv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int j = base + w + 16 * u;
-      const int jj = j0 + j;
-      const float* vp = jj == len ? vcur : vc + static_cast<size_t>(jj) * kW + h * 64;
-      vv[u] = j < cnt ? __ldcg(reinterpret_cast<const float2*>(vp + 2 * lane)) : make_float2(0.f, 0.f);
+      vv[u] = base == 0 ? vv0[u]
+                        : (j < cnt ? __ldcg(reinterpret_cast<const float2*>(vrow(j) + 2 * lane)) : make_float2(0.f, 0.f));
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -452,29 +555,55 @@ __device__ void cons_attention(const GptPersistParams& p, const Smem& sm, int la
 }
 
 // The attention partials merged into the heads' outputs (xs[0, kW)):
-// M = max_r m_r, out = sum_r acc_r e^(m_r - M) / sum_r l_r e^(m_r - M).
-__device__ __forceinline__ void cons_attn_combine(const GptPersistParams& p, float* xs) {
-  for (int i = threadIdx.x; i < kW; i += kCons) {
-    const int h = i >> 6, d = i & 63;
-    const float* pp = p.part + static_cast<size_t>(h) * kSplits * kPart;
-    float ms[kSplits], ls[kSplits];
+// M = max_r m_r, out = sum_r acc_r e^(m_r - M) / sum_r l_r e^(m_r - M), ranges
+// in index order. Threads 0..139 read one (head, range) max and sum each, the
+// others' accumulator loads are issued at the same time; the per-head
+// weights e^(m_r - M) / L go through shared memory (after the scores'
+// scratch, which is free by now).
+__device__ __forceinline__ void cons_attn_combine(const GptPersistParams& p, float* xs, float* wsc) {
+  const int tid = threadIdx.x;
+  float as[kPer][kSplits];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = tid + k * kCons;
+    const int ii = i < kW ? i : 0;
+    const float* pp = p.part + static_cast<size_t>(ii >> 6) * kSplits * kPart + 2 + (ii & 63);
+#pragma unroll
+    for (int r = 0; r < kSplits; ++r) as[k][r] = __ldcg(pp + r * kPart);
+  }
+  float m = 0.0f, l = 0.0f;
+  if (tid < kAttnCtas) {
+    m = __ldcg(p.part + static_cast<size_t>(tid) * kPart);
+    l = __ldcg(p.part + static_cast<size_t>(tid) * kPart + 1);
+    wsc[tid] = m;
+    wsc[kAttnCtas + tid] = l;
+  }
+  cbar();
+  if (tid < kAttnCtas) {  // weight of range r of head h: e^(m_r - M) / L (0 for empty ranges)
+    const int h = tid / kSplits;
     float M = -INFINITY;
 #pragma unroll
-    for (int r = 0; r < kSplits; ++r) {
-      ms[r] = __ldcg(pp + r * kPart);
-      ls[r] = __ldcg(pp + r * kPart + 1);
-      if (ls[r] > 0.0f) M = fmaxf(M, ms[r]);
-    }
-    float L = 0.0f, A = 0.0f;
+    for (int r = 0; r < kSplits; ++r)
+      if (wsc[kAttnCtas + h * kSplits + r] > 0.0f) M = fmaxf(M, wsc[h * kSplits + r]);
+    float L = 0.0f;
 #pragma unroll
     for (int r = 0; r < kSplits; ++r) {
-      if (ls[r] > 0.0f) {
-        const float e = expf(ms[r] - M);
-        L = fmaf(ls[r], e, L);
-        A = fmaf(__ldcg(pp + r * kPart + 2 + d), e, A);
-      }
+      const float lr = wsc[kAttnCtas + h * kSplits + r];
+      if (lr > 0.0f) L = fmaf(lr, expf(wsc[h * kSplits + r] - M), L);
     }
-    xs[i] = A / L;
+    wsc[2 * kAttnCtas + tid] = l > 0.0f ? expf(m - M) / L : 0.0f;
+  }
+  cbar();
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = tid + k * kCons;
+    if (i < kW) {
+      const float* wr = wsc + 2 * kAttnCtas + (i >> 6) * kSplits;
+      float A = 0.0f;
+#pragma unroll
+      for (int r = 0; r < kSplits; ++r) A = fmaf(as[k][r], wr[r], A);
+      xs[i] = A;
+    }
   }
   cbar();
 }
@@ -492,6 +621,11 @@ __global__ void __launch_bounds__(kThreads, 1) gpt_persist_kernel(GptPersistPara
     sm.flags[0] = 0;
     sm.flags[1] = 0;
   }
+  {  // the layer pointer table into shared memory
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(p.layers);
+    uint64_t* dst = reinterpret_cast<uint64_t*>(sm.layers);
+    for (int i = tid; i < static_cast<int>(sizeof(GptLayerPtrs) * kLayers / 8); i += kThreads) dst[i] = src[i];
+  }
   __syncthreads();
   if (tid >= kCons) {
     if (tid == kCons) producer(p, sm);
@@ -502,70 +636,127 @@ __global__ void __launch_bounds__(kThreads, 1) gpt_persist_kernel(GptPersistPara
   unsigned int bar_k = 0;
   int len = 0, step = 0, code = kStart;
   bool ok = true;
+  bool tracing = false, trace_arrivals = false;
+  int stage_no = 0;  // stage index within the traced token
   auto sync = [&]() {
-    ++bar_k;
-    return grid_sync(p, bar_k * static_cast<unsigned int>(G), sm);
+    unsigned long long* arrive =
+        trace_arrivals ? p.trace + kGptTraceCap + static_cast<size_t>(stage_no) * G + b : nullptr;
+    ++stage_no;
+    return grid_sync(p, ++bar_k, sm, arrive);
   };
+  int tr = 0;
+  auto mark = [&]() {
+    if (tracing && tr < kGptTraceCap) p.trace[tr++] = globaltimer();
+  };
+  auto slot_mark = [&]() -> unsigned long long* {  // reserves the "slots done" point
+    return tracing && tr < kGptTraceCap ? p.trace + tr++ : nullptr;
+  };
+  float v[kPer], gg[kPer], bb[kPer];
+  float eb, er;
   const int tokens = p.P + p.max_steps;
   for (int tok = 0; tok < tokens && ok; ++tok) {
     const bool decode = tok >= p.P;
     if (tok == p.P && b == 0 && tid == 0) p.times[1] = globaltimer();
+    tracing = p.trace != nullptr && tok == p.P && b == 0 && tid == 0;
+    trace_arrivals = p.trace != nullptr && tok == p.P && tid == 0;
+    stage_no = 0;
+    mark();
     for (int l = 0; l < kLayers && ok; ++l) {
-      const GptLayerPtrs& L = p.layers[l];
-      // c_attn(ln_1(x)); layer 0 builds x (the prefix row, or mel_embedding[code]
-      // + mel_pos_embedding[step] as build_gpt_greedy_current_cpu,
-      // runtime/impl/gpt.cpp:1545-1554) and publishes the CTA's slice of it.
+      const GptLayerPtrs& L = sm.layers[l];
+      // ---- c_attn(ln_1(x)). Layer 0 builds x (the prefix row, or
+      // mel_embedding[code] + mel_pos_embedding[position] as
+      // build_gpt_greedy_current_cpu, runtime/impl/gpt.cpp:1545-1554, with
+      // gpt_cached_generate_position, :1873-1875) and publishes the CTA's
+      // slice of it for the residual of attn.c_proj.
+      epi_prefetch<kSQkv>(p, sm, l, eb, er);
+      load_params(L.ln1_g, L.ln1_b, gg, bb);
       if (l == 0) {
-        const float* e0 = decode ? p.emb + static_cast<size_t>(code) * kW : p.prefix + static_cast<size_t>(tok) * kW;
-        // gpt_cached_generate_position (runtime/impl/gpt.cpp:1873-1875)
         const int position = p.hf_positions && step > 0 ? step + 1 : step;
+        const float* e0 = decode ? p.emb + static_cast<size_t>(code) * kW : p.prefix + static_cast<size_t>(tok) * kW;
         const float* e1 = p.pos + static_cast<size_t>(position) * kW;
         const int x0 = static_cast<int>(static_cast<long long>(b) * kW / G);
         const int x1 = static_cast<int>(static_cast<long long>(b + 1) * kW / G);
-        for (int i = tid; i < kW; i += kCons) {
-          const float v = decode ? e0[i] + e1[i] : e0[i];
-          sm.xs[i] = v;
-          if (i >= x0 && i < x1) p.x[i] = v;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int i = tid + k * kCons;
+          v[k] = i < kW ? (decode ? e0[i] + e1[i] : e0[i]) : 0.0f;
+          if (i >= x0 && i < x1) p.x[i] = v[k];
         }
       } else {
-        for (int i = tid; i < kW; i += kCons) sm.xs[i] = __ldcg(p.x + i);
+        load_row_cg(p.x, v);
       }
-      cbar();
-      cons_layer_norm(sm.xs, L.ln1_g, L.ln1_b, sm.red);
-      ok = cons_proj<kSQkv>(p, sm, l, it) && sync();
+      layer_norm_regs(v, gg, bb, sm.red);
+      store_row(v, sm.xs);
+      mark();
+      ok = cons_proj<kSQkv>(p, sm, l, it, eb, er, slot_mark());
+      mark();
+      ok = ok && sync();
+      mark();
       if (!ok) break;
+      // ---- attention over the cache with this token appended
+      mark();
       if (b < kAttnCtas) cons_attention(p, sm, l, len);
+      mark();
+      mark();
       ok = sync();
+      mark();
       if (!ok) break;
-      cons_attn_combine(p, sm.xs);
-      ok = cons_proj<kSProj>(p, sm, l, it) && sync();
+      // ---- h = x + attn.c_proj(merged heads)
+      epi_prefetch<kSProj>(p, sm, l, eb, er);
+      cons_attn_combine(p, sm.xs, sm.xs + kW);
+      mark();
+      ok = cons_proj<kSProj>(p, sm, l, it, eb, er, slot_mark());
+      mark();
+      ok = ok && sync();
+      mark();
       if (!ok) break;
-      for (int i = tid; i < kW; i += kCons) sm.xs[i] = __ldcg(p.h + i);
-      cbar();
-      cons_layer_norm(sm.xs, L.ln2_g, L.ln2_b, sm.red);
-      ok = cons_proj<kSFc>(p, sm, l, it) && sync();
+      // ---- m = gelu_new(c_fc(ln_2(h)))
+      epi_prefetch<kSFc>(p, sm, l, eb, er);
+      load_params(L.ln2_g, L.ln2_b, gg, bb);
+      load_row_cg(p.h, v);
+      layer_norm_regs(v, gg, bb, sm.red);
+      store_row(v, sm.xs);
+      mark();
+      ok = cons_proj<kSFc>(p, sm, l, it, eb, er, slot_mark());
+      mark();
+      ok = ok && sync();
+      mark();
       if (!ok) break;
+      // ---- x = h + mlp.c_proj(m)
+      epi_prefetch<kSMproj>(p, sm, l, eb, er);
       for (int i = tid; i < kMlp; i += kCons) sm.xs[i] = __ldcg(p.m + i);
       cbar();
-      ok = cons_proj<kSMproj>(p, sm, l, it) && sync();
+      mark();
+      ok = cons_proj<kSMproj>(p, sm, l, it, eb, er, slot_mark());
+      mark();
+      ok = ok && sync();
+      mark();
     }
     if (!ok) break;
     ++len;
     if (!decode) continue;
-    // ln_f, final_norm, mel head, argmax (runtime/impl/gpt.cpp:1901-1905)
-    for (int i = tid; i < kW; i += kCons) sm.xs[i] = __ldcg(p.x + i);
-    cbar();
-    cons_layer_norm(sm.xs, p.lnf_g, p.lnf_b, sm.red);
-    cons_layer_norm(sm.xs, p.fn_g, p.fn_b, sm.red);
-    ok = cons_proj<kSHead>(p, sm, 0, it) && sync();
+    // ---- ln_f, final_norm, mel head, argmax (runtime/impl/gpt.cpp:1901-1905)
+    epi_prefetch<kSHead>(p, sm, 0, eb, er);
+    float g2[kPer], b2[kPer];
+    load_params(p.lnf_g, p.lnf_b, gg, bb);
+    load_params(p.fn_g, p.fn_b, g2, b2);
+    load_row_cg(p.x, v);
+    layer_norm_regs(v, gg, bb, sm.red);
+    layer_norm_regs(v, g2, b2, sm.red);
+    store_row(v, sm.xs);
+    mark();
+    ok = cons_proj<kSHead>(p, sm, 0, it, eb, er, slot_mark());
+    mark();
+    ok = ok && sync();
+    mark();
     if (!ok) break;
     if (tid == 0) {  // candidates in CTA order = row order: the first maximum
       float bv = __ldcg(p.cand_val);
       int bi = __ldcg(p.cand_idx);
       for (int c = 1; c < G; ++c) {
-        const float v = __ldcg(p.cand_val + c);
-        if (v > bv) {
-          bv = v;
+        const float cv = __ldcg(p.cand_val + c);
+        if (cv > bv) {
+          bv = cv;
           bi = __ldcg(p.cand_idx + c);
         }
       }

@@ -26,12 +26,21 @@ struct GptPersistParams {
   int* cand_idx;              // [grid]
   uint32_t* codes;            // [max_steps]
   int* out;                   // [0] codes produced
-  unsigned int* barrier;      // grid barrier counter, zero at launch
+  unsigned int* barrier;      // grid barrier arrival counter, zero at launch
   unsigned int* status;       // nonzero: a bounded wait gave up
   unsigned long long* times;  // globaltimer at start, end of prefill, end
   int P, max_steps;
   int hf_positions;  // nonzero: decode step s > 0 takes position embedding s + 1
+  // Optional stage trace of the first decode token: CTA 0's global timer when
+  // the token starts and, per stage, when its prologue is done, when its first
+  // warp has finished its weight slots, when its compute is done and when its
+  // grid barrier is passed (kGptTraceCap entries); then every CTA's barrier
+  // arrival per stage ([121][grid]).
+  unsigned long long* trace;
 };
+
+constexpr int kGptTraceCap = 1 + 121 * 4;
+constexpr int kGptTraceStages = 121;
 
 // Dynamic shared memory of one CTA; the one-time function attribute; the
 // launch (cooperative, one CTA per SM, `grid` CTAs).

@@ -39,7 +39,7 @@ EXPORTED = [
     "itts_pipeline_create", "itts_pipeline_destroy", "itts_pipeline_last_error", "itts_pipeline_create_error",
     "itts_pipeline_synthesize",
     "itts_gpt_create", "itts_gpt_destroy", "itts_gpt_last_error", "itts_gpt_create_error", "itts_gpt_generate",
-    "itts_gpt_generate_ex",
+    "itts_gpt_generate_ex", "itts_gpt_set_tracing", "itts_gpt_stage_trace",
     "itts_gpt_timing", "itts_gpt_launch_kernels", "itts_gpt_weight_bytes_per_token",
 ]
 GPT_WIDTH = 1280
@@ -150,6 +150,8 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_gpt_create_error": (C.c_char_p, []),
         "itts_gpt_generate": (i32, [vp, vp, u32, u32, vp, C.POINTER(u32), vp]),
         "itts_gpt_generate_ex": (i32, [vp, vp, u32, u32, u32, vp, C.POINTER(u32), vp]),
+        "itts_gpt_set_tracing": (i32, [vp, i32]),
+        "itts_gpt_stage_trace": (i32, [vp, vp, u32]),
         "itts_gpt_timing": (i32, [vp, C.POINTER(f32), C.POINTER(f32)]),
         "itts_gpt_launch_kernels": (i32, [vp]),
         "itts_gpt_weight_bytes_per_token": (f64, []),
@@ -616,6 +618,16 @@ class GptDecoder:
 
     def launch_kernels(self) -> int:
         return int(self.lib.itts_gpt_launch_kernels(self.h))
+
+    def set_tracing(self, on: bool) -> None:
+        self.lib.itts_gpt_set_tracing(self.h, int(bool(on)))
+
+    def stage_trace(self) -> np.ndarray:
+        """Microseconds since the first decode token started at each trace
+        point of the persistent decoder (empty unless tracing)."""
+        buf = np.zeros(2 * 485 + 121 * 160, np.float64)
+        n = int(self.lib.itts_gpt_stage_trace(self.h, _ptr(buf), buf.size))
+        return buf[:max(n, 0)]
 
     @staticmethod
     def weight_bytes_per_token() -> float:
