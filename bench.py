@@ -375,15 +375,16 @@ def gpt_line(args, rank, world, local, barrier, max_over_ranks, hbm_peak):
     if rank == 0 or world == 1:
         mit2.make_gpt_bundle(GPT_BUNDLE_DIR, seed=0)
     barrier()
+    P_rows, S_steps = args.gpt_prefix, args.gpt_steps
     rng = np.random.default_rng(3000 + rank)
-    prefix = rng.standard_normal((GPT_PREFIX, 1280)).astype(np.float32)
+    prefix = rng.standard_normal((P_rows, 1280)).astype(np.float32)
     dec = itts_cfm.GptDecoder(GPT_BUNDLE_DIR, device=local)
-    dec.generate(prefix, 16)
+    dec.generate(prefix, min(16, S_steps))
     runs, pre, dcd, wall = 3, [], [], []
     for _ in range(runs):
         barrier()
         t0 = time.perf_counter()
-        codes, _ = dec.generate(prefix, GPT_STEPS)
+        codes, _ = dec.generate(prefix, S_steps)
         wall.append(time.perf_counter() - t0)
         p_ms, d_ms = dec.timing()
         pre.append(p_ms)
@@ -391,9 +392,10 @@ def gpt_line(args, rank, world, local, barrier, max_over_ranks, hbm_peak):
     n = len(codes)
     pre_ms, dec_ms, t_e2e = (max_over_ranks(float(np.median(v))) for v in (pre, dcd, wall))
     launches = dec.launch_kernels()
+    trace = gpt_stage_trace(dec, prefix) if args.gpt_trace else None
     dec.close()
     wb = itts_cfm.GptDecoder.weight_bytes_per_token()
-    kv = 24 * 1280 * 2 * 4 * (GPT_PREFIX + 0.5 * (n + 1))  # fp32 K and V rows read per token, mean over the run
+    kv = 24 * 1280 * 2 * 4 * (P_rows + 0.5 * (n + 1))  # fp32 K and V rows read per token, mean over the run
     gbs = (wb + kv) / (dec_ms / n / 1e3) / 1e9
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -410,15 +412,43 @@ def gpt_line(args, rank, world, local, barrier, max_over_ranks, hbm_peak):
         cpu = {"value": (ps + ss) / dt, "unit": "tokens/s (prefix rows + decode steps)", "cores": cores, "kind": "port",
                "sample": f"oracle/gpt_oracle.py greedy, {ps} prefix rows + {ss} steps, numpy BLAS; {dt:.2f} s"}
     return {"metric": "GPT mel-code decode, tokens/s (cached greedy, one utterance per GPU)",
-            "value": n * world / (dec_ms / 1e3), "unit": "tokens/s", "prefix_rows": GPT_PREFIX, "steps": n,
-            "ms_per_token": dec_ms / n, "prefill_ms": pre_ms, "prefill_ms_per_row": pre_ms / GPT_PREFIX,
+            "value": n * world / (dec_ms / 1e3), "unit": "tokens/s", "prefix_rows": P_rows, "steps": n,
+            "ms_per_token": dec_ms / n, "prefill_ms": pre_ms, "prefill_ms_per_row": pre_ms / max(P_rows, 1),
             "gpu_launches": launches,
             "path": "graphs per token" if os.environ.get("ITTS_GPT_MODE") == "graph" else "one persistent kernel per call",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                          "bytes_per_token": wb + kv, "note": "f16 weights once per token + mean fp32 KV-cache reads"},
             "e2e": {"value": n * world / t_e2e, "unit": "tokens/s (prefill included)",
                     "h2d_bytes_per_step": int(prefix.nbytes), "d2h_bytes_per_step": int(n * 4 + 8194 * 4)},
-            "cpu_baseline": cpu}
+            "cpu_baseline": cpu, "stage_trace": trace}
+
+
+def gpt_stage_trace(dec, prefix):
+    """Per-stage time split of the persistent decoder's first decode token
+    (mean over the 24 layers, microseconds), from its global-timer trace:
+    prologue, weight slots (ring compute), epilogue, barrier wait of CTA 0;
+    the barrier's latency after the last CTA arrived, the arrival skew (last
+    minus median), and CTA 0's wait for weight slots."""
+    dec.set_tracing(True)
+    dec.generate(prefix, 4)
+    t = dec.stage_trace()
+    dec.set_tracing(False)
+    H, S = 485, 121
+    G = (len(t) - 2 * H) // S
+    if G <= 0:
+        return None
+    cta0, arr, wait = t[:H], t[H:H + S * G].reshape(S, G), t[H + S * G:]
+    names = ["c_attn", "attention", "attn.c_proj", "c_fc", "mlp.c_proj"]
+    acc = {}
+    for s in range(S):
+        nm = "head" if s == S - 1 else names[s % 5]
+        start, pro, slots, comp, syn = cta0[4 * s:4 * s + 5]
+        acc.setdefault(nm, []).append((pro - start, slots - pro, comp - slots, syn - comp, syn - arr[s].max(),
+                                       arr[s].max() - np.median(arr[s]), wait[4 * s + 2]))
+    keys = ["prologue", "slots", "epilogue", "barrier_wait", "barrier_latency", "arrival_skew", "slot_wait"]
+    out = {nm: dict(zip(keys, (round(float(x), 3) for x in np.mean(v, axis=0)))) for nm, v in acc.items()}
+    out["token_us"] = round(float(cta0[H - 1]), 1)
+    return out
 
 
 def pipeline_line(cfg, rank, world, local, barrier, max_over_ranks):
@@ -522,6 +552,10 @@ def main():
     ap.add_argument("--pipeline", type=int, default=1,
                     help="also time the whole semantic-features-to-waveform chain (0 = skip)")
     ap.add_argument("--gpt", type=int, default=1, help="also time the GPT mel-code decoder (0 = skip)")
+    ap.add_argument("--gpt-only", action="store_true", help="time only the GPT decoder and print its line")
+    ap.add_argument("--gpt-prefix", type=int, default=GPT_PREFIX, help="GPT prefix rows")
+    ap.add_argument("--gpt-steps", type=int, default=GPT_STEPS, help="GPT decode steps")
+    ap.add_argument("--gpt-trace", action="store_true", help="add the persistent decoder's stage trace to the gpt line")
     ap.add_argument("--vocoder-only", action="store_true",
                     help="time only the BigVGAN vocoder and print its line (profiling aid)")
     args = ap.parse_args()
@@ -559,6 +593,17 @@ def main():
         return float(t.item())
 
     cfg = workloads.CONFIGS[args.workload]
+    if args.gpt_only:
+        peaks, _ = measured_peaks()
+        g = gpt_line(args, rank, world, local, barrier, max_over_ranks, float(peaks.get("hbm_gbs", 6546.0)))
+        if rank == 0:
+            print(json.dumps(dict(g, n_gpus=world, higher_is_better=True, scaling="weak", data="synthetic",
+                                  dtype="f32 activations, f16 weights",
+                                  config={"workload": f"GPT decode: {g['prefix_rows']} prefix rows + "
+                                                      f"{g['steps']} steps, random-init f16 weights seed 0"})))
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
     if args.vocoder_only:
         peaks, _ = measured_peaks()
         v = vocoder_line(args, cfg, rank, world, local, barrier, max_over_ranks,
