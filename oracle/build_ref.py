@@ -50,6 +50,7 @@ RANGES = [
     ("runtime/impl/gpt.cpp", 1297, 1308),  # argmax
     ("runtime/impl/gpt.cpp", 1545, 1554),  # GPT current-token embedding
     ("runtime/impl/gpt.cpp", 1583, 1590),  # GPT greedy outputs
+    ("runtime/impl/gpt.cpp", 1592, 1755),  # GPT sampling: config, SplitMix64, logits processors, sampler
     ("runtime/impl/gpt.cpp", 1792, 1806),  # GPT KV prefill
     ("runtime/impl/gpt.cpp", 1873, 1909),  # GPT KV greedy decode
     ("runtime/impl/gpt.cpp", 5271, 5281),  # length regulator front (content_in_proj + interpolation)
@@ -104,6 +105,22 @@ void ref_glue_gpt_kv_greedy(const mit2::Bundle& bundle, const std::vector<float>
   *tokens = o.predicted_tokens;
   *last_logits = o.last_logits;
   *first_stop = o.first_stop_step;
+}
+
+void ref_glue_gpt_sample(const std::vector<float>& logits, const std::vector<uint32_t>& history, uint64_t seed,
+                         float temperature, uint32_t top_k, float top_p, float repetition_penalty, uint32_t draws,
+                         std::vector<float>* processed, std::vector<uint32_t>* tokens) {
+  GptSamplingConfig c;
+  c.do_sample = true;
+  c.seed = seed;
+  c.temperature = temperature;
+  c.top_k = top_k;
+  c.top_p = top_p;
+  c.repetition_penalty = repetition_penalty;
+  *processed = apply_gpt_sampling_processors(logits, history, c);
+  SplitMix64 rng(seed);
+  tokens->clear();
+  for (uint32_t d = 0; d < draws; ++d) tokens->push_back(sample_gpt_token_from_logits(*processed, rng));
 }
 """
 

@@ -227,6 +227,8 @@ class RefOracle:
         L.ref_length_regulator.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
         L.ref_gpt_kv_greedy.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_int, C.c_void_p,
                                         C.POINTER(C.c_uint32), C.c_void_p, C.POINTER(C.c_int)]
+        L.ref_gpt_sample.argtypes = [C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32, C.c_uint64, C.c_float,
+                                     C.c_uint32, C.c_float, C.c_float, C.c_uint32, C.c_void_p, C.c_void_p]
         L.ref_bigvgan_activation.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
 
     def _ok(self, rc):
@@ -295,6 +297,19 @@ class RefOracle:
                                             _p(toks), C.byref(n),
                                             _p(logits), C.byref(stop)))
         return toks[: n.value].tolist(), logits, stop.value
+
+    def gpt_sample(self, logits, history, seed: int, temperature: float, top_k: int, top_p: float,
+                   repetition_penalty: float, draws: int):
+        """apply_gpt_sampling_processors + `draws` x sample_gpt_token_from_logits
+        (one SplitMix64 stream): (processed logits, tokens)."""
+        logits = _f32(logits)
+        history = np.ascontiguousarray(history, np.uint32)
+        proc = np.empty_like(logits)
+        toks = np.zeros(max(draws, 1), np.uint32)
+        self._ok(self.lib.ref_gpt_sample(_p(logits), logits.size, _p(history), history.size, int(seed),
+                                         float(temperature), int(top_k), float(top_p), float(repetition_penalty),
+                                         int(draws), _p(proc), _p(toks)))
+        return proc, toks[:draws].tolist()
 
     def length_regulator(self, x, n_out: int):
         x = _f32(x)

@@ -37,6 +37,9 @@ std::vector<float> run_length_regulator_full_cpu(const mit2::Bundle& bundle, con
 void ref_glue_gpt_kv_greedy(const mit2::Bundle& bundle, const std::vector<float>& prefix, uint32_t prefix_tokens,
                             uint32_t steps, bool hf_generate_positions, std::vector<uint32_t>* tokens,
                             std::vector<float>* last_logits, int* first_stop);
+void ref_glue_gpt_sample(const std::vector<float>& logits, const std::vector<uint32_t>& history, uint64_t seed,
+                         float temperature, uint32_t top_k, float top_p, float repetition_penalty, uint32_t draws,
+                         std::vector<float>* processed, std::vector<uint32_t>* tokens);
 std::vector<float> run_bigvgan_activation_cpu(const mit2::Bundle& bundle, const std::string& prefix,
                                               const std::vector<float>& x, uint32_t tokens, uint32_t channels);
 
@@ -165,6 +168,22 @@ int ref_gpt_kv_greedy(const char* bundle_dir, const float* prefix, uint32_t P, u
     std::memcpy(tokens, t.data(), t.size() * sizeof(uint32_t));
     *n_tokens = static_cast<uint32_t>(t.size());
     std::memcpy(last_logits, l.data(), l.size() * sizeof(float));
+  });
+}
+
+// apply_gpt_sampling_processors + sample_gpt_token_from_logits: the processed
+// logits [n] of one step and `draws` tokens drawn from them with one SplitMix64
+// stream seeded `seed`.
+int ref_gpt_sample(const float* logits, uint32_t n, const uint32_t* history, uint32_t n_history, uint64_t seed,
+                   float temperature, uint32_t top_k, float top_p, float repetition_penalty, uint32_t draws,
+                   float* processed, uint32_t* tokens) {
+  return guard([&] {
+    std::vector<float> p;
+    std::vector<uint32_t> t;
+    ref_glue_gpt_sample(std::vector<float>(logits, logits + n), std::vector<uint32_t>(history, history + n_history),
+                        seed, temperature, top_k, top_p, repetition_penalty, draws, &p, &t);
+    std::memcpy(processed, p.data(), p.size() * sizeof(float));
+    std::memcpy(tokens, t.data(), t.size() * sizeof(uint32_t));
   });
 }
 

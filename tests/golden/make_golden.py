@@ -31,8 +31,12 @@ Cases (inputs follow the reference's self-tests where it has them):
                     on a seeded 4-row prefix for 3 steps, synthetic GPT bundle seed 0
   kat_gpt_decode_hf the same with hf_generate_positions = true (the synthesis
                     pipeline's call) on a seeded 5-row prefix for 3 steps
+  kat_gpt_sampling  apply_gpt_sampling_processors + sample_gpt_token_from_logits
+                    (repetition penalty, temperature, top-k, top-p, SplitMix64
+                    draws) on the reference's own test vector and on the GPT
+                    golden's last logits under five configurations
 
-    python tests/golden/make_golden.py [--only bigvgan|lr|gpt|gpt_hf]
+    python tests/golden/make_golden.py [--only bigvgan|lr|gpt|gpt_hf|gpt_sampling]
 """
 from __future__ import annotations
 
@@ -116,6 +120,37 @@ def gpt_cases():
                         last_logits=logits, first_stop=np.int32(stop), bundle_seed=0, weights_sha256=weights_sha(gb))
 
 
+SAMPLING_CASES = [
+    # (name, seed, temperature, top_k, top_p, repetition_penalty, draws)
+    ("ref_test", 20240605, 0.5, 4, 0.95, 2.0, 8),          # the reference's own processors test
+    ("production", 20240605, 0.8, 30, 0.8, 10.0, 32),     # the synthesis pipeline's sampled call
+    ("wide", 7, 1.0, 200, 0.95, 1.0, 32),
+    ("greedy_k1", 11, 0.8, 1, 1.0, 1.3, 8),
+    ("big_topp", 3, 1.2, 2048, 0.5, 1.0, 32),
+]
+
+
+def gpt_sampling_cases():
+    """apply_gpt_sampling_processors + sample_gpt_token_from_logits of the
+    reference on its own test vector and on the GPT golden's last logits."""
+    gb = mit2.make_gpt_bundle(ROOT / "gpt_seed0", seed=0)
+    r = oracle.RefOracle(gb)
+    g = np.load(HERE / "kat_gpt_decode.npz")
+    big = g["last_logits"].astype(np.float32)
+    hist_big = np.array([1] * 30 + [8192] + [int(c) for c in g["codes"]], np.uint32)
+    out = {}
+    for name, seed, t, k, p, pen, draws in SAMPLING_CASES:
+        logits = np.arange(-2, 8, dtype=np.float32) if name == "ref_test" else big
+        hist = np.array([2, 7, 3, 7], np.uint32) if name == "ref_test" else hist_big
+        proc, toks = r.gpt_sample(logits, hist, seed, t, k, p, pen, draws)
+        out[f"{name}_logits"] = logits
+        out[f"{name}_history"] = hist
+        out[f"{name}_config"] = np.array([seed, t, k, p, pen, draws], np.float64)
+        out[f"{name}_processed"] = proc
+        out[f"{name}_tokens"] = np.array(toks, np.uint32)
+    np.savez_compressed(HERE / "kat_gpt_sampling.npz", **out)
+
+
 def gpt_hf_cases():
     """The synthesis pipeline's call (hf_generate_positions = true,
     runtime/impl/tts_synthesis/synthesis_pipeline.cpp:675, 795)."""
@@ -129,9 +164,14 @@ def gpt_hf_cases():
 
 def main():
     only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only == "gpt_sampling":
+        gpt_sampling_cases()
+        print("golden vectors written to", HERE)
+        return
     if only in ("gpt", "gpt_hf"):
         if only == "gpt":
             gpt_cases()
+            gpt_sampling_cases()
         gpt_hf_cases()
         print("golden vectors written to", HERE)
         return
@@ -147,6 +187,7 @@ def main():
     length_regulator_cases()
     gpt_cases()
     gpt_hf_cases()
+    gpt_sampling_cases()
     unit = mit2.make_dit_bundle(ROOT / "seed0_unit", seed=0, init="unit")
     base = mit2.make_dit_bundle(ROOT / "seed0_baseline", seed=0, init="baseline")
     ru, rb = oracle.RefOracle(unit), oracle.RefOracle(base)

@@ -165,6 +165,26 @@ def test_gpt_greedy_decode(gpt_oracle):
     _close(g["last_logits"], logits[-1])
 
 
+@pytest.mark.parametrize("name", ["ref_test", "production", "wide", "greedy_k1", "big_topp"])
+def test_gpt_sampling_matches_reference(name):
+    """The restated logits processors reproduce the reference's processed
+    logits bit for bit (including which entries are -inf), and the restated
+    SplitMix64 sampler its draws; "ref_test" is the reference's own known
+    answer (processed[8] = 12, processed[9] = 14, draw 9)."""
+    import gpt_oracle as G
+
+    g = _load("kat_gpt_sampling")
+    seed, t, k, p, pen, draws = g[f"{name}_config"].tolist()
+    proc = G.sampling_processors(g[f"{name}_logits"], g[f"{name}_history"], t, int(k), p, pen)
+    ref = g[f"{name}_processed"]
+    assert np.array_equal(np.isfinite(proc), np.isfinite(ref))
+    assert np.array_equal(proc[np.isfinite(ref)], ref[np.isfinite(ref)])
+    rng = G.SplitMix64(int(seed))
+    assert [G.sample_token(proc, rng) for _ in range(int(draws))] == g[f"{name}_tokens"].tolist()
+    if name == "ref_test":
+        assert ref[8] == 12.0 and ref[9] == 14.0 and g[f"{name}_tokens"][0] == 9
+
+
 def test_gpt_greedy_decode_hf_positions(gpt_oracle):
     """hf_generate_positions = true, as the synthesis pipeline calls the
     decoder: step s > 0 takes position embedding s + 1."""
