@@ -392,6 +392,17 @@ def gpt_line(args, rank, world, local, barrier, max_over_ranks, hbm_peak):
     n = len(codes)
     pre_ms, dec_ms, t_e2e = (max_over_ranks(float(np.median(v))) for v in (pre, dcd, wall))
     launches = dec.launch_kernels()
+    sampled = None
+    if os.environ.get("ITTS_GPT_MODE") != "graph":  # the synthesis pipeline's sampled call (persistent path)
+        cfg_s = dict(seed=20240605, temperature=0.8, top_k=30, top_p=0.8, repetition_penalty=10.0)
+        hist = [1] * P_rows + [8192]
+        dec.generate_sampled(prefix, min(16, S_steps), cfg_s, history=hist, hf_positions=True)
+        s_codes, _ = dec.generate_sampled(prefix, S_steps, cfg_s, history=hist, hf_positions=True)
+        s_pre, s_dec = dec.timing()
+        s_dec = max_over_ranks(s_dec)
+        sampled = {"config": "temperature 0.8, top_k 30, top_p 0.8, repetition_penalty 10, generate-style positions",
+                   "steps": len(s_codes), "ms_per_token": s_dec / len(s_codes),
+                   "value": len(s_codes) * world / (s_dec / 1e3), "unit": "tokens/s"}
     trace = gpt_stage_trace(dec, prefix) if args.gpt_trace else None
     dec.close()
     wb = itts_cfm.GptDecoder.weight_bytes_per_token()
@@ -420,7 +431,7 @@ def gpt_line(args, rank, world, local, barrier, max_over_ranks, hbm_peak):
                          "bytes_per_token": wb + kv, "note": "f16 weights once per token + mean fp32 KV-cache reads"},
             "e2e": {"value": n * world / t_e2e, "unit": "tokens/s (prefill included)",
                     "h2d_bytes_per_step": int(prefix.nbytes), "d2h_bytes_per_step": int(n * 4 + 8194 * 4)},
-            "cpu_baseline": cpu, "stage_trace": trace}
+            "cpu_baseline": cpu, "sampled": sampled, "stage_trace": trace}
 
 
 def gpt_stage_trace(dec, prefix):

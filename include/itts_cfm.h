@@ -388,6 +388,31 @@ int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32
 #define ITTS_GPT_HF_POSITIONS 0x1u
 int itts_gpt_generate_ex(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t flags,
                          uint32_t* codes, uint32_t* n_codes, float* last_logits);
+
+/* The reference's GptSamplingConfig with do_sample = true
+ * (runtime/impl/gpt.cpp:1592-1599). */
+typedef struct {
+  uint64_t seed;            /* SplitMix64 seed */
+  float temperature;        /* > 0 */
+  uint32_t top_k;           /* 1..ITTS_GPT_SAMPLE_MAX_TOP_K */
+  float top_p;              /* (0, 1] */
+  float repetition_penalty; /* > 0 (1 = off) */
+} itts_gpt_sampling;
+#define ITTS_GPT_SAMPLE_MAX_TOP_K 2048u
+
+/* Sampled decode: as itts_gpt_generate_ex, but each code is drawn as the
+ * reference's sampled step of run_gpt_kv_greedy_metal (runtime/impl/gpt.cpp:
+ * 2220-2233, apply_gpt_sampling_processors :1618-1718 and
+ * sample_gpt_token_from_logits :1720-1755): repetition penalty over
+ * history + the codes so far, temperature, top-k, top-p, one SplitMix64 draw
+ * per step. history [n_history] is its repetition_history_prefix (the
+ * synthesis pipeline passes the prefix's fake_inputs,
+ * runtime/impl/tts_synthesis/synthesis_pipeline.cpp:795-802); NULL / 0 means
+ * [8192]. top_k is bounded (the reference also accepts 0 = off): the finite
+ * set is sorted on the device. */
+int itts_gpt_generate_sampled(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t flags,
+                              const itts_gpt_sampling* sampling, const uint32_t* history, uint32_t n_history,
+                              uint32_t* codes, uint32_t* n_codes, float* last_logits);
 /* Device time (ms) of the last generate's prefill and decode (no reference
  * counterpart); kernel launches of the last generate (1: the whole call is one
  * persistent kernel); f16 weight bytes one decode step streams. */

@@ -81,6 +81,38 @@ int itts_gpt_generate_ex(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uin
   }
 }
 
+int itts_gpt_generate_sampled(itts_gpt_ctx* ctx, const float* prefix, uint32_t P, uint32_t steps, uint32_t flags,
+                              const itts_gpt_sampling* sampling, const uint32_t* history, uint32_t n_history,
+                              uint32_t* codes, uint32_t* n_codes, float* last_logits) {
+  if (!ctx) return ITTS_EINVAL_SHAPE;
+  try {
+    ctx->err.clear();
+    if (!sampling) throw std::invalid_argument("gpt: sampling must be non-null");
+    if (P > ITTS_GPT_MAX_LEN || steps > ITTS_GPT_MAX_STEPS || n_history > ITTS_GPT_MAX_LEN ||
+        sampling->top_k > ITTS_GPT_SAMPLE_MAX_TOP_K)
+      throw std::invalid_argument("gpt: need 1 <= steps <= 1818, P + steps <= 4096, n_history <= 4096, top_k <= 2048");
+    if (flags & ~ITTS_GPT_HF_POSITIONS) throw std::invalid_argument("gpt: unknown flag bits");
+    cudaSetDevice(ctx->dec->device());
+    itts::GptDecoder::Sampling s;
+    s.seed = sampling->seed;
+    s.temperature = sampling->temperature;
+    s.top_k = static_cast<int>(sampling->top_k);
+    s.top_p = sampling->top_p;
+    s.repetition_penalty = sampling->repetition_penalty;
+    const int n = ctx->dec->generate_sampled(prefix, static_cast<int>(P), static_cast<int>(steps),
+                                             (flags & ITTS_GPT_HF_POSITIONS) != 0, s, history,
+                                             static_cast<int>(n_history), codes, last_logits);
+    if (n_codes) *n_codes = static_cast<uint32_t>(n);
+    return ITTS_OK;
+  } catch (const std::exception& e) {
+    ctx->err = e.what();
+    return gclassify(e);
+  } catch (...) {
+    ctx->err = "unknown error";
+    return ITTS_ECUDA;
+  }
+}
+
 int itts_gpt_timing(const itts_gpt_ctx* ctx, float* prefill_ms, float* decode_ms) {
   if (!ctx) return ITTS_EINVAL_SHAPE;
   if (prefill_ms) *prefill_ms = ctx->dec->last_prefill_ms();

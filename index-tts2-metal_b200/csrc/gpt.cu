@@ -566,7 +566,9 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
   check(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device), "SM count");
   const size_t o_layers = carve(sizeof(GptLayerPtrs) * kLayers), o_cval = carve(static_cast<size_t>(sms_) * 4),
                o_cidx = carve(static_cast<size_t>(sms_) * 4), o_bar = carve(512), o_out = carve(16),
-               o_times = carve(4 * 8), o_trace = carve((2 * static_cast<size_t>(kGptTraceCap) + static_cast<size_t>(kGptTraceStages) * sms_) * 8);
+               o_times = carve(4 * 8), o_trace = carve((2 * static_cast<size_t>(kGptTraceCap) + static_cast<size_t>(kGptTraceStages) * sms_) * 8),
+               o_hist = carve(static_cast<size_t>(kMaxLen) * 4), o_seen = carve(((kVocab + 31) / 32) * 4),
+               o_rng = carve(8), o_sampled = carve(4);
   check(cudaMalloc(&state_, off), "gpt state cudaMalloc");
   check(cudaMemset(state_, 0, off), "gpt state memset");
   uint8_t* s = static_cast<uint8_t*>(state_);
@@ -589,6 +591,10 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
   out_ = reinterpret_cast<int*>(s + o_out);
   times_ = reinterpret_cast<unsigned long long*>(s + o_times);
   trace_ = reinterpret_cast<unsigned long long*>(s + o_trace);
+  history_ = reinterpret_cast<uint32_t*>(s + o_hist);
+  seen_ = reinterpret_cast<unsigned int*>(s + o_seen);
+  rng_ = reinterpret_cast<unsigned long long*>(s + o_rng);
+  sampled_ = reinterpret_cast<int*>(s + o_sampled);
   check(cudaMemcpy(layers_dev_, L_, sizeof(GptLayerPtrs) * kLayers, cudaMemcpyHostToDevice), "gpt layer table upload");
   check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   for (auto& e : ev_) check(cudaEventCreate(&e), "cudaEventCreate");
@@ -689,6 +695,32 @@ void GptDecoder::build_graphs() {
 
 int GptDecoder::generate(const float* prefix, int P, int max_steps, bool hf_positions, uint32_t* codes,
                          float* last_logits) {
+  sample_ = false;
+  return generate_common(prefix, P, max_steps, hf_positions, codes, last_logits);
+}
+
+int GptDecoder::generate_sampled(const float* prefix, int P, int max_steps, bool hf_positions, const Sampling& sampling,
+                                 const uint32_t* history, int n_history, uint32_t* codes, float* last_logits) {
+  if (!persistent_) throw std::invalid_argument("gpt: sampled decode needs the persistent decoder");
+  if (!(sampling.temperature > 0.0f)) throw std::invalid_argument("gpt: sampling temperature must be positive");
+  if (sampling.top_k < 1 || sampling.top_k > kGptSampleMaxFinite)
+    throw std::invalid_argument("gpt: sampling top_k must be within 1..2048");
+  if (!(sampling.top_p > 0.0f && sampling.top_p <= 1.0f)) throw std::invalid_argument("gpt: top_p must be in (0, 1]");
+  if (!(sampling.repetition_penalty > 0.0f)) throw std::invalid_argument("gpt: repetition penalty must be positive");
+  if (n_history < 0 || n_history > kMaxLen || (n_history > 0 && !history))
+    throw std::invalid_argument("gpt: the repetition history must hold 0..4096 tokens");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (n_history > 0)
+    check(cudaMemcpyAsync(history_, history, static_cast<size_t>(n_history) * 4, cudaMemcpyHostToDevice, stream_),
+          "gpt history upload");
+  sample_ = true;
+  sampling_ = sampling;
+  n_history_ = n_history;
+  return generate_common(prefix, P, max_steps, hf_positions, codes, last_logits);
+}
+
+int GptDecoder::generate_common(const float* prefix, int P, int max_steps, bool hf_positions, uint32_t* codes,
+                                float* last_logits) {
   const int max_allowed = hf_positions ? kPositions - 1 : kPositions;
   if (P < 0 || max_steps < 1 || max_steps > max_allowed || P + max_steps > kMaxLen)
     throw std::invalid_argument("gpt: need 0 <= P, 1 <= max_steps <= 1818 (1817 with generate-style positions) and "
@@ -705,6 +737,7 @@ int GptDecoder::generate(const float* prefix, int P, int max_steps, bool hf_posi
   check(cudaMemcpy(&st, status_, sizeof(st), cudaMemcpyDeviceToHost), "gpt status read");
   if (st != 0) {
     check(cudaMemset(status_, 0, sizeof(st)), "gpt status clear");
+    if (st == 43) throw std::runtime_error("gpt: sampling: more than 2048 scores tie at the top-k pivot");
     throw std::runtime_error("timeout: a GPT kernel abandoned a bounded wait (device status " + std::to_string(st) + ")");
   }
   if (n < 1 || n > max_steps) throw std::runtime_error("cuda: gpt: decoder produced an invalid step count");
@@ -749,6 +782,17 @@ int GptDecoder::generate_persistent(int P, int max_steps) {
   p.max_steps = max_steps;
   p.hf_positions = hf_ ? 1 : 0;
   p.trace = tracing_ ? trace_ : nullptr;
+  p.sample = sample_ ? 1 : 0;
+  p.temperature = sampling_.temperature;
+  p.top_k = sampling_.top_k;
+  p.top_p = sampling_.top_p;
+  p.repetition_penalty = sampling_.repetition_penalty;
+  p.seed = sampling_.seed;
+  p.history = history_;
+  p.n_history = n_history_;
+  p.seen = seen_;
+  p.rng = rng_;
+  p.sampled = sampled_;
   if (tracing_)
     check(cudaMemsetAsync(trace_, 0,
                           (2 * static_cast<size_t>(kGptTraceCap) + static_cast<size_t>(kGptTraceStages) * sms_) * 8,

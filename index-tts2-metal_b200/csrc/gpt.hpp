@@ -44,6 +44,21 @@ class GptDecoder {
   // hf_positions: the reference's hf_generate_positions (decode step s > 0
   // at position s + 1), as its synthesis pipeline calls the decoder.
   int generate(const float* prefix, int P, int max_steps, bool hf_positions, uint32_t* codes, float* last_logits);
+
+  // The reference's GptSamplingConfig with do_sample (runtime/impl/gpt.cpp:
+  // 1592-1599): repetition penalty, temperature, top-k, top-p, SplitMix64 seed.
+  struct Sampling {
+    unsigned long long seed = 0;
+    float temperature = 1.0f;
+    int top_k = 0;  // 1..2048 (the finite set the device sorts)
+    float top_p = 1.0f;
+    float repetition_penalty = 1.0f;
+  };
+  // As generate, drawing each code from the processed logits instead of the
+  // argmax; history (host, n_history tokens; NULL/0 = [8192]) is the
+  // repetition history before the codes. Persistent path only.
+  int generate_sampled(const float* prefix, int P, int max_steps, bool hf_positions, const Sampling& sampling,
+                       const uint32_t* history, int n_history, uint32_t* codes, float* last_logits);
   // Device time of the last generate call's prefill and decode parts (ms).
   float last_prefill_ms() const { return prefill_ms_; }
   float last_decode_ms() const { return decode_ms_; }
@@ -72,6 +87,8 @@ class GptDecoder {
   void enqueue_layers();
   void build_graphs();
   int generate_persistent(int P, int max_steps);
+  int generate_common(const float* prefix, int P, int max_steps, bool hf_positions, uint32_t* codes,
+                      float* last_logits);
   int generate_graphs(int P, int max_steps);
 
   int device_ = 0;
@@ -104,6 +121,13 @@ class GptDecoder {
   unsigned long long* times_ = nullptr;
   long long launches_ = 0;
   bool hf_ = false;
+  bool sample_ = false;
+  Sampling sampling_;
+  int n_history_ = 0;
+  uint32_t* history_ = nullptr;       // [kMaxLen] device copy of the repetition history
+  unsigned int* seen_ = nullptr;      // sampler scratch: seen-token bitmap
+  unsigned long long* rng_ = nullptr; // sampler scratch: SplitMix64 state
+  int* sampled_ = nullptr;            // sampler scratch: the drawn code
   bool tracing_ = false;
   unsigned long long* trace_ = nullptr;  // [kGptTraceCap]
   cudaGraphExec_t g_prefill_ = nullptr, g_decode_ = nullptr;

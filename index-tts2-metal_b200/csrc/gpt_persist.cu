@@ -51,7 +51,7 @@ constexpr int kTaskBytes = kTaskCols * 2;
 constexpr int kSlotTasks = 8;
 constexpr int kSlotBytes = kSlotTasks * kTaskBytes;  // 20 KB
 constexpr int kMaxTasks = 64;          // tasks of one CTA in one stage
-enum : unsigned int { kDevTimeoutGrid = 40, kDevTimeoutRing = 41, kDevTimeoutSlot = 42 };
+enum : unsigned int { kDevTimeoutGrid = 40, kDevTimeoutRing = 41, kDevTimeoutSlot = 42, kDevSampleTies = 43 };
 
 constexpr size_t kOffXs = static_cast<size_t>(kSlots) * kSlotBytes;
 constexpr size_t kOffBars = kOffXs + static_cast<size_t>(kMlp) * 4;
@@ -608,6 +608,203 @@ __device__ __forceinline__ void cons_attn_combine(const GptPersistParams& p, flo
   cbar();
 }
 
+// ---------------------------------------------------------------- sampler
+
+// SplitMix64 of the reference (runtime/impl/gpt.cpp:1601-1616).
+__device__ __forceinline__ unsigned long long splitmix_next(unsigned long long& state) {
+  unsigned long long z = (state += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Order-preserving unsigned key of a float (larger float -> larger key).
+__device__ __forceinline__ unsigned int fkey(float f) {
+  const unsigned int b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float unfkey(unsigned int k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+constexpr int kSPer = (kVocab + kCons - 1) / kCons;  // scores per consumer thread
+
+// Bitonic sort of n (a power of two <= 2048) (score, index) pairs in shared
+// memory, ascending by index (by_score = false) or by (score, index).
+__device__ void bitonic_pairs(float* ks, int* ki, int n, bool by_score) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int t = threadIdx.x; t < n / 2; t += kCons) {
+        const int i = 2 * t - (t & (j - 1));  // lower element of the pair
+        const int l = i + j;
+        const bool up = (i & k) == 0;
+        const bool gt = by_score ? (ks[i] > ks[l] || (ks[i] == ks[l] && ki[i] > ki[l])) : ki[i] > ki[l];
+        if (gt == up) {
+          const float fs = ks[i];
+          ks[i] = ks[l];
+          ks[l] = fs;
+          const int fi = ki[i];
+          ki[i] = ki[l];
+          ki[l] = fi;
+        }
+      }
+      cbar();
+    }
+  }
+}
+
+// The sampled step of run_gpt_kv_greedy_metal (runtime/impl/gpt.cpp:2220-2233)
+// in CTA 0: apply_gpt_sampling_processors (:1618-1718) then
+// sample_gpt_token_from_logits (:1720-1755) on the head's logits:
+//  * repetition penalty on each distinct history token (seen bitmap), score
+//    * p when negative else / p; temperature division (float, as the
+//    reference);
+//  * top-k: the exact k-th largest score by a 4-pass radix select over
+//    order-preserving keys; scores below it -> -inf;
+//  * the finite scores are gathered into shared memory and bitonic-sorted by
+//    index; top-p sorts them by (score, index), accumulates the normalised
+//    double probabilities in that order and drops the low tail (cumulative <=
+//    1 - top_p, the largest kept), then sorts back by index;
+//  * the draw: one SplitMix64 unit x the sum of e^(s - max) in index order,
+//    the first index whose running sum exceeds it.
+// The sums run on one thread in the reference's order (exact). Returns the
+// code (-1 on a finite set larger than kGptSampleMaxFinite).
+__device__ int cons_sample(const GptPersistParams& p, const Smem& sm) {
+  const int tid = threadIdx.x;
+  unsigned int* hist = reinterpret_cast<unsigned int*>(sm.xs);  // [256]
+  float* ls = sm.xs + 256;                                       // [2048] scores
+  int* li = reinterpret_cast<int*>(sm.xs + 256 + kGptSampleMaxFinite);  // [2048] indices
+  volatile int* ctl = reinterpret_cast<volatile int*>(sm.xs + 256 + 2 * kGptSampleMaxFinite);  // [4]
+  float s[kSPer];
+  const float pen = p.repetition_penalty, temp = p.temperature;
+#pragma unroll
+  for (int j = 0; j < kSPer; ++j) {
+    const int i = tid + j * kCons;
+    float v = i < kVocab ? __ldcg(p.logits + i) : -INFINITY;
+    if (i < kVocab) {
+      if (pen != 1.0f && ((__ldcg(p.seen + (i >> 5)) >> (i & 31)) & 1u)) v = v < 0.0f ? v * pen : v / pen;
+      if (temp != 1.0f) v = v / temp;
+    }
+    s[j] = v;
+  }
+  // top-k pivot (k-th largest), most significant byte first
+  unsigned int prefix = 0;
+  int remaining = p.top_k;
+  if (p.top_k < kVocab) {
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      if (tid < 256) hist[tid] = 0;
+      cbar();
+#pragma unroll
+      for (int j = 0; j < kSPer; ++j) {
+        const int i = tid + j * kCons;
+        if (i < kVocab) {
+          const unsigned int key = fkey(s[j]);
+          const bool match = shift == 24 || (key >> (shift + 8)) == (prefix >> (shift + 8));
+          if (match) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+      }
+      cbar();
+      if (tid == 0) {
+        int acc = 0, digit = 0;
+        for (int d = 255; d >= 0; --d) {
+          const int c = static_cast<int>(hist[d]);
+          if (acc + c >= remaining) {
+            digit = d;
+            break;
+          }
+          acc += c;
+        }
+        ctl[0] = digit;
+        ctl[1] = remaining - acc;
+      }
+      cbar();
+      prefix |= static_cast<unsigned int>(ctl[0]) << shift;
+      remaining = ctl[1];
+      cbar();
+    }
+    const float pivot = unfkey(prefix);
+#pragma unroll
+    for (int j = 0; j < kSPer; ++j)
+      if (s[j] < pivot) s[j] = -INFINITY;
+  }
+  // gather the finite scores
+  if (tid == 0) ctl[2] = 0;
+  cbar();
+#pragma unroll
+  for (int j = 0; j < kSPer; ++j) {
+    const int i = tid + j * kCons;
+    if (i < kVocab && isfinite(s[j])) {
+      const int pos = atomicAdd(const_cast<int*>(&ctl[2]), 1);
+      if (pos < kGptSampleMaxFinite) {
+        ls[pos] = s[j];
+        li[pos] = i;
+      }
+    }
+  }
+  cbar();
+  const int F = ctl[2];
+  cbar();
+  if (F < 1 || F > kGptSampleMaxFinite) return -1;
+  int n2 = 32;
+  while (n2 < F) n2 <<= 1;
+  for (int t = F + tid; t < n2; t += kCons) {
+    ls[t] = INFINITY;  // pads sort last in both orders
+    li[t] = INT_MAX;
+  }
+  cbar();
+  bitonic_pairs(ls, li, n2, false);
+  if (p.top_p < 1.0f) {
+    if (tid == 0) {
+      float m = -INFINITY;
+      for (int t = 0; t < F; ++t) m = fmaxf(m, ls[t]);
+      double total = 0.0;
+      for (int t = 0; t < F; ++t) total += exp(static_cast<double>(ls[t] - m));
+      reinterpret_cast<volatile double*>(sm.red)[0] = total;
+      reinterpret_cast<volatile float*>(sm.red)[2] = m;
+    }
+    cbar();
+    const double total = reinterpret_cast<volatile double*>(sm.red)[0];
+    const float m = reinterpret_cast<volatile float*>(sm.red)[2];
+    cbar();
+    bitonic_pairs(ls, li, n2, true);
+    if (tid == 0) {
+      const double low_tail = 1.0 - static_cast<double>(p.top_p);
+      double cumulative = 0.0;
+      for (int t = 0; t < F; ++t) {
+        cumulative += exp(static_cast<double>(ls[t] - m)) / total;
+        if (cumulative <= low_tail && t != F - 1) ls[t] = -INFINITY;
+      }
+    }
+    cbar();
+    bitonic_pairs(ls, li, n2, false);
+  }
+  if (tid == 0) {
+    float m = -INFINITY;
+    for (int t = 0; t < F; ++t)
+      if (isfinite(ls[t])) m = fmaxf(m, ls[t]);
+    double total = 0.0;
+    for (int t = 0; t < F; ++t)
+      if (isfinite(ls[t])) total += exp(static_cast<double>(ls[t] - m));
+    unsigned long long st = *p.rng;
+    const double unit = static_cast<double>(splitmix_next(st) >> 11) * (1.0 / 9007199254740992.0);
+    *p.rng = st;
+    const double target = unit * total;
+    double cumulative = 0.0;
+    int pick = -1, last = -1;
+    for (int t = 0; t < F && pick < 0; ++t) {
+      if (!isfinite(ls[t])) continue;
+      const double pr = exp(static_cast<double>(ls[t] - m));
+      if (pr <= 0.0) continue;
+      last = li[t];
+      cumulative += pr;
+      if (target < cumulative) pick = li[t];
+    }
+    ctl[3] = pick >= 0 ? pick : last;
+  }
+  cbar();
+  return ctl[3];
+}
+
 __global__ void __launch_bounds__(kThreads, 1) gpt_persist_kernel(GptPersistParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const Smem sm = smem_of(smem_raw);
@@ -632,6 +829,20 @@ __global__ void __launch_bounds__(kThreads, 1) gpt_persist_kernel(GptPersistPara
     return;
   }
   if (b == 0 && tid == 0) p.times[0] = globaltimer();
+  if (p.sample && b == 0) {  // the repetition history before the first code
+    for (int i = tid; i < (kVocab + 31) / 32; i += kCons) p.seen[i] = 0u;
+    cbar();
+    if (p.n_history == 0) {
+      if (tid == 0) atomicOr(p.seen + (kStart >> 5), 1u << (kStart & 31));
+    } else {
+      for (int i = tid; i < p.n_history; i += kCons) {
+        const uint32_t t = p.history[i];
+        if (t < static_cast<uint32_t>(kVocab)) atomicOr(p.seen + (t >> 5), 1u << (t & 31));
+      }
+    }
+    if (tid == 0) *p.rng = p.seed;
+    cbar();
+  }
   uint32_t it = 0;
   unsigned int bar_k = 0;
   int len = 0, step = 0, code = kStart;
@@ -639,8 +850,9 @@ __global__ void __launch_bounds__(kThreads, 1) gpt_persist_kernel(GptPersistPara
   bool tracing = false, trace_arrivals = false;
   int stage_no = 0;  // stage index within the traced token
   auto sync = [&]() {
-    unsigned long long* arrive =
-        trace_arrivals ? p.trace + kGptTraceCap + static_cast<size_t>(stage_no) * G + b : nullptr;
+    unsigned long long* arrive = trace_arrivals && stage_no < kGptTraceStages
+                                     ? p.trace + kGptTraceCap + static_cast<size_t>(stage_no) * G + b
+                                     : nullptr;
     ++stage_no;
     return grid_sync(p, ++bar_k, sm, arrive);
   };
@@ -750,7 +962,21 @@ __global__ void __launch_bounds__(kThreads, 1) gpt_persist_kernel(GptPersistPara
     ok = ok && sync();
     mark();
     if (!ok) break;
-    if (tid == 0) {  // candidates in CTA order = row order: the first maximum
+    if (p.sample) {  // CTA 0 draws the code; one more barrier publishes it
+      if (b == 0) {
+        const int c = cons_sample(p, sm);
+        if (tid == 0) {
+          if (c < 0) atomicCAS(p.status, 0u, kDevSampleTies);
+          const int cc = c < 0 ? kStop : c;
+          *p.sampled = cc;
+          p.codes[step] = static_cast<uint32_t>(cc);
+          atomicOr(p.seen + (cc >> 5), 1u << (cc & 31));
+        }
+      }
+      ok = sync();
+      if (!ok) break;
+      if (tid == 0) sm.flags[2] = __ldcg(p.sampled);
+    } else if (tid == 0) {  // candidates in CTA order = row order: the first maximum
       float bv = __ldcg(p.cand_val);
       int bi = __ldcg(p.cand_idx);
       for (int c = 1; c < G; ++c) {

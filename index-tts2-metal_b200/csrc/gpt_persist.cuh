@@ -37,7 +37,21 @@ struct GptPersistParams {
   // grid barrier is passed (kGptTraceCap entries); then every CTA's barrier
   // arrival per stage ([121][grid]).
   unsigned long long* trace;
+  // Sampled decode (the reference's GptSamplingConfig with do_sample): when
+  // `sample` is nonzero CTA 0 draws each code after the head stage.
+  int sample;
+  float temperature, top_p, repetition_penalty;
+  int top_k;                 // 1..kGptSampleMaxFinite
+  unsigned long long seed;
+  const uint32_t* history;   // repetition history before the codes (device)
+  int n_history;             // 0: [8192]
+  unsigned int* seen;        // [ceil(8194 / 32)] seen-token bitmap (device scratch)
+  unsigned long long* rng;   // SplitMix64 state (device scratch)
+  int* sampled;              // the drawn code, read by every CTA after a barrier
 };
+
+// Largest finite set the sampler sorts in shared memory (top_k's upper bound).
+constexpr int kGptSampleMaxFinite = 2048;
 
 constexpr int kGptTraceCap = 1 + 121 * 4;
 constexpr int kGptTraceStages = 121;

@@ -39,7 +39,7 @@ EXPORTED = [
     "itts_pipeline_create", "itts_pipeline_destroy", "itts_pipeline_last_error", "itts_pipeline_create_error",
     "itts_pipeline_synthesize",
     "itts_gpt_create", "itts_gpt_destroy", "itts_gpt_last_error", "itts_gpt_create_error", "itts_gpt_generate",
-    "itts_gpt_generate_ex", "itts_gpt_set_tracing", "itts_gpt_stage_trace",
+    "itts_gpt_generate_ex", "itts_gpt_set_tracing", "itts_gpt_stage_trace", "itts_gpt_generate_sampled",
     "itts_gpt_timing", "itts_gpt_launch_kernels", "itts_gpt_weight_bytes_per_token",
 ]
 GPT_WIDTH = 1280
@@ -56,6 +56,12 @@ ITTS_COMPONENT_GPT = 0x8
 ITTS_COMPONENT_ALL = 0xF
 VOCODER_HOP = 256
 VOCODER_MAX_T = 16384
+
+
+class GptSampling(C.Structure):
+    """itts_gpt_sampling: the reference's GptSamplingConfig with do_sample."""
+    _fields_ = [("seed", C.c_uint64), ("temperature", C.c_float), ("top_k", C.c_uint32), ("top_p", C.c_float),
+                ("repetition_penalty", C.c_float)]
 
 
 class IttsError(RuntimeError):
@@ -151,6 +157,8 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_gpt_generate": (i32, [vp, vp, u32, u32, vp, C.POINTER(u32), vp]),
         "itts_gpt_generate_ex": (i32, [vp, vp, u32, u32, u32, vp, C.POINTER(u32), vp]),
         "itts_gpt_set_tracing": (i32, [vp, i32]),
+        "itts_gpt_generate_sampled": (i32, [vp, vp, u32, u32, u32, C.POINTER(GptSampling), vp, u32, vp,
+                                            C.POINTER(u32), vp]),
         "itts_gpt_stage_trace": (i32, [vp, vp, u32]),
         "itts_gpt_timing": (i32, [vp, C.POINTER(f32), C.POINTER(f32)]),
         "itts_gpt_launch_kernels": (i32, [vp]),
@@ -606,6 +614,27 @@ class GptDecoder:
         n = C.c_uint32(0)
         rc = self.lib.itts_gpt_generate_ex(self.h, _ptr(prefix), P, int(steps), GPT_HF_POSITIONS if hf_positions else 0,
                                            _ptr(codes), C.byref(n), _ptr(logits))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_gpt_last_error(self.h).decode())
+        return [int(c) for c in codes[:n.value]], logits
+
+    def generate_sampled(self, prefix, steps: int, sampling: dict, history=None,
+                         hf_positions: bool = False) -> tuple[list[int], np.ndarray]:
+        """Sampled decode (itts_gpt_generate_sampled). sampling: seed,
+        temperature, top_k, top_p, repetition_penalty; history: the
+        repetition history before the codes (default [8192])."""
+        prefix = None if prefix is None or len(prefix) == 0 else _f32(prefix)
+        P = 0 if prefix is None else prefix.shape[0]
+        cfg = GptSampling(int(sampling["seed"]), float(sampling["temperature"]), int(sampling["top_k"]),
+                          float(sampling["top_p"]), float(sampling["repetition_penalty"]))
+        hist = None if history is None else np.ascontiguousarray(history, np.uint32)
+        codes = np.zeros(max(int(steps), 1), np.uint32)
+        logits = np.empty(GPT_VOCAB, np.float32)
+        n = C.c_uint32(0)
+        rc = self.lib.itts_gpt_generate_sampled(self.h, _ptr(prefix), P, int(steps),
+                                                GPT_HF_POSITIONS if hf_positions else 0, C.byref(cfg), _ptr(hist),
+                                                0 if hist is None else hist.size, _ptr(codes), C.byref(n),
+                                                _ptr(logits))
         if rc != ITTS_OK:
             raise IttsError(rc, self.lib.itts_gpt_last_error(self.h).decode())
         return [int(c) for c in codes[:n.value]], logits
