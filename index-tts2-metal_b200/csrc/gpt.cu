@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "bundle.hpp"
+#include "gpt_prefill.cuh"
 #include "launch.cuh"
 #include "ptx.cuh"
 
@@ -569,6 +570,9 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
                o_times = carve(4 * 8), o_trace = carve((2 * static_cast<size_t>(kGptTraceCap) + static_cast<size_t>(kGptTraceStages) * sms_) * 8),
                o_hist = carve(static_cast<size_t>(kMaxLen) * 4), o_seen = carve(((kVocab + 31) / 32) * 4),
                o_rng = carve(8), o_sampled = carve(4);
+  const size_t rows = static_cast<size_t>(kMaxLen);
+  const size_t o_pf_h = carve(rows * kW * 4), o_pf_xn = carve(rows * kW * 4), o_pf_q = carve(rows * kW * 4),
+               o_pf_attn = carve(rows * kW * 4), o_pf_m = carve(rows * kMlp * 4), o_pf_part = carve(4 * rows * kW * 4);
   check(cudaMalloc(&state_, off), "gpt state cudaMalloc");
   check(cudaMemset(state_, 0, off), "gpt state memset");
   uint8_t* s = static_cast<uint8_t*>(state_);
@@ -592,6 +596,15 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
   times_ = reinterpret_cast<unsigned long long*>(s + o_times);
   trace_ = reinterpret_cast<unsigned long long*>(s + o_trace);
   history_ = reinterpret_cast<uint32_t*>(s + o_hist);
+  pf_.x = prefix_;  // the residual stream starts as the prefix rows
+  pf_.h = reinterpret_cast<float*>(s + o_pf_h);
+  pf_.xn = reinterpret_cast<float*>(s + o_pf_xn);
+  pf_.q = reinterpret_cast<float*>(s + o_pf_q);
+  pf_.attn = reinterpret_cast<float*>(s + o_pf_attn);
+  pf_.m = reinterpret_cast<float*>(s + o_pf_m);
+  pf_.part = reinterpret_cast<float*>(s + o_pf_part);
+  pf_.kc = kc_;
+  pf_.vc = vc_;
   seen_ = reinterpret_cast<unsigned int*>(s + o_seen);
   rng_ = reinterpret_cast<unsigned long long*>(s + o_rng);
   sampled_ = reinterpret_cast<int*>(s + o_sampled);
@@ -603,6 +616,9 @@ GptDecoder::GptDecoder(const std::string& bundle_dir, int device, bool verify_sh
   if (persistent_) {
     if (sms_ < gpt_persist_min_grid()) throw std::runtime_error("gpt: too few SMs for the persistent decoder");
     check(gpt_persist_prepare(), "persistent decoder shared memory");
+    check(gpt_prefill_prepare(), "prefill attention shared memory");
+    const char* pm = std::getenv("ITTS_GPT_PREFILL");
+    batched_prefill_ = !(pm && std::string(pm) == "rows");
   }
   build_graphs();
 }
@@ -800,7 +816,15 @@ int GptDecoder::generate_persistent(int P, int max_steps) {
           "trace reset");
   check(cudaMemsetAsync(barrier_, 0, 512, stream_), "grid barrier reset");
   check(cudaMemsetAsync(out_, 0, 16, stream_), "gpt output reset");
+  const bool batched = batched_prefill_ && P > 0;
+  p.len0 = 0;
   check(cudaEventRecord(ev_[0], stream_), "event");
+  if (batched) {  // all prefix rows per layer at once; the decode starts from a cache of P rows
+    check(gpt_prefill_enqueue(L_, pf_, P, stream_), "batched prefill launch");
+    p.P = 0;
+    p.len0 = P;
+  }
+  check(cudaEventRecord(ev_[1], stream_), "event");
   check(gpt_persist_launch(p, sms_, stream_), "persistent decoder launch");
   check(cudaEventRecord(ev_[2], stream_), "event");
   int n = 0;
@@ -810,10 +834,16 @@ int GptDecoder::generate_persistent(int P, int max_steps) {
   check(cudaStreamSynchronize(stream_), "gpt sync");
   float total = 0.0f;
   check(cudaEventElapsedTime(&total, ev_[0], ev_[2]), "event time");
-  const double pre = t[1] >= t[0] ? (t[1] - t[0]) * 1e-6 : 0.0;
-  prefill_ms_ = static_cast<float>(pre);
-  decode_ms_ = total - prefill_ms_;
-  launches_ = 1;
+  if (batched) {
+    check(cudaEventElapsedTime(&prefill_ms_, ev_[0], ev_[1]), "event time");
+    decode_ms_ = total - prefill_ms_;
+    launches_ = 1 + gpt_prefill_kernels_per_call();
+  } else {
+    const double pre = t[1] >= t[0] ? (t[1] - t[0]) * 1e-6 : 0.0;
+    prefill_ms_ = static_cast<float>(pre);
+    decode_ms_ = total - prefill_ms_;
+    launches_ = 1;
+  }
   return n;
 }
 

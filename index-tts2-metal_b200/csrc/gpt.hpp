@@ -28,6 +28,7 @@
 #include <string>
 
 #include "gpt_persist.cuh"
+#include "gpt_prefill.cuh"
 
 namespace itts {
 
@@ -128,6 +129,11 @@ class GptDecoder {
   unsigned int* seen_ = nullptr;      // sampler scratch: seen-token bitmap
   unsigned long long* rng_ = nullptr; // sampler scratch: SplitMix64 state
   int* sampled_ = nullptr;            // sampler scratch: the drawn code
+  // batched prefill (all prefix rows per layer at once) before the persistent
+  // decode; ITTS_GPT_PREFILL=rows in the environment keeps the row-by-row
+  // pass inside the persistent kernel (a diagnostic)
+  bool batched_prefill_ = true;
+  GptPrefillBuffers pf_{};
   bool tracing_ = false;
   unsigned long long* trace_ = nullptr;  // [kGptTraceCap]
   cudaGraphExec_t g_prefill_ = nullptr, g_decode_ = nullptr;

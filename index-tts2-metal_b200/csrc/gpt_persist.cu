@@ -845,7 +845,7 @@ __global__ void __launch_bounds__(kThreads, 1) gpt_persist_kernel(GptPersistPara
   }
   uint32_t it = 0;
   unsigned int bar_k = 0;
-  int len = 0, step = 0, code = kStart;
+  int len = p.len0, step = 0, code = kStart;
   bool ok = true;
   bool tracing = false, trace_arrivals = false;
   int stage_no = 0;  // stage index within the traced token

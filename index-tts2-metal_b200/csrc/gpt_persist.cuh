@@ -30,6 +30,7 @@ struct GptPersistParams {
   unsigned int* status;       // nonzero: a bounded wait gave up
   unsigned long long* times;  // globaltimer at start, end of prefill, end
   int P, max_steps;
+  int len0;          // KV cache rows already filled (a batched prefill), prefix rows P after them
   int hf_positions;  // nonzero: decode step s > 0 takes position embedding s + 1
   // Optional stage trace of the first decode token: CTA 0's global timer when
   // the token starts and, per stage, when its prologue is done, when its first
