@@ -12,6 +12,12 @@
 //   mtts_cfm --inspect-voice-bundle DIR
 //       the bundle contract gates (reference: runtime/main.cpp:2688-2691);
 //       print the JSON report, exit 0 when the contract holds, 1 otherwise.
+//   mtts_cfm --gpt BUNDLE P STEPS PREFIX.f32 OUT.u32 [SEED TEMP TOP_K TOP_P PENALTY] [DEVICE]
+//       GPT mel-code decode of a prefix [P,1280] (raw float32) with
+//       generate-style positions, as the synthesis pipeline calls it
+//       (runtime/impl/tts_synthesis/synthesis_pipeline.cpp:675, 795):
+//       greedy, or sampled when the five sampling values are given; writes
+//       the codes (uint32) to OUT.u32 and prints a JSON report.
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -77,6 +83,49 @@ int run_cfm(int argc, char** argv) {
   return o ? 0 : 1;
 }
 
+int run_gpt(int argc, char** argv) {
+  if (argc < 7) {
+    std::fprintf(stderr, "usage: mtts_cfm --gpt BUNDLE P STEPS PREFIX.f32 OUT.u32 [SEED TEMP TOP_K TOP_P PENALTY] [DEVICE]\n");
+    return 2;
+  }
+  const uint32_t P = static_cast<uint32_t>(std::strtoul(argv[3], nullptr, 10));
+  const uint32_t steps = static_cast<uint32_t>(std::strtoul(argv[4], nullptr, 10));
+  const bool sampled = argc >= 12;
+  const int device = sampled ? (argc > 12 ? std::atoi(argv[12]) : 0) : (argc > 7 ? std::atoi(argv[7]) : 0);
+  const std::vector<float> prefix = read_f32(argv[5], static_cast<size_t>(P) * ITTS_GPT_WIDTH);
+  itts_gpt_ctx* g = nullptr;
+  if (itts_gpt_create(argv[2], device, &g) != ITTS_OK) throw std::runtime_error(itts_gpt_create_error());
+  std::vector<uint32_t> codes(steps > 0 ? steps : 1);
+  std::vector<float> logits(ITTS_GPT_VOCAB);
+  uint32_t n = 0;
+  int rc;
+  if (sampled) {
+    itts_gpt_sampling s{std::strtoull(argv[7], nullptr, 10), std::strtof(argv[8], nullptr),
+                        static_cast<uint32_t>(std::strtoul(argv[9], nullptr, 10)), std::strtof(argv[10], nullptr),
+                        std::strtof(argv[11], nullptr)};
+    rc = itts_gpt_generate_sampled(g, prefix.data(), P, steps, ITTS_GPT_HF_POSITIONS, &s, nullptr, 0, codes.data(), &n,
+                                   logits.data());
+  } else {
+    rc = itts_gpt_generate_ex(g, prefix.data(), P, steps, ITTS_GPT_HF_POSITIONS, codes.data(), &n, logits.data());
+  }
+  if (rc != ITTS_OK) {
+    const std::string msg = itts_gpt_last_error(g);
+    itts_gpt_destroy(g);
+    throw std::runtime_error(msg);
+  }
+  float prefill_ms = 0.0f, decode_ms = 0.0f;
+  itts_gpt_timing(g, &prefill_ms, &decode_ms);
+  itts_gpt_destroy(g);
+  std::ofstream o(argv[6], std::ios::binary);
+  o.write(reinterpret_cast<const char*>(codes.data()), static_cast<std::streamsize>(n * sizeof(uint32_t)));
+  const int first_stop = (n > 0 && codes[n - 1] == ITTS_GPT_STOP) ? static_cast<int>(n - 1) : -1;
+  std::printf("{\n  \"stage\": \"gpt_%s\",\n  \"prefix_tokens\": %u,\n  \"codes\": %u,\n", sampled ? "sampled" : "greedy",
+              P, n);
+  std::printf("  \"first_stop_step\": %d,\n  \"prefill_ms\": %.4f,\n  \"decode_ms_per_token\": %.5f\n}\n", first_stop,
+              prefill_ms, n ? decode_ms / n : 0.0);
+  return o ? 0 : 1;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -87,6 +136,7 @@ int main(int argc, char** argv) {
                        static_cast<uint32_t>(std::strtoul(argv[5], nullptr, 10)), argc > 6 ? std::atoi(argv[6]) : 0);
     }
     if (argc >= 2 && std::strcmp(argv[1], "--cfm") == 0) return run_cfm(argc, argv);
+    if (argc >= 2 && std::strcmp(argv[1], "--gpt") == 0) return run_gpt(argc, argv);
     if (argc >= 3 && (std::strcmp(argv[1], "--inspect-model-bundle") == 0 ||
                       std::strcmp(argv[1], "--inspect-voice-bundle") == 0)) {
       std::string report(1 << 16, '\0');
@@ -108,7 +158,8 @@ int main(int argc, char** argv) {
     std::fprintf(stderr, "usage: mtts_cfm --bench-cfm BUNDLE T STEPS ITERS [DEVICE]\n"
                          "       mtts_cfm --cfm BUNDLE T P STEPS CFG IN_PREFIX OUT.f32 [DEVICE]\n"
                          "       mtts_cfm --inspect-model-bundle DIR [cfm,length_regulator,bigvgan,gpt]\n"
-                         "       mtts_cfm --inspect-voice-bundle DIR\n");
+                         "       mtts_cfm --inspect-voice-bundle DIR\n"
+                         "       mtts_cfm --gpt BUNDLE P STEPS PREFIX.f32 OUT.u32 [SEED TEMP TOP_K TOP_P PENALTY] [DEVICE]\n");
     return 2;
   } catch (const std::exception& e) {
     std::fprintf(stderr, "error: %s\n", e.what());

@@ -45,3 +45,28 @@ def test_cli_rejects_bad_bundle(tmp_path):
     r = subprocess.run([str(CLI), "--bench-cfm", str(tmp_path / "nope"), "8", "1", "1"], capture_output=True, text=True,
                        timeout=120)
     assert r.returncode == 1 and "itts_cfm_create" in r.stderr
+
+
+@pytest.mark.parametrize("sampled", [False, True])
+def test_cli_gpt_matches_capi(gpt_bundle, tmp_path, sampled):
+    """--gpt (generate-style positions, as the synthesis pipeline calls the
+    decoder): the codes the C++ driver writes equal the C ABI's, greedy and
+    sampled."""
+    import itts_cfm
+
+    P, steps = 7, 9
+    prefix = np.random.default_rng(77).standard_normal((P, 1280)).astype(np.float32)
+    pre, out = tmp_path / "prefix.f32", tmp_path / "codes.u32"
+    prefix.tofile(pre)
+    cfg = dict(seed=99, temperature=0.8, top_k=30, top_p=0.8, repetition_penalty=10.0)
+    extra = [str(cfg[k]) for k in ("seed", "temperature", "top_k", "top_p", "repetition_penalty")] if sampled else []
+    r = subprocess.run([str(CLI), "--gpt", str(gpt_bundle), str(P), str(steps), str(pre), str(out)] + extra,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    rep = json.loads(r.stdout)
+    codes = np.fromfile(out, np.uint32).tolist()
+    assert rep["codes"] == len(codes) and rep["stage"] == ("gpt_sampled" if sampled else "gpt_greedy")
+    with itts_cfm.GptDecoder(gpt_bundle, device=0) as d:
+        want = d.generate_sampled(prefix, steps, cfg, hf_positions=True)[0] if sampled else \
+            d.generate(prefix, steps, hf_positions=True)[0]
+    assert codes == want
