@@ -6,7 +6,7 @@
 //   xn = ln_1(x);  [q | K | V] = xn W_attn^T + b  (K, V straight into the cache)
 //   a = causal attention;  h = x + a W_proj^T + b
 //   xn = ln_2(h);  m = gelu_new(xn W_fc^T + b);  x = h + m W_mproj^T + b
-// The projections are tiled fp32 GEMMs (32 x 64 output tiles, 32-deep k
+// The projections are tiled fp32 GEMMs (64 x 64 output tiles, 32-deep k
 // steps with the next step's loads in registers, f16 weights widened in
 // shared memory); the narrow ones split K over 4 CTAs and sum the partials
 // in order in a separate epilogue kernel (deterministic).
@@ -19,7 +19,7 @@ namespace itts {
 namespace {
 
 constexpr int kW = 1280, kQkv = 3840, kMlp = 5120, kLayers = 24, kMaxLen = 4096, kHeads = 20;
-constexpr int kBM = 32, kBN = 64, kBK = 32;
+constexpr int kBM = 64, kBN = 64, kBK = 32;
 constexpr int kSplitNarrow = 4;  // K splits of the 1280-row projections
 
 enum { kEpiStore = 0, kEpiQkv = 1, kEpiGelu = 2, kEpiResid = 3, kEpiPartial = 4 };
@@ -41,7 +41,7 @@ struct RowsGemm {
   int M, N, K, kchunk;
 };
 
-// One 32 x 64 output tile over K range [z * kchunk, (z + 1) * kchunk).
+// One 64 x 64 output tile (4 x 4 per thread) over K range [z * kchunk, (z + 1) * kchunk).
 template <int EPI>
 __global__ void __launch_bounds__(256) rows_gemm_kernel(RowsGemm g) {
   __shared__ __align__(16) float xs[kBK][kBM];
@@ -49,21 +49,29 @@ __global__ void __launch_bounds__(256) rows_gemm_kernel(RowsGemm g) {
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
   const int kb = blockIdx.z * g.kchunk, ke = kb + g.kchunk;
-  // loaders: x tile 32 x 32 (a float4 per thread), w tile 64 x 32 halves (a uint4 per thread)
+  // loaders: x tile 64 x 32 (two float4 per thread: rows xr and xr + 32),
+  // w tile 64 x 32 halves (a uint4 per thread)
   const int xr = tid >> 3, xc = (tid & 7) * 4;
   const int wr = tid >> 2, wc = (tid & 3) * 8;
-  const bool xrow = m0 + xr < g.M;
-  const float* xp = g.x + static_cast<size_t>(xrow ? m0 + xr : 0) * g.K + xc;
+  const bool xrow0 = m0 + xr < g.M, xrow1 = m0 + xr + 32 < g.M;
+  const float* xp0 = g.x + static_cast<size_t>(xrow0 ? m0 + xr : 0) * g.K + xc;
+  const float* xp1 = g.x + static_cast<size_t>(xrow1 ? m0 + xr + 32 : 0) * g.K + xc;
   const __half* wp = g.w + static_cast<size_t>(n0 + wr) * g.K + wc;
-  float4 xa = xrow ? *reinterpret_cast<const float4*>(xp + kb) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 xa = xrow0 ? *reinterpret_cast<const float4*>(xp0 + kb) : z4;
+  float4 xb = xrow1 ? *reinterpret_cast<const float4*>(xp1 + kb) : z4;
   uint4 wa = *reinterpret_cast<const uint4*>(wp + kb);
-  float acc[2][4] = {};
+  float acc[4][4] = {};
   for (int k0 = kb; k0 < ke; k0 += kBK) {
     __syncthreads();
     xs[xc + 0][xr] = xa.x;
     xs[xc + 1][xr] = xa.y;
     xs[xc + 2][xr] = xa.z;
     xs[xc + 3][xr] = xa.w;
+    xs[xc + 0][xr + 32] = xb.x;
+    xs[xc + 1][xr + 32] = xb.y;
+    xs[xc + 2][xr + 32] = xb.z;
+    xs[xc + 3][xr + 32] = xb.w;
     {
       const __half2* h2 = reinterpret_cast<const __half2*>(&wa);
 #pragma unroll
@@ -75,26 +83,24 @@ __global__ void __launch_bounds__(256) rows_gemm_kernel(RowsGemm g) {
     }
     __syncthreads();
     if (k0 + kBK < ke) {  // the next k step's loads overlap this step's FMAs
-      xa = xrow ? *reinterpret_cast<const float4*>(xp + k0 + kBK) : make_float4(0.f, 0.f, 0.f, 0.f);
+      xa = xrow0 ? *reinterpret_cast<const float4*>(xp0 + k0 + kBK) : z4;
+      xb = xrow1 ? *reinterpret_cast<const float4*>(xp1 + k0 + kBK) : z4;
       wa = *reinterpret_cast<const uint4*>(wp + k0 + kBK);
     }
 #pragma unroll
     for (int kk = 0; kk < kBK; ++kk) {
-      const float2 a = *reinterpret_cast<const float2*>(&xs[kk][ty * 2]);
+      const float4 a = *reinterpret_cast<const float4*>(&xs[kk][ty * 4]);
       const float4 b = *reinterpret_cast<const float4*>(&ws[kk][tx * 4]);
-      acc[0][0] = fmaf(a.x, b.x, acc[0][0]);
-      acc[0][1] = fmaf(a.x, b.y, acc[0][1]);
-      acc[0][2] = fmaf(a.x, b.z, acc[0][2]);
-      acc[0][3] = fmaf(a.x, b.w, acc[0][3]);
-      acc[1][0] = fmaf(a.y, b.x, acc[1][0]);
-      acc[1][1] = fmaf(a.y, b.y, acc[1][1]);
-      acc[1][2] = fmaf(a.y, b.z, acc[1][2]);
-      acc[1][3] = fmaf(a.y, b.w, acc[1][3]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
   }
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int m = m0 + ty * 2 + i;
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
     if (m >= g.M) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
