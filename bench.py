@@ -426,7 +426,9 @@ def gpt_line(args, rank, world, local, barrier, max_over_ranks, hbm_peak):
             "value": n * world / (dec_ms / 1e3), "unit": "tokens/s", "prefix_rows": P_rows, "steps": n,
             "ms_per_token": dec_ms / n, "prefill_ms": pre_ms, "prefill_ms_per_row": pre_ms / max(P_rows, 1),
             "gpu_launches": launches,
-            "path": "graphs per token" if os.environ.get("ITTS_GPT_MODE") == "graph" else "one persistent kernel per call",
+            "path": ("graphs per token" if os.environ.get("ITTS_GPT_MODE") == "graph" else
+                     "one persistent decode kernel per call" + ("" if os.environ.get("ITTS_GPT_PREFILL") == "rows"
+                                                                else ", after the batched prefill kernels")),
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                          "bytes_per_token": wb + kv, "note": "f16 weights once per token + mean fp32 KV-cache reads"},
             "e2e": {"value": n * world / t_e2e, "unit": "tokens/s (prefill included)",
