@@ -206,7 +206,7 @@ int itts_op_adarms(itts_cfm_ctx* ctx, const float* x, uint32_t R, const float* w
  * allocating library routine. No counterpart in the reference.
  *
  * x: [S*T, 512] f16 UNPADDED rows (16-byte aligned); w, bias, out as for
- * itts_op_conv5. The reflect-padded staging copy the conv reads lives in one
+ * itts_op_conv5, with N a multiple of 128 (other N: ITTS_EINVAL_SHAPE). The reflect-padded staging copy the conv reads lives in one
  * static device array of ITTS_NOALLOC_CONV5_MAX_ROWS x 512 f16 (16 MiB) per
  * GPU, held from the first call on that GPU until the process exits;
  * S*(T+4) above that limit returns ITTS_ECAP. Runs on the calling thread's
@@ -350,6 +350,26 @@ const char* itts_pipeline_create_error(void);
 int itts_pipeline_synthesize(itts_pipeline* p, const char* voice_bundle_dir, uint32_t prompt_tokens,
                              const float* s_infer, uint32_t n_in, uint32_t G, const float* noise, uint32_t steps,
                              float cfg_rate, float* wave, float* full_mel);
+
+/* As itts_pipeline_synthesize, with the sampler's initial noise drawn the
+ * way the reference's synthesis pipeline draws it:
+ * itts_make_noise(P + G, 80, seed, temperature) (synthesis_pipeline.cpp:1333,
+ * make_deterministic_normal_noise(tokens, mel_dim, seed, temperature)). */
+int itts_pipeline_synthesize_seeded(itts_pipeline* p, const char* voice_bundle_dir, uint32_t prompt_tokens,
+                                    const float* s_infer, uint32_t n_in, uint32_t G, uint64_t seed, float temperature,
+                                    uint32_t steps, float cfg_rate, float* wave, float* full_mel);
+
+/* ------------------------------------------------------------------------
+ * Seeded noise. itts_make_noise writes tokens x channels normals (row-major)
+ * scaled by temperature, bit-identical to the reference's
+ * make_deterministic_normal_noise(tokens, channels, seed, temperature)
+ * (runtime/impl/tokenizer_tests.cpp:2102-2140): SplitMix64 uniforms in (0, 1),
+ * Box-Muller pairs (cos then sin) in single precision. Host code; no context
+ * or GPU needed. tokens in [1, ITTS_MAX_T], channels in
+ * [1, ITTS_NOISE_MAX_CHANNELS]; out holds tokens * channels floats.
+ * ------------------------------------------------------------------------ */
+#define ITTS_NOISE_MAX_CHANNELS 4096u
+int itts_make_noise(uint32_t tokens, uint32_t channels, uint64_t seed, float temperature, float* out);
 
 /* ------------------------------------------------------------------------
  * GPT mel-code decoder: cached greedy decode of mel codes (24 GPT-2 blocks,

@@ -469,15 +469,10 @@ bool make_attn_tmap(CUtensorMap* tm, const __half* qkv, int R) {
 cudaError_t attention_tc_run(const CUtensorMap& tm, const float* row_mask, __half* out, int S, int T,
                              unsigned int* status, cudaStream_t st) {
   if (S <= 0 || T <= 0) return cudaErrorInvalidValue;
-  static std::atomic<uint32_t> configured{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint32_t bit = 1u << (dev & 31);
-  if ((configured.load() & bit) == 0) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_A);
-    if (e != cudaSuccess) return e;
-    configured.fetch_or(bit);
-  }
+  static PerDeviceOnce configured;
+  const cudaError_t e = configured.run(
+      [] { return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_A); });
+  if (e != cudaSuccess) return e;
   dim3 grid((T + kQ - 1) / kQ, 8, S);
   return launch_pdl(attn_tc_kernel, grid, dim3(kThreadsA), SMEM_A, st, tm, row_mask, out, T, status);
 }

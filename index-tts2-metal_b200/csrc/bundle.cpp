@@ -322,12 +322,54 @@ uint16_t float_to_half_bits(float f) {
   return static_cast<uint16_t>(sign | r);
 }
 
+void Mit2Bundle::map_file(const std::string& path) {
+  fd_ = ::open(path.c_str(), O_RDONLY);
+  if (fd_ < 0) throw std::runtime_error("bundle: missing weights file " + path);
+  struct stat st {};
+  if (fstat(fd_, &st) != 0) throw std::runtime_error("bundle: cannot stat " + path);
+  size_ = static_cast<size_t>(st.st_size);
+  if (size_ < 12) throw std::runtime_error("bundle: weights file too small for the MIT2 header");
+  void* p = mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd_, 0);
+  if (p == MAP_FAILED) throw std::runtime_error("bundle: mmap failed for " + path);
+  base_ = static_cast<const uint8_t*>(p);
+}
+
+bool bundle_is_single_file(const std::string& path) {
+  struct stat st {};
+  return ::stat(path.c_str(), &st) == 0 && S_ISREG(st.st_mode);
+}
+
 Mit2Bundle::Mit2Bundle(const std::string& dir, bool verify_sha256) : dir_(dir) {
-  std::ifstream mf(dir + "/manifest.json");
-  if (!mf) throw std::runtime_error("bundle: cannot open " + dir + "/manifest.json");
-  std::stringstream ss;
-  ss << mf.rdbuf();
-  const std::string text = ss.str();
+  // Two forms (the reference's Bundle constructor, runtime/bundle.cpp:172-213):
+  // a directory holding manifest.json + the weights file, or ONE file that is a
+  // valid MIT2 weights stream with the manifest JSON appended after the
+  // payloads and a 24-byte footer [u64 manifest offset][u64 manifest size]
+  // ["MIT2VOIC"] (little endian) at its very end.
+  const bool single_file = bundle_is_single_file(dir);
+  std::string text;
+  if (single_file) {
+    map_file(dir);
+    constexpr size_t kFooter = 24;
+    if (size_ < 12 + kFooter) throw std::runtime_error("bundle: single-file bundle is too small: " + dir);
+    const uint8_t* foot = base_ + size_ - kFooter;
+    if (std::memcmp(foot + 16, "MIT2VOIC", 8) != 0)
+      throw std::runtime_error("bundle: single-file bundle footer magic missing: " + dir);
+    uint64_t moff = 0, msize = 0;
+    for (int b = 7; b >= 0; --b) {
+      moff = (moff << 8) | foot[b];
+      msize = (msize << 8) | foot[8 + b];
+    }
+    const uint64_t limit = size_ - kFooter;
+    if (moff > limit || msize > limit - moff)
+      throw std::runtime_error("bundle: single-file bundle manifest exceeds the file: " + dir);
+    text.assign(reinterpret_cast<const char*>(base_ + moff), static_cast<size_t>(msize));
+  } else {
+    std::ifstream mf(dir + "/manifest.json");
+    if (!mf) throw std::runtime_error("bundle: cannot open " + dir + "/manifest.json");
+    std::stringstream ss;
+    ss << mf.rdbuf();
+    text = ss.str();
+  }
   JVal root = JParser(text).parse();
   if (root.kind != JVal::Obj) throw std::runtime_error("manifest: root must be an object");
   const std::string format = as_str(root.get("format"), "format");
@@ -341,19 +383,11 @@ Mit2Bundle::Mit2Bundle(const std::string& dir, bool verify_sha256) : dir_(dir) {
   if (alignment == 0) throw std::runtime_error("bundle: alignment must be non-zero");
   version_ = static_cast<uint32_t>(version);
   alignment_ = alignment;
-  std::string wname = "weights.bin";
-  if (const JVal* wf = root.get("weights_file")) wname = as_str(wf, "weights_file");
-
-  const std::string wpath = dir + "/" + wname;
-  fd_ = ::open(wpath.c_str(), O_RDONLY);
-  if (fd_ < 0) throw std::runtime_error("bundle: missing weights file " + wpath);
-  struct stat st {};
-  if (fstat(fd_, &st) != 0) throw std::runtime_error("bundle: cannot stat " + wpath);
-  size_ = static_cast<size_t>(st.st_size);
-  if (size_ < 12) throw std::runtime_error("bundle: weights file too small for the MIT2 header");
-  void* p = mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd_, 0);
-  if (p == MAP_FAILED) throw std::runtime_error("bundle: mmap failed for " + wpath);
-  base_ = static_cast<const uint8_t*>(p);
+  if (!single_file) {
+    std::string wname = "weights.bin";
+    if (const JVal* wf = root.get("weights_file")) wname = as_str(wf, "weights_file");
+    map_file(dir + "/" + wname);
+  }
   if (std::memcmp(base_, "MIT2", 4) != 0) throw std::runtime_error("bundle: weights file has an invalid MIT2 magic");
   if (rd_u32(base_ + 4) != version) throw std::runtime_error("bundle: weights header version mismatch");
   if (rd_u32(base_ + 8) != alignment) throw std::runtime_error("bundle: weights header alignment mismatch");

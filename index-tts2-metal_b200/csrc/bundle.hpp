@@ -24,11 +24,17 @@ struct TensorRec {
   std::string component;  // manifest "component" (gpt, semantic_codec, s2mel, bigvgan, voice, ...), may be empty
 };
 
+// True when `path` names a regular file: a single-file bundle (the reference's
+// bundle_path_is_single_file, runtime/bundle.cpp:163).
+bool bundle_is_single_file(const std::string& path);
+
 class Mit2Bundle {
  public:
-  // Opens and validates a bundle directory; throws std::runtime_error with a
-  // message naming the violated rule. With verify_sha256, every payload's
-  // SHA-256 is checked against the manifest.
+  // Opens and validates a bundle: a directory (manifest.json + weights file)
+  // or a single file (weights stream + appended manifest + "MIT2VOIC"
+  // footer); throws std::runtime_error with a message naming the violated
+  // rule. With verify_sha256, every payload's SHA-256 is checked against the
+  // manifest.
   explicit Mit2Bundle(const std::string& dir, bool verify_sha256 = false);
   ~Mit2Bundle();
   Mit2Bundle(const Mit2Bundle&) = delete;
@@ -48,6 +54,7 @@ class Mit2Bundle {
   size_t weights_bytes() const { return size_; }
 
  private:
+  void map_file(const std::string& path);  // maps `path` read-only into base_ / size_
   std::string dir_;
   int fd_ = -1;
   const uint8_t* base_ = nullptr;

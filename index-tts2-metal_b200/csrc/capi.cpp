@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -420,10 +421,13 @@ int itts_op_gemm(itts_cfm_ctx* ctx, const void* a0, uint32_t lda0, const void* a
 int itts_op_conv5(itts_cfm_ctx* ctx, const void* xp, uint32_t S, uint32_t T, const void* w, const float* bias,
                   float* out, uint32_t N) {
   return guarded(ctx, [&] {
-    need(xp && w && out && S > 0 && T >= ITTS_MIN_T && N > 0 && N % 16 == 0, "bad conv arguments");
+    need(xp && w && out && S > 0 && T >= ITTS_MIN_T && T <= ITTS_MAX_T && N > 0 && N % 16 == 0,
+         "bad conv arguments");
+    const uint64_t rows = static_cast<uint64_t>(S) * (static_cast<uint64_t>(T) + 4);
+    need(rows <= static_cast<uint64_t>(INT32_MAX), "conv too large: S*(T+4) padded rows must fit in 31 bits");
     itts::GemmLaunch g;
     std::memset(&g, 0, sizeof(g));
-    const uint32_t Rp = S * (T + 4);
+    const uint32_t Rp = static_cast<uint32_t>(rows);
     // Tile shape and form as the engine picks them for its WaveNet convs.
     const itts::GemmPick pk = itts::gemm_pick(static_cast<int>(Rp), static_cast<int>(N), false);
     const uint32_t kbox = static_cast<uint32_t>(itts::gemm_kbox(pk.bn));

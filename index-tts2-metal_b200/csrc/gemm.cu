@@ -867,15 +867,10 @@ cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
   auto kern = gemm_tc_kernel<BN, STAGES, EPI, PAIR>;
   const size_t smem = gemm_smem_bytes(BN, STAGES, PAIR);
   // The shared-memory opt-in is set once per device for each instantiation.
-  static std::atomic<uint32_t> configured{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint32_t bit = 1u << (dev & 31);
-  if ((configured.load() & bit) == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    configured.fetch_or(bit);
-  }
+  static PerDeviceOnce configured;
+  cudaError_t e = configured.run(
+      [&] { return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); });
+  if (e != cudaSuccess) return e;
   const int unit_m = PAIR ? 2 * kBM : kBM;
   const int units = ((g.args.M + unit_m - 1) / unit_m) * ((g.args.N + BN - 1) / BN);
   if constexpr (PAIR) {

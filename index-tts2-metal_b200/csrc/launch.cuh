@@ -7,6 +7,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <utility>
 
@@ -19,6 +20,28 @@ inline bool pdl_enabled() {
   }();
   return on;
 }
+
+// Runs a set-up call (e.g. a kernel's shared-memory opt-in) once per device
+// ordinal: keep one instance per kernel as a function-local static. Ordinals
+// beyond the table (never seen on one node) simply repeat the call.
+class PerDeviceOnce {
+ public:
+  template <typename F>
+  cudaError_t run(F&& setup) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const bool tracked = dev >= 0 && dev < kMaxOrdinals;
+    if (tracked && done_[dev].load(std::memory_order_acquire)) return cudaSuccess;
+    e = setup();
+    if (e == cudaSuccess && tracked) done_[dev].store(true, std::memory_order_release);
+    return e;
+  }
+
+ private:
+  static constexpr int kMaxOrdinals = 1024;
+  std::atomic<bool> done_[kMaxOrdinals] = {};
+};
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {

@@ -83,8 +83,10 @@ void put_err(char* err, uint32_t cap, const char* msg) {
 extern "C" int itts_op_conv5_noalloc(const void* x, uint32_t S, uint32_t T, const void* w, const float* bias,
                                      float* out, uint32_t N, void* stream, char* err, uint32_t err_cap) {
   put_err(err, err_cap, "");
-  if (!x || !w || !out || S == 0 || N == 0 || N % 16 != 0 || T < ITTS_MIN_T) {
-    put_err(err, err_cap, "bad conv arguments (x, w, out non-null; S > 0; T >= 2; N a positive multiple of 16)");
+  // N is tiled by 128-column weight boxes with no partial tile (the WaveNet
+  // conv this serves has N = 1024).
+  if (!x || !w || !out || S == 0 || N == 0 || N % 128 != 0 || T < ITTS_MIN_T) {
+    put_err(err, err_cap, "bad conv arguments (x, w, out non-null; S > 0; T >= 2; N a positive multiple of 128)");
     return ITTS_EINVAL_SHAPE;
   }
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) {

@@ -112,4 +112,36 @@ int itts_pipeline_synthesize(itts_pipeline* p, const char* voice_bundle_dir, uin
   }
 }
 
+int itts_pipeline_synthesize_seeded(itts_pipeline* p, const char* voice_bundle_dir, uint32_t prompt_tokens,
+                                    const float* s_infer, uint32_t n_in, uint32_t G, uint64_t seed, float temperature,
+                                    uint32_t steps, float cfg_rate, float* wave, float* full_mel) {
+  if (!p) return ITTS_EINVAL_SHAPE;
+  p->err.clear();
+  if (!voice_bundle_dir || G == 0) {
+    p->err = "null voice bundle or G == 0";
+    return ITTS_EINVAL_SHAPE;
+  }
+  uint32_t P = 0;
+  char verr[512];
+  int rc = itts_voice_load(voice_bundle_dir, prompt_tokens, &P, nullptr, nullptr, nullptr, verr, sizeof(verr));
+  if (rc != ITTS_OK) {
+    p->err = std::string("voice: ") + verr;
+    return rc;
+  }
+  if (static_cast<uint64_t>(P) + G > ITTS_MAX_T) {
+    p->err = "P + G exceeds ITTS_MAX_T";
+    return ITTS_EINVAL_SHAPE;
+  }
+  // x0 over all P + G rows, as the reference's pipeline draws it; the
+  // sampler zeroes the prompt rows itself.
+  std::vector<float> noise(static_cast<size_t>(P + G) * 80);
+  rc = itts_make_noise(P + G, 80, seed, temperature, noise.data());
+  if (rc != ITTS_OK) {
+    p->err = "noise: bad shape";
+    return rc;
+  }
+  return itts_pipeline_synthesize(p, voice_bundle_dir, prompt_tokens, s_infer, n_in, G, noise.data(), steps, cfg_rate,
+                                  wave, full_mel);
+}
+
 }  // extern "C"

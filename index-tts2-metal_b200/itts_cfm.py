@@ -37,7 +37,7 @@ EXPORTED = [
     "itts_cond_stage", "itts_cond_launch", "itts_cond_fetch", "itts_cond_stream", "itts_cond_launch_kernels",
     "itts_cond_flops", "itts_inspect_voice_bundle", "itts_inspect_model_bundle", "itts_voice_load",
     "itts_pipeline_create", "itts_pipeline_destroy", "itts_pipeline_last_error", "itts_pipeline_create_error",
-    "itts_pipeline_synthesize",
+    "itts_pipeline_synthesize", "itts_pipeline_synthesize_seeded", "itts_make_noise",
     "itts_gpt_create", "itts_gpt_destroy", "itts_gpt_last_error", "itts_gpt_create_error", "itts_gpt_generate",
     "itts_gpt_generate_ex", "itts_gpt_set_tracing", "itts_gpt_stage_trace", "itts_gpt_generate_sampled",
     "itts_gpt_timing", "itts_gpt_launch_kernels", "itts_gpt_weight_bytes_per_token",
@@ -56,6 +56,7 @@ ITTS_COMPONENT_GPT = 0x8
 ITTS_COMPONENT_ALL = 0xF
 VOCODER_HOP = 256
 VOCODER_MAX_T = 16384
+NOISE_MAX_CHANNELS = 4096
 
 
 class GptSampling(C.Structure):
@@ -150,6 +151,9 @@ def load(path: str | Path | None = None) -> C.CDLL:
         "itts_pipeline_last_error": (C.c_char_p, [vp]),
         "itts_pipeline_create_error": (C.c_char_p, []),
         "itts_pipeline_synthesize": (i32, [vp, C.c_char_p, u32, vp, u32, u32, vp, u32, f32, vp, vp]),
+        "itts_pipeline_synthesize_seeded": (i32, [vp, C.c_char_p, u32, vp, u32, u32, C.c_uint64, f32, u32, f32, vp,
+                                                  vp]),
+        "itts_make_noise": (i32, [u32, u32, C.c_uint64, f32, vp]),
         "itts_gpt_create": (i32, [C.c_char_p, i32, C.POINTER(vp)]),
         "itts_gpt_destroy": (None, [vp]),
         "itts_gpt_last_error": (C.c_char_p, [vp]),
@@ -570,6 +574,32 @@ class Pipeline:
         if rc != ITTS_OK:
             raise IttsError(rc, self.lib.itts_pipeline_last_error(self.h).decode())
         return wave, mel
+
+    def synthesize_seeded(self, voice_bundle: str | Path, s_infer, G: int, seed: int, temperature: float, steps: int,
+                          cfg: float, prompt_tokens: int = 0) -> tuple[np.ndarray, np.ndarray]:
+        """As synthesize, with x0 = make_noise(P + G, 80, seed, temperature)
+        (the reference pipeline's draw)."""
+        s_infer = _f32(s_infer)
+        P = voice_load(voice_bundle, prompt_tokens)["P"]
+        wave = np.empty(int(G) * VOCODER_HOP, np.float32)
+        mel = np.empty((P + int(G), 80), np.float32)
+        rc = self.lib.itts_pipeline_synthesize_seeded(self.h, str(voice_bundle).encode(), int(prompt_tokens),
+                                                      _ptr(s_infer), s_infer.shape[0], int(G), int(seed),
+                                                      float(temperature), int(steps), float(cfg), _ptr(wave),
+                                                      _ptr(mel))
+        if rc != ITTS_OK:
+            raise IttsError(rc, self.lib.itts_pipeline_last_error(self.h).decode())
+        return wave, mel
+
+
+def make_noise(tokens: int, channels: int, seed: int, temperature: float = 1.0) -> np.ndarray:
+    """itts_make_noise: [tokens, channels] seeded normals, bit-identical to the
+    reference's make_deterministic_normal_noise (host code, no GPU)."""
+    out = np.empty((int(tokens), int(channels)), np.float32)
+    rc = load().itts_make_noise(int(tokens), int(channels), int(seed) & (2**64 - 1), float(temperature), _ptr(out))
+    if rc != ITTS_OK:
+        raise IttsError(rc, f"noise shape out of range: {tokens} x {channels}")
+    return out
 
 
 class GptDecoder:

@@ -12,7 +12,8 @@ reference's names (prefix ``s2mel.net.cfm.estimator.``), from a seeded
 
 * ``init="baseline"`` — the benchmark configuration: f16 weights ~ N(0, 0.02),
   RMSNorm gammas 1, timestep frequencies exp(-ln(10000) i / 128), weight-norm
-  pairs with g = ||v_row|| (so the folded weight equals v).
+  pairs with g = ||v_row|| * U(0.5, 1.5) (a per-row gain, so the folded
+  weight differs from v and the fold is visible in every output).
 * ``init="unit"`` — same tensors with fan-in scaled weights (std 1/sqrt(K))
   and AdaRMS project_layer biases of 1 on the scale half, so every block
   contributes O(1) to the output; used by parity tests so no sub-path hides
@@ -101,13 +102,54 @@ def write_bundle(out_dir: str | Path, tensors: Iterable[tuple[str, np.ndarray]],
     return manifest
 
 
+SINGLE_FILE_FOOTER_MAGIC = b"MIT2VOIC"
+
+
+def write_single_file_bundle(path: str | Path, tensors: Iterable[tuple[str, np.ndarray]],
+                             metadata: dict | None = None) -> dict:
+    """Write the single-file form of an MIT2 bundle (the reference reads it
+    wherever it takes a bundle path, runtime/bundle.cpp:153-200): the weights
+    stream, then the manifest JSON, then a 24-byte footer
+    [u64 manifest offset][u64 manifest size][b"MIT2VOIC"], little endian."""
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    tmp = path.parent / (path.name + ".dir")
+    man = write_bundle(tmp, tensors, metadata)
+    body = (tmp / "weights.bin").read_bytes()
+    man = dict(man)
+    man.pop("weights_file", None)
+    text = json.dumps(man, indent=2, sort_keys=True).encode("utf-8")
+    with path.open("wb") as fp:
+        fp.write(body)
+        fp.write(text)
+        fp.write(struct.pack("<QQ8s", len(body), len(text), SINGLE_FILE_FOOTER_MAGIC))
+    for f in tmp.iterdir():
+        f.unlink()
+    tmp.rmdir()
+    return man
+
+
+def _single_file_manifest(path: Path) -> dict:
+    raw = path.read_bytes()
+    off, size, magic = struct.unpack("<QQ8s", raw[-24:])
+    if magic != SINGLE_FILE_FOOTER_MAGIC:
+        raise ValueError(f"single-file bundle footer magic missing: {path}")
+    return json.loads(raw[off : off + size].decode("utf-8"))
+
+
 def read_bundle(bundle_dir: str | Path, names: Iterable[str] | None = None, verify: bool = False) -> dict[str, np.ndarray]:
-    """Read tensors (all, or ``names``) as numpy arrays in their stored dtype."""
+    """Read tensors (all, or ``names``) as numpy arrays in their stored dtype,
+    from a bundle directory or a single-file bundle."""
     d = Path(bundle_dir)
-    man = json.loads((d / "manifest.json").read_text(encoding="utf-8"))
+    if d.is_file():
+        man = _single_file_manifest(d)
+        weights = d
+    else:
+        man = json.loads((d / "manifest.json").read_text(encoding="utf-8"))
+        weights = d / man.get("weights_file", "weights.bin")
     want = set(names) if names is not None else None
     out = {}
-    raw = np.memmap(d / man.get("weights_file", "weights.bin"), dtype=np.uint8, mode="r")
+    raw = np.memmap(weights, dtype=np.uint8, mode="r")
     for rec in man["tensors"]:
         if want is not None and rec["name"] not in want:
             continue
@@ -198,7 +240,11 @@ def make_dit_tensors(seed: int, init: str = "baseline") -> list[tuple[str, np.nd
     out: list[tuple[str, np.ndarray]] = []
     pending_v: dict[str, np.ndarray] = {}
     specs = dit_tensor_specs()
-    # Draw weight_v before weight_g so g can be set to ||v_row||.
+    # Draw weight_v before weight_g: g is ||v_row|| times a per-row gain drawn
+    # from U(0.5, 1.5) (its own generator, so the other tensors do not move),
+    # so the folded W = g * v / ||v_row|| differs from v and a wrong gain, norm
+    # or norm axis in the fold changes the estimator's output.
+    gain_rng = np.random.default_rng(seed + 7919)
     for name, shape, kind in specs:
         if kind == "wv":
             fan_in = int(np.prod(shape[1:]))
@@ -229,7 +275,8 @@ def make_dit_tensors(seed: int, init: str = "baseline") -> list[tuple[str, np.nd
         elif kind == "wg":
             v = pending_v[name[: -len("weight_g")] + "weight_v"].astype(np.float32)
             norms = np.sqrt((v.reshape(v.shape[0], -1) ** 2).sum(axis=1))
-            arr = norms.reshape(shape).astype(np.float16)
+            gains = gain_rng.uniform(0.5, 1.5, size=norms.shape).astype(np.float32)
+            arr = (norms * gains).reshape(shape).astype(np.float16)
         else:
             raise AssertionError(kind)
         out.append((full, arr))
@@ -240,7 +287,7 @@ def make_dit_bundle(out_dir: str | Path, seed: int = 0, init: str = "baseline") 
     """Write the synthetic estimator bundle; skips work when an identical one exists."""
     out = Path(out_dir)
     stamp = out / ".synthetic"
-    key = f"seed={seed} init={init} v1"
+    key = f"seed={seed} init={init} v2"
     if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():
         return out
     write_bundle(out, make_dit_tensors(seed, init), metadata={"synthetic": True, "seed": seed, "init": init})
@@ -412,9 +459,14 @@ def make_voice_tensors(seed: int, prompt_tokens: int = 200, spk_tokens: int = 17
             ("mel", rng.standard_normal((1, 80, prompt_tokens), dtype=np.float32))]
 
 
-def make_voice_bundle(out_dir: str | Path, seed: int = 0, prompt_tokens: int = 200) -> Path:
-    """Write a synthetic voice bundle; skips work when an identical one exists."""
+def make_voice_bundle(out_dir: str | Path, seed: int = 0, prompt_tokens: int = 200, single_file: bool = False) -> Path:
+    """Write a synthetic voice bundle (a directory, or with single_file the
+    one-file form at out_dir); skips work when an identical directory exists."""
     out = Path(out_dir)
+    if single_file:
+        write_single_file_bundle(out, make_voice_tensors(seed, prompt_tokens),
+                                 metadata={"synthetic": True, "seed": seed, "model": "voice"})
+        return out
     stamp = out / ".synthetic"
     key = f"voice seed={seed} P={prompt_tokens} v1"
     if stamp.exists() and stamp.read_text() == key and (out / "weights.bin").exists():

@@ -126,3 +126,58 @@ def test_cli_gates(voice, unit_bundle, tmp_path):
     r = subprocess.run([str(cli), "--inspect-model-bundle", str(unit_bundle), "bigvgan"], capture_output=True,
                        text=True, timeout=120)
     assert r.returncode == 1 and json.loads(r.stdout)["ok"] is False
+
+
+def test_single_file_voice_bundle_equals_directory_form(tmp_path):
+    """The one-file bundle form (weights stream + manifest + "MIT2VOIC" footer,
+    the reference's runtime/bundle.cpp:153-200) passes the same gate with the
+    same report and loads the same voice as the directory form."""
+    d = mit2.make_voice_bundle(tmp_path / "voice_dir", seed=5, prompt_tokens=23)
+    f = mit2.make_voice_bundle(tmp_path / "voice.mit2", seed=5, prompt_tokens=23, single_file=True)
+    assert f.is_file()
+    rc_d, rep_d = itts_cfm.inspect_voice_bundle(d)
+    rc_f, rep_f = itts_cfm.inspect_voice_bundle(f)
+    assert rc_d == rc_f == itts_cfm.ITTS_OK and rep_f["ok"] is True
+    for k in ("prompt_tokens", "mel_frames", "spk_cond_tokens"):
+        assert rep_f[k] == rep_d[k]
+    vd, vf = itts_cfm.voice_load(d, 11), itts_cfm.voice_load(f, 11)
+    for k in ("prompt_cond", "style", "prompt_mel"):
+        assert np.array_equal(vd[k], vf[k])
+    got = mit2.read_bundle(f, verify=True)
+    want = mit2.read_bundle(d, verify=True)
+    assert got.keys() == want.keys() and all(np.array_equal(got[k], want[k]) for k in got)
+
+
+def _single_file_voice(tmp_path):
+    return mit2.make_voice_bundle(tmp_path / "v.mit2", seed=6, prompt_tokens=9, single_file=True)
+
+
+@pytest.mark.parametrize("damage,msg", [
+    ("truncate", "footer magic"),
+    ("manifest_past_end", "manifest exceeds"),
+    ("tiny", "too small"),
+    ("payload_flip", "sha256"),
+])
+def test_single_file_bundle_rejections(tmp_path, damage, msg):
+    f = _single_file_voice(tmp_path)
+    raw = bytearray(f.read_bytes())
+    if damage == "truncate":
+        raw = raw[:-5]
+    elif damage == "manifest_past_end":
+        off = int.from_bytes(raw[-24:-16], "little")
+        raw[-16:-8] = (len(raw) - off).to_bytes(8, "little")
+    elif damage == "tiny":
+        raw = raw[:20]
+    else:
+        raw[4096 + 3] ^= 0x40  # inside the first payload (offsets are 4096-aligned)
+    f.write_bytes(bytes(raw))
+    rc, rep = itts_cfm.inspect_voice_bundle(f)
+    assert rc == itts_cfm.ITTS_EBUNDLE and rep["ok"] is False
+    assert msg in rep["error"].lower() or msg in json.dumps(rep).lower(), rep
+
+
+def test_single_file_model_bundle_gate(tmp_path):
+    f = tmp_path / "cfm.mit2"
+    mit2.write_single_file_bundle(f, mit2.make_dit_tensors(0, "unit"))
+    rc, rep = itts_cfm.inspect_model_bundle(f, itts_cfm.ITTS_COMPONENT_CFM)
+    assert rc == itts_cfm.ITTS_OK and rep["ok"] is True, rep

@@ -168,3 +168,20 @@ def test_full_size_config2_single_step(ctx_baseline, port_baseline):
     vel = ctx_baseline.estimator(x[None], px[None], u.cond[None], u.style[None], mask, t=0.0, branches=2)
     ref_c = port_baseline.estimator(x, px, u.cond, u.style, 0.0, mask[0])
     _vel_ok(ref_c, vel[0, 0])
+
+
+def test_single_file_bundle_context(ctx_unit, unit_tensors, tmp_path, rng):
+    """A context created from the one-file form of the bundle computes exactly
+    what the directory form computes."""
+    import itts_cfm
+    import mit2
+
+    f = tmp_path / "unit.mit2"
+    mit2.write_single_file_bundle(f, mit2.make_dit_tensors(0, "unit"))
+    T = 24
+    x, px, cond, style = _inputs(rng, 1, T, P=4)
+    mask = np.ones((1, T), np.uint32)
+    with itts_cfm.Context(f, device=0) as one:
+        got = one.estimator(x, px, cond, style, mask, t=0.3, branches=2)
+    want = ctx_unit.estimator(x, px, cond, style, mask, t=0.3, branches=2)
+    assert np.array_equal(got, want)

@@ -71,3 +71,16 @@ def test_pipeline_reports_stage_errors(pipe, voice, tmp_path):
     with pytest.raises(itts_cfm.IttsError) as e:
         pipe.synthesize(voice, s_infer, 0, noise, 2, 0.7)
     assert e.value.code == itts_cfm.ITTS_EINVAL_SHAPE
+
+
+def test_pipeline_seeded_noise_form(pipe, voice):
+    """itts_pipeline_synthesize_seeded draws x0 as the reference's pipeline
+    does (make_deterministic_normal_noise(P + G, 80, seed, temperature)) and
+    then equals the explicit-noise call bit for bit."""
+    P, G, n_in = 6, 24, 7
+    s_infer, _ = _inputs(P, G, n_in, 4)
+    seed, temp = 20240605, 0.8
+    wave_s, mel_s = pipe.synthesize_seeded(voice, s_infer, G, seed, temp, 3, 0.7)
+    noise = itts_cfm.make_noise(P + G, 80, seed, temp)
+    wave, mel = pipe.synthesize(voice, s_infer, G, noise, 3, 0.7)
+    assert np.array_equal(mel_s, mel) and np.array_equal(wave_s, wave)

@@ -107,6 +107,25 @@ def test_oracle_detects_planted_error(port_unit, unit_tensors):
         _close(g["vel_unit"], wrong.estimator(*args))
 
 
+def test_weight_norm_gain_is_visible(port_unit, unit_tensors):
+    """The synthetic bundles' weight-norm gains differ from ||v_row||, so a fold
+    that drops g (W = v) or normalises along the wrong axis breaks the pin."""
+    g = _load("kat_estimator_t6")
+    args = (g["x"], g["prompt_x"], g["cond"], g["style"], float(g["t"]), g["mask"])
+    for planted in ("drop_gain", "column_norm"):
+        bad = dict(unit_tensors)
+        for k in [k for k in bad if k.endswith("weight_g")]:
+            v = bad[k[: -len("weight_g")] + "weight_v"].astype(np.float32)
+            rows = v.reshape(v.shape[0], -1)
+            if planted == "drop_gain":
+                gain = np.sqrt((rows**2).sum(axis=1))
+            else:
+                gain = np.sqrt((rows**2).sum(axis=0)).mean() * np.ones(rows.shape[0], np.float32)
+            bad[k] = gain.reshape(bad[k].shape).astype(np.float32)
+        with pytest.raises(AssertionError):
+            _close(g["vel_unit"], O.PortOracle(bad).estimator(*args))
+
+
 def test_bigvgan_bundle_matches_golden_generator(vocoder_bundle):
     assert _sha(vocoder_bundle) == str(_load("kat_bigvgan")["weights_sha256"])
 

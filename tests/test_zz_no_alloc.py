@@ -80,3 +80,29 @@ def test_conv5_noalloc_rejects_beyond_scratch():
         itts_cfm.conv5_noalloc(x.data_ptr(), S, T, w.data_ptr(), None, out.data_ptr(), 512)
     assert ei.value.code == itts_cfm.ITTS_ECAP
     assert str(itts_cfm.NOALLOC_CONV5_MAX_ROWS) in str(ei.value)
+
+
+def test_conv5_noalloc_five_weight_tiles(ctx_unit):
+    """N = 640 output channels (five 128-row weight tiles) against itts_op_conv5."""
+    dev = _dev()
+    S, T, N = 3, 131, 640
+    x, xp, w, bias = _case(S, T, N, 13, dev)
+    want = torch.full((S * T, N), float("nan"), device=dev)
+    ctx_unit.op_conv5(xp.data_ptr(), S, T, w.data_ptr(), bias.data_ptr(), want.data_ptr(), N)
+    got = torch.full((S * T, N), float("nan"), device=dev)
+    itts_cfm.conv5_noalloc(x.data_ptr(), S, T, w.data_ptr(), bias.data_ptr(), got.data_ptr(), N)
+    assert torch.isfinite(got).all()
+    diff = got.double() - want.double()
+    assert float(diff.norm() / want.double().norm()) < 1e-5 and float(diff.abs().max()) < 1e-3
+
+
+@pytest.mark.parametrize("N", [80, 48, 720])
+def test_conv5_noalloc_rejects_partial_weight_tiles(N):
+    """N that is not a multiple of 128 is refused with ITTS_EINVAL_SHAPE before any GPU work."""
+    dev = _dev()
+    x = torch.zeros(2 * 16, 512, device=dev, dtype=torch.float16)
+    w = torch.zeros(N, 5 * 512, device=dev, dtype=torch.float16)
+    out = torch.zeros(2 * 16, N, device=dev)
+    with pytest.raises(itts_cfm.IttsError) as ei:
+        itts_cfm.conv5_noalloc(x.data_ptr(), 2, 16, w.data_ptr(), None, out.data_ptr(), N)
+    assert ei.value.code == itts_cfm.ITTS_EINVAL_SHAPE
