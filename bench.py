@@ -5,15 +5,20 @@
                     [--workload 2|5] [--utts B]
 
 A bench "step" is one full sampler run (all CFM steps) over the rank's batch.
-Default workload is BASELINE config 2 per rank: one utterance of T=800 frames
-(P=200 prompt frames), 25 Euler steps, CFG 0.7, random-init f16 weights
-~N(0, 0.02), inputs ~N(0, 1) (seed 1 + rank). Under torchrun each rank owns
-one GPU and its own utterances (weak scaling, no data-path collective); timing
-is CUDA events on the engine's stream, max over ranks.
+The headline workload is configuration 2 per rank: one utterance of T=800
+frames (P=200 prompt frames), 25 Euler steps, CFG 0.7, random-init f16
+weights ~N(0, 0.02), inputs ~N(0, 1) (seed 1 + rank). Under torchrun each
+rank owns one GPU and its own utterance (weak scaling, no data-path
+collective); timing is CUDA events on the engine's stream, max over ranks.
+Every line also carries `scale_out`: configuration 5 (1024 utterances of
+T=800, 12 steps) as ONE job split over the ranks by shard.shard and run
+through itts_cfm_run_batch, timed as the max over ranks.
 
 --impl reference times the reference's own CPU path (oracle/_ref, the
 reference's run_dit_estimator_step_cpu compiled from its sources) on the
-host's cores on a bounded sample of the same workload; rank 0 only.
+host's cores: K guided CFM steps of the configuration-2 utterance at its full
+length (each a conditional and a null estimator call at T=800), spread over
+all host threads; rank 0 only.
 """
 from __future__ import annotations
 
@@ -501,6 +506,9 @@ def pipeline_line(cfg, rank, world, local, barrier, max_over_ranks):
 
 
 def cpu_reference_rate(u, steps_cfm: int, threads: int, reps: int = 1):
+    """Our arm's bounded CPU sample: `threads` host threads each run one guided
+    step of the reference on a REF_SAMPLE_FRAMES-frame slice; frames/s of a
+    `steps_cfm`-step run, and the seconds per guided step per slice."""
     import oracle
 
     ref = oracle.RefOracle(BUNDLE_DIR)
@@ -510,7 +518,62 @@ def cpu_reference_rate(u, steps_cfm: int, threads: int, reps: int = 1):
     return fps, t
 
 
+def _ref_call_pool(calls, threads: int, durations: list | None = None) -> float:
+    """Run reference estimator calls (zero-argument callables) on `threads`
+    host threads, each thread taking the next call as it frees up; returns
+    the wall seconds until the last call ends (and appends each call's own
+    seconds to `durations`)."""
+    import queue
+
+    q = queue.Queue()
+    for c in calls:
+        q.put(c)
+    errs = []
+
+    def worker():
+        while True:
+            try:
+                c = q.get_nowait()
+            except queue.Empty:
+                return
+            try:
+                t0 = time.perf_counter()
+                c()
+                if durations is not None:
+                    durations.append(time.perf_counter() - t0)
+            except Exception as e:  # pragma: no cover
+                errs.append(e)
+
+    ths = [threading.Thread(target=worker) for _ in range(max(1, min(threads, len(calls))))]
+    t0 = time.perf_counter()
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    dt = time.perf_counter() - t0
+    if errs:
+        raise errs[0]
+    return dt
+
+
+def _guided_step_calls(ref, u, t: float = 0.0):
+    """The two reference estimator calls of one guided CFM step over the
+    whole utterance (conditional, then null with zero prompt/cond/style)."""
+    x = u.noise.copy()
+    x[: u.P] = 0
+    px = u.prompt_x()
+    mask = np.ones(u.T, np.uint32)
+    zp, zc, zs = np.zeros_like(px), np.zeros_like(u.cond), np.zeros_like(u.style)
+    return [lambda: ref.estimator(x, px, u.cond, u.style, t, mask), lambda: ref.estimator(x, zp, zc, zs, t, mask)]
+
+
 def run_reference(args, rank):
+    """The reference arm: the reference's compiled run_dit_estimator_step_cpu
+    on the configuration-2 utterance at its full length (T=800). The timed
+    region runs `steps` guided CFM steps (2 * steps estimator calls at
+    T=800) spread over all host threads; frames/s is that of full 25-step
+    sampler runs. Configuration 1 (one guided step at T=400, P=150, t=0.5) is
+    measured exactly on one thread while the warm-up calls run."""
     if rank != 0:
         return 0
     import oracle
@@ -523,27 +586,197 @@ def run_reference(args, rank):
     u = workloads.config_utterances(args.workload, n=1)[0]
     threads = _host_threads()
     ref = oracle.RefOracle(BUNDLE_DIR)
-    for _ in range(args.warmup):
-        _ref_guided_step_sample(ref, u, REF_SAMPLE_FRAMES, threads)
-    t0 = time.perf_counter()
-    per = [_ref_guided_step_sample(ref, u, REF_SAMPLE_FRAMES, threads) for _ in range(args.steps)]
-    total = time.perf_counter() - t0
-    # frames of a full `steps_cfm` sampler run per sample, scaled from one guided step
-    fps = threads * REF_SAMPLE_FRAMES * args.steps / (cfg["steps"] * total)
-    sample = (f"per step: {threads} host threads each run one conditional + one null "
-              f"run_dit_estimator_step_cpu call on a {REF_SAMPLE_FRAMES}-frame slice of the config-{args.workload} "
-              f"utterance; frames/s = threads*{REF_SAMPLE_FRAMES}/({cfg['steps']} CFM steps * step time)")
+    # Configuration 1 exactly, on its own thread, during the warm-up calls.
+    u1 = workloads.config_utterances(1)[0]
+    c1 = {}
+
+    def config1():
+        px1 = u1.prompt_x()
+        m1 = np.ones(u1.T, np.uint32)
+        t0 = time.perf_counter()
+        ref.estimator(u1.noise, px1, u1.cond, u1.style, 0.5, m1)
+        ref.estimator(u1.noise, np.zeros_like(px1), np.zeros_like(u1.cond), np.zeros_like(u1.style), 0.5, m1)
+        c1["s"] = time.perf_counter() - t0
+
+    th1 = threading.Thread(target=config1)
+    th1.start()
+    warm = [c for _ in range(args.warmup) for c in _guided_step_calls(ref, u)]
+    _ref_call_pool(warm, max(1, threads - 1))
+    th1.join()
+    calls = [c for _ in range(args.steps) for c in _guided_step_calls(ref, u)]
+    per_call = []
+    wall = _ref_call_pool(calls, threads, per_call)
+    fps = args.steps * u.T / (cfg["steps"] * wall)
+    sample = (f"{args.steps} guided CFM steps of the config-{args.workload} utterance at its full length "
+              f"(T={u.T}, P={u.P}): {2 * args.steps} run_dit_estimator_step_cpu calls (conditional + null) over "
+              f"{threads} host threads, {wall:.1f} s; frames/s = steps*T/({cfg['steps']} CFM steps * wall)")
     line = {
         "impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": 1e3 * wall / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"config {args.workload}", "T": cfg["T"], "steps_cfm": cfg["steps"], "cfg_rate": cfg["cfg"]},
-        "cpu_baseline": {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+        "config": {"workload": f"config {args.workload}", "T": u.T, "P": u.P, "steps_cfm": cfg["steps"],
+                   "cfg_rate": cfg["cfg"]},
+        "s_per_estimator_call_median": statistics.median(per_call),
+        "ms_per_guided_step_one_thread": 2e3 * statistics.median(per_call),
+        "cpu_baseline": {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample,
+                         "host": _host_model()},
+        "config1": {"workload": "config 1: one guided step (cond + null), T=400, P=150, t=0.5, seed 0",
+                    "ms_per_guided_step": 1e3 * c1.get("s", float("nan")), "cores": 1,
+                    "note": "measured on one thread while the warm-up calls ran on the other threads"},
         "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "per_step_s": per,
     }
     print(json.dumps(line))
     return 0
+
+
+def _host_model() -> str:
+    try:
+        for line in subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout.splitlines():
+            if line.startswith("Model name"):
+                return f"{line.split(':', 1)[1].strip()}, nproc {os.cpu_count()}"
+    except Exception:
+        pass
+    return f"nproc {os.cpu_count()}"
+
+
+# ---------------------------------------------------------------- configurations 3, 4 and 5
+
+def _timed_launches(ctx, launches, steps: int, cfg_rate: float, reps: int = 1) -> float:
+    """Device milliseconds of the sampler over a list of padded batches
+    (vl, pl, noise, px, cond, style) with inputs resident: each batch is
+    staged, warmed once, then its graph launches are bracketed by CUDA events
+    on the context's stream; the sum over batches of the mean per launch."""
+    import torch
+
+    st = torch.cuda.ExternalStream(ctx.stream())
+    total = 0.0
+    for vl, pl, noise, px, cond, style in launches:
+        ctx.stage_padded(vl, pl, noise, px, cond, style, steps, cfg_rate)
+        ctx.launch()
+        ctx.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            ctx.launch()
+        e1.record(st)
+        e1.synchronize()
+        total += e0.elapsed_time(e1) / reps
+    return total
+
+
+def scale_out_line(ctx, rank, world, barrier, max_over_ranks, gather_ranks, peak):
+    """Configuration 5 as ONE job: 1024 utterances of T=800 (utterance i from
+    default_rng((4, i))), 12 CFM steps, CFG 0.7, partitioned over the ranks by
+    shard.shard (longest-processing-time on F(T), no communication) and run
+    through the sampler. `value`: the whole job's frames over the max over
+    ranks of each rank's device time with its share resident in HBM (its
+    share is one padded batch, as itts_cfm_run_batch plans it); `e2e`: the same
+    job through itts_cfm_run_batch with host buffers (wall clock, max over
+    ranks)."""
+    import itts_cfm
+    import shard
+
+    c = workloads.CONFIGS[5]
+    n, T = c["n"], c["T"]
+    lengths = [T] * n
+    parts = shard.shard(lengths, world)
+    mine = parts[rank]
+    utts = [workloads.utterance_at(5, i) for i in mine]
+    plan = itts_cfm.batch_plan([u.T for u in utts], c["cfg"])
+    launches = [workloads.pad_batch([utts[i] for i in idx], utts[idx[0]].T) for idx in plan]
+    barrier()
+    dev_ms = _timed_launches(ctx, launches, c["steps"], c["cfg"])
+    del launches
+    per_rank_ms = gather_ranks(dev_ms)
+    job_ms = max(per_rank_ms)
+    batch = [dict(noise=u.noise, prompt=u.prompt, cond=u.cond, style=u.style) for u in utts]
+    barrier()
+    t0 = time.perf_counter()
+    ctx.run_batch(batch, c["steps"], c["cfg"])
+    host_s = time.perf_counter() - t0
+    job_host_s = max_over_ranks(host_s)
+    flops = n * itts_cfm.step_flops(2, T) * c["steps"]
+    h2d = sum(u.noise.nbytes + u.prompt.nbytes + u.cond.nbytes + u.style.nbytes for u in utts)
+    return {"metric": "mel frames/s, configuration 5 as one job sharded over the GPUs",
+            "workload": f"{n} utterances x T={T} (P={c['P']}), {c['steps']} CFM steps, CFG {c['cfg']}, "
+                        f"shard.shard over {world} rank(s), utterance i from default_rng((4, i))",
+            "value": n * T / (job_ms / 1e3), "unit": UNIT, "job_ms": job_ms, "per_rank_ms": per_rank_ms,
+            "utterances_per_rank": [len(p) for p in parts], "imbalance": shard.imbalance(lengths, parts),
+            "tflops": flops / (job_ms / 1e3) / 1e12, "frac": flops / (job_ms / 1e3) / 1e12 / peak,
+            "gpus_active": sum(1 for v in per_rank_ms if v > 0), "scaling": "strong (fixed job)",
+            "e2e": {"value": n * T / job_host_s, "unit": UNIT, "job_s": job_host_s,
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(len(utts) * T * 80 * 4),
+                    "path": "itts_cfm_run_batch, host buffers in and out (this rank's share)"}}
+
+
+def config3_line(ctx, rank, world, barrier, max_over_ranks, peak, cpu_sec_per_flop):
+    """Configuration 3 on every GPU: 64 utterances with lengths drawn from
+    200..1500 (seed 2), 16 CFM steps, CFG 0.7, planned into padded launches as
+    itts_cfm_run_batch plans them (length classes, each launch padded to its
+    longest utterance, key-padding masks). Frames and FLOPs count the real
+    (unpadded) lengths."""
+    import itts_cfm
+
+    c = workloads.CONFIGS[3]
+    utts = workloads.config_utterances(3)
+    Ts = [u.T for u in utts]
+    plan = itts_cfm.batch_plan(Ts, c["cfg"])
+    launches = [workloads.pad_batch([utts[i] for i in idx], Ts[idx[0]]) for idx in plan]
+    barrier()
+    dev_ms = max_over_ranks(_timed_launches(ctx, launches, c["steps"], c["cfg"]))
+    del launches
+    batch = [dict(noise=u.noise, prompt=u.prompt, cond=u.cond, style=u.style) for u in utts]
+    barrier()
+    t0 = time.perf_counter()
+    ctx.run_batch(batch, c["steps"], c["cfg"])
+    host_s = max_over_ranks(time.perf_counter() - t0)
+    frames = sum(Ts)
+    padded = sum(Ts[idx[0]] * len(idx) for idx in plan)
+    flops = sum(itts_cfm.step_flops(2, T) for T in Ts) * c["steps"]
+    cpu = None
+    if cpu_sec_per_flop:
+        cpu_s = flops * cpu_sec_per_flop
+        cpu = {"value": frames / cpu_s, "unit": UNIT, "kind": "reference", "extrapolated": True,
+               "sample": "the configuration-2 CPU sample's seconds per algorithmic FLOP times this workload's "
+                         "F(T) summed over the drawn lengths and 16 steps"}
+    return {"metric": "mel frames/s, configuration 3 (bucketed serving batch)",
+            "workload": f"{len(utts)} utterances, T in [{min(Ts)}, {max(Ts)}] (seed 2), {c['steps']} CFM steps, "
+                        f"CFG {c['cfg']}, {len(plan)} padded launches, padding {padded / frames - 1:.1%}",
+            "value": world * frames / (dev_ms / 1e3), "unit": UNIT, "ms_per_run": dev_ms,
+            "tflops": flops / (dev_ms / 1e3) / 1e12, "frac": flops / (dev_ms / 1e3) / 1e12 / peak,
+            "e2e": {"value": world * frames / host_s, "unit": UNIT, "s_per_run": host_s,
+                    "path": "itts_cfm_run_batch, host buffers in and out"},
+            "cpu_baseline": cpu}
+
+
+def config4_line(ctx, rank, world, barrier, max_over_ranks, peak, cpu_sec_per_flop):
+    """Configuration 4 on every GPU: one utterance of T=4096 (P=300, seed 3),
+    25 CFM steps, CFG 0.7; device-timed graph runs with inputs resident and
+    the per-kernel split of one CFM step."""
+    import itts_cfm
+
+    c = workloads.CONFIGS[4]
+    u = workloads.config_utterances(4)[0]
+    launches = [workloads.pad_batch([u], u.T)]
+    barrier()
+    dev_ms = max_over_ranks(_timed_launches(ctx, launches, c["steps"], c["cfg"], reps=3))
+    prof = ctx.profile_step(reps=1)
+    prof.sort(key=lambda d: -d["ms"])
+    flops = itts_cfm.step_flops(2, u.T) * c["steps"]
+    attn = [d for d in prof if d["name"] == "attention"]
+    tot = sum(d["ms"] for d in prof)
+    cpu = None
+    if cpu_sec_per_flop:
+        cpu_s = flops * cpu_sec_per_flop
+        cpu = {"value": u.T / cpu_s, "unit": UNIT, "kind": "reference", "extrapolated": True,
+               "sample": "the configuration-2 CPU sample's seconds per algorithmic FLOP times F(4096) x 25 steps"}
+    return {"metric": "mel frames/s, configuration 4 (T=4096 long utterance)",
+            "workload": f"1 utterance, T={u.T}, P={u.P}, {c['steps']} CFM steps, CFG {c['cfg']}",
+            "value": world * u.T / (dev_ms / 1e3), "unit": UNIT, "ms_per_run": dev_ms,
+            "ms_per_cfm_step": dev_ms / c["steps"], "tflops": flops / (dev_ms / 1e3) / 1e12,
+            "frac": flops / (dev_ms / 1e3) / 1e12 / peak,
+            "attention_share": attn[0]["ms"] / tot if attn and tot else None,
+            "kernels": [kernel_row(d, 1) for d in prof], "cpu_baseline": cpu}
 
 
 # ---------------------------------------------------------------- our arm
@@ -571,6 +804,12 @@ def main():
     ap.add_argument("--gpt-trace", action="store_true", help="add the persistent decoder's stage trace to the gpt line")
     ap.add_argument("--vocoder-only", action="store_true",
                     help="time only the BigVGAN vocoder and print its line (profiling aid)")
+    ap.add_argument("--scale-out", type=int, default=1,
+                    help="also run configuration 5 as one job sharded over the ranks (0 = skip)")
+    ap.add_argument("--config3", type=int, default=1, help="also time configuration 3 (0 = skip)")
+    ap.add_argument("--config4", type=int, default=1, help="also time configuration 4 (0 = skip)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling aid)")
+    ap.add_argument("--no-profile", action="store_true", help="skip the per-launch profile (profiling aid)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -604,6 +843,14 @@ def main():
         t = torch.tensor([v], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    def gather_ranks(v: float) -> list[float]:
+        if dist is None:
+            return [v]
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        out = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [float(x.item()) for x in out]
 
     cfg = workloads.CONFIGS[args.workload]
     if args.gpt_only:
@@ -678,41 +925,59 @@ def main():
         if rc != 0:
             raise RuntimeError(lib.itts_cfm_last_error(ctx.h).decode())
 
-    for _ in range(2):
-        e2e_once()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        e2e_once()
-    t_e2e = time.perf_counter() - t0
-    barrier()
-    t_e2e = max_over_ranks(t_e2e)
-    e2e_value = frames_per_step * args.steps / t_e2e
+    e2e_value = None
+    if not args.no_e2e:
+        for _ in range(2):
+            e2e_once()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_once()
+        t_e2e = time.perf_counter() - t0
+        barrier()
+        t_e2e = max_over_ranks(t_e2e)
+        e2e_value = frames_per_step * args.steps / t_e2e
     h2d = noise.nbytes + px.nbytes + cond.nbytes + style.nbytes + vl.nbytes + pl.nbytes + B * 2 * T * 4
     d2h = B * T * 80 * 4 + 4
 
-    # Roofline of the dominant kernel (all tcgen05 GEMM launches), timed per launch.
-    ctx.stage_padded(vl, pl, noise, px, cond, style, cfg["steps"], cfg["cfg"])
-    prof = ctx.profile_step(reps=3)
-    prof.sort(key=lambda d: -d["ms"])
-    total_prof_ms = sum(d["ms"] for d in prof)
-    gemm = gemm_family(prof)
+    # Roofline of the dominant kernel family (all tcgen05 GEMM launches of a
+    # CFM step). The per-launch event profile gives each kernel kind's share
+    # of the summed launch time; the GEMM family's time INSIDE the timed graph
+    # is that share of the device-timed CFM step, so the family's time never
+    # exceeds the step it belongs to.
+    ms_per_cfm = ms / args.steps / cfg["steps"]
     peaks, peaks_kind = measured_peaks()
-    achieved = gemm["flops"] / (gemm["ms"] / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops", 1590.0))
-    traffic = None
-    tf = REPO / "profiles" / "gemm_traffic.json"
-    if tf.exists():
-        try:
-            traffic = json.loads(tf.read_text()).get(f"config{args.workload}_bytes_per_launch")
-        except Exception:
-            traffic = None
-    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": "gemm_tc_kernel (tcgen05, all GEMM launches of one CFM step)",
-                "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(gemm["launches"], 1),
-                "peak_source": f"MEASURED_PEAKS.json bf16_tflops ({peaks_kind}, burst)",
-                "time_share": gemm["ms"] / total_prof_ms if total_prof_ms else None,
-                "kernels": [kernel_row(d, 3) for d in prof]}
+    roofline = None
+    if not args.no_profile:
+        ctx.stage_padded(vl, pl, noise, px, cond, style, cfg["steps"], cfg["cfg"])
+        prof = ctx.profile_step(reps=3)
+        prof.sort(key=lambda d: -d["ms"])
+        total_prof_ms = sum(d["ms"] for d in prof)
+        gemm = gemm_family(prof)
+        share = gemm["ms"] / total_prof_ms
+        gemm_ms_in_graph = share * ms_per_cfm
+        gemm_flops_per_step = gemm["flops"] / 3
+        achieved = gemm_flops_per_step / (gemm_ms_in_graph / 1e3) / 1e12
+        assert gemm_ms_in_graph <= ms_per_cfm * (1 + 1e-9)
+        traffic = None
+        tf = REPO / "profiles" / "gemm_traffic.json"
+        if tf.exists():
+            try:
+                traffic = json.loads(tf.read_text()).get(f"config{args.workload}_bytes_per_launch")
+            except Exception:
+                traffic = None
+        launches = gemm["launches"] // 3
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "traffic": traffic, "kernel": "gemm_tc_kernel (tcgen05, all GEMM launches of one CFM step)",
+                    "launches_per_cfm_step": launches, "gemm_flops_per_cfm_step": gemm_flops_per_step,
+                    "time_share": share, "gemm_ms_per_cfm_step_in_graph": gemm_ms_in_graph,
+                    "avg_launch_us": 1e3 * gemm_ms_in_graph / max(launches, 1),
+                    "event_sum_ms_per_cfm_step": total_prof_ms / 3, "ms_per_cfm_step": ms_per_cfm,
+                    "method": "achieved = GEMM FLOPs per CFM step / (GEMM share of the per-launch event profile x "
+                              "device-timed CFM step of the graph run)",
+                    "peak_source": f"MEASURED_PEAKS.json bf16_tflops ({peaks_kind}, burst)",
+                    "kernels": [kernel_row(d, 3) for d in prof]}
 
     # Batched serving throughput on the same utterance shape (supplementary):
     # utterances per GPU share one padded batch, so the GEMMs see large M.
@@ -763,16 +1028,29 @@ def main():
         gpt = gpt_line(args, rank, world, local, barrier, max_over_ranks, float(peaks.get("hbm_gbs", 6546.0)))
 
     cpu = None
+    cpu_sec_per_flop = None  # reference CPU seconds per algorithmic FLOP, from the sample (for extrapolation)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
 
         if oracle.ref_available():
             threads = _host_threads()
             fps, t = cpu_reference_rate(utts[0], cfg["steps"], threads)
+            cpu_sec_per_flop = t / (threads * itts_cfm.step_flops(2, REF_SAMPLE_FRAMES))
             cpu = {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference",
                    "sample": (f"{threads} threads, each one guided CFM step (cond + null run_dit_estimator_step_cpu) "
-                              f"on a {REF_SAMPLE_FRAMES}-frame slice; {t:.2f} s; scaled to frames/s of a "
-                              f"{cfg['steps']}-step run")}
+                              f"on a {REF_SAMPLE_FRAMES}-frame slice of the T={T} utterance; {t:.2f} s; scaled to "
+                              f"frames/s of a {cfg['steps']}-step run (the full-length measurement is the "
+                              f"--impl reference arm)"), "host": _host_model()}
+
+    scale_out = None
+    if args.scale_out:
+        scale_out = scale_out_line(ctx, rank, world, barrier, max_over_ranks, gather_ranks, peak)
+    config3 = None
+    if args.config3:
+        config3 = config3_line(ctx, rank, world, barrier, max_over_ranks, peak, cpu_sec_per_flop)
+    config4 = None
+    if args.config4:
+        config4 = config4_line(ctx, rank, world, barrier, max_over_ranks, peak, cpu_sec_per_flop)
 
     ctx.close()
     if rank == 0:
@@ -786,13 +1064,16 @@ def main():
                        "global_batch": B * world, "parallelism": f"utterance-sharded x{world}",
                        "l2": "working set > L2: 182 MB of weights re-read every CFM step (126 MB L2)",
                        "weights": "random-init f16 ~N(0,0.02), seed 0"},
-            "ms_per_cfm_step": ms / args.steps / cfg["steps"],
+            "ms_per_cfm_step": ms_per_cfm,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": launches_per_step * args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clk,
             "batched": batched,
+            "scale_out": scale_out,
+            "config3": config3,
+            "config4": config4,
             "condition": condition,
             "vocoder": vocoder,
             "pipeline": pipeline,

@@ -89,16 +89,19 @@ int itts_cfm_run(itts_cfm_ctx* ctx, const float* noise, const float* prompt, con
                  uint32_t T, uint32_t P, uint32_t steps, float cfg_rate, float* out_mel);
 
 /*
- * Batched serving: utterances are sorted into length buckets
- * (itts_cfm_bucket_len), padded with zero rows and key-padding masks, and run
- * bucket by bucket. A padded utterance equals the single-utterance sampler run
- * at the padded length with its mask (reflect padding and masking make it
- * differ slightly from the unpadded run; bucket length == T gives exactly
+ * Batched serving: utterances are grouped into length classes
+ * (itts_cfm_bucket_len), sorted longest first within a class (ties by index),
+ * cut into launches of at most ITTS_MAX_ROWS rows, and each launch is padded
+ * to its longest utterance with zero rows and key-padding masks. A padded
+ * utterance equals the single-utterance sampler run at the padded length with
+ * its mask (reflect padding and masking make it differ slightly from the
+ * unpadded run; an utterance as long as its launch gives exactly
  * itts_cfm_run). Has no single reference function: it batches calls of
  * run_cfm_euler_metal (runtime/impl/tts_synthesis/synthesis_pipeline.cpp:1085).
  */
 int itts_cfm_run_batch(itts_cfm_ctx* ctx, uint32_t n, const itts_cfm_utt* utts, uint32_t steps, float cfg_rate);
-/* Padded length an utterance of T frames is bucketed to by itts_cfm_run_batch. */
+/* Length class of an utterance of T frames in itts_cfm_run_batch (an upper
+ * bound of the length its launch is padded to). */
 uint32_t itts_cfm_bucket_len(uint32_t T);
 
 /*

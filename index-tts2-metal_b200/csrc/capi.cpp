@@ -243,13 +243,19 @@ int itts_cfm_run_batch(itts_cfm_ctx* ctx, uint32_t n, const itts_cfm_utt* utts, 
       need(u.P <= u.T && (u.P == 0 || u.prompt), "bad prompt");
     }
     const uint32_t branches = cfg_rate > 0.0f ? 2u : 1u;
+    // Group by length class, longest first within a class (ties by index),
+    // cut into launches of at most ITTS_MAX_ROWS rows, and pad each launch to
+    // its longest utterance: a launch whose utterances share one length runs
+    // unpadded, exactly as itts_cfm_run would.
     std::map<uint32_t, std::vector<uint32_t>> buckets;
     for (uint32_t i = 0; i < n; ++i) buckets[itts_cfm_bucket_len(utts[i].T)].push_back(i);
     for (auto& kv : buckets) {
-      const uint32_t Tp = kv.first;
-      const uint32_t per = std::max<uint32_t>(1u, ITTS_MAX_ROWS / (branches * Tp));
+      std::stable_sort(kv.second.begin(), kv.second.end(),
+                       [&](uint32_t a, uint32_t b) { return utts[a].T > utts[b].T; });
+      const uint32_t per = std::max<uint32_t>(1u, ITTS_MAX_ROWS / (branches * kv.first));
       for (size_t off = 0; off < kv.second.size(); off += per) {
         const uint32_t B = static_cast<uint32_t>(std::min<size_t>(per, kv.second.size() - off));
+        const uint32_t Tp = utts[kv.second[off]].T;
         std::vector<float> noise(static_cast<size_t>(B) * Tp * 80, 0.0f), px(noise.size(), 0.0f),
             cond(static_cast<size_t>(B) * Tp * 512, 0.0f), style(static_cast<size_t>(B) * 192, 0.0f),
             out(noise.size(), 0.0f);

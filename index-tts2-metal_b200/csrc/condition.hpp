@@ -1,5 +1,5 @@
-// Condition assembly before the CFM sampler (SURVEY row "condition assembly
-// and length regulator"): s_infer [n_in, 1024] -> length regulator -> [G, 512],
+// Condition assembly before the CFM sampler (the length regulator and the
+// prompt-condition merge): s_infer [n_in, 1024] -> length regulator -> [G, 512],
 // placed after the voice prompt's P condition rows: cond [P + G, 512].
 //
 // Follows run_length_regulator_full_metal / _cpu (runtime/impl/gpt.cpp:

@@ -344,6 +344,36 @@ def step_flops(S: int, T: int) -> float:
     return float(load().itts_cfm_step_flops(S, T))
 
 
+MAX_ROWS = 1 << 22
+
+
+def batch_plan(lengths: list[int], cfg_rate: float) -> list[list[int]]:
+    """The launches itts_cfm_run_batch makes, as lists of utterance indices
+    (longest first): utterances are grouped by bucket_len (ascending), sorted
+    longest first within a group (ties by index) and cut into launches of at
+    most MAX_ROWS rows; each launch is padded to its first (longest) member."""
+    branches = 2 if cfg_rate > 0 else 1
+    groups: dict[int, list[int]] = {}
+    for i, T in enumerate(lengths):
+        groups.setdefault(bucket_len(T), []).append(i)
+    plan = []
+    for cls in sorted(groups):
+        idx = sorted(groups[cls], key=lambda i: -lengths[i])
+        per = max(1, MAX_ROWS // (branches * cls))
+        plan += [idx[off : off + per] for off in range(0, len(idx), per)]
+    return plan
+
+
+def batch_padded_lengths(lengths: list[int], cfg_rate: float) -> list[int]:
+    """The padded length itts_cfm_run_batch runs each utterance at (the
+    longest utterance of its launch, see batch_plan)."""
+    out = [0] * len(lengths)
+    for launch in batch_plan(lengths, cfg_rate):
+        for i in launch:
+            out[i] = lengths[launch[0]]
+    return out
+
+
 class Vocoder:
     """BigVGAN vocoder bound to one GPU (itts_vocoder_create): mel [T, 80] ->
     waveform [256 T] in [-1, 1]."""

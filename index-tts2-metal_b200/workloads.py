@@ -10,6 +10,7 @@ Configurations (token-major layouts):
   3  64 utterances, T ~ U{200..1500}, 16 steps, cfg 0.7, padded seed 2
   4  T=4096, P=300, 25 steps, cfg 0.7                           seed 3
   5  1024 x T=800, 12 steps, cfg 0.7, sharded over GPUs         seed 4
+     (utterance i from default_rng((4, i)))
 """
 from __future__ import annotations
 
@@ -57,10 +58,24 @@ def utterance(rng: np.random.Generator, T: int, P: int) -> Utterance:
     )
 
 
+def utterance_at(cfg_id: int, index: int) -> Utterance:
+    """Utterance `index` of a fixed-length configuration, drawn from its own
+    stream default_rng((seed, index)), so that any shard of a large job can be
+    drawn without the utterances before it."""
+    c = CONFIGS[cfg_id]
+    if isinstance(c["T"], tuple):
+        raise ValueError("utterance_at needs a fixed-length configuration")
+    return utterance(np.random.default_rng((c["seed"], index)), c["T"], c["P"])
+
+
 def config_utterances(cfg_id: int, n: int | None = None, seed_offset: int = 0) -> list[Utterance]:
     """Utterances of a configuration (optionally only the first n, or a shard
-    drawn with a distinct seed offset for multi-GPU runs)."""
+    drawn with a distinct seed offset for multi-GPU runs). Configuration 5's
+    utterances come from utterance_at (one stream per utterance)."""
     c = CONFIGS[cfg_id]
+    if cfg_id == 5:
+        count = c["n"] if n is None else n
+        return [utterance_at(5, seed_offset + i) for i in range(count)]
     rng = np.random.default_rng(c["seed"] + seed_offset)
     count = c["n"] if n is None else n
     out = []

@@ -24,7 +24,9 @@ from pathlib import Path
 ORACLE = Path(__file__).resolve().parent
 REF_OUT = ORACLE / "_ref"
 LIB_OUT = ORACLE / "lib"
-DEFAULT_REF = Path(os.environ.get("ITTS_REFERENCE_DIR", "/root/reference"))
+# The reference tree: $ITTS_REFERENCE_DIR, else a `reference` checkout next to
+# this repository's directory (when neither exists, build_ref() skips).
+DEFAULT_REF = Path(os.environ.get("ITTS_REFERENCE_DIR", str(ORACLE.parent.parent / "reference")))
 
 # (file inside the reference, first line, last line) of each function group.
 RANGES = [

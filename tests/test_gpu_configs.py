@@ -1,4 +1,4 @@
-"""BASELINE configs 3 and 4 at their full sizes on the GPU, through the C ABI.
+"""Benchmark configurations 3 and 4 at their full sizes on the GPU, through the C ABI.
 
 Config 4 (one utterance of T=4096, P=300, 25 steps, CFG 0.7) stresses the
 masked RoPE attention at long sequence length: one teacher-forced guided step
@@ -77,17 +77,19 @@ def test_config3_bucketed_batch_full_size(ctx_baseline, port_baseline):
         assert o.shape == (u.T, 80)
         assert np.isfinite(o).all()
         assert np.all(o[: u.P] == 0.0)
-    # Shortest utterance: the oracle's masked sampler at the bucket length.
+    lens = itts_cfm.batch_padded_lengths([u.T for u in utts], 0.7)
+    # Shortest utterance: the oracle's masked sampler at its launch's padded length.
     i = int(np.argmin([u.T for u in utts]))
     u = utts[i]
-    Tp = itts_cfm.bucket_len(u.T)
+    Tp = lens[i]
     vl, pl, noise, px, cond, style = W.pad_batch([u], Tp)
     mask = (np.arange(Tp) < u.T).astype(np.uint32)
     ref = port_baseline.euler(noise[0], px[0], cond[0], style[0], u.P, 16, 0.7, mask=mask)
     _mel_ok(ref[: u.T], outs[i])
-    # Longest utterance: identical to a padded run of itself alone.
+    # Longest utterance: its launch is padded to its own length, so it equals
+    # the single-utterance sampler bit for bit (rows never mix across sequences).
     j = int(np.argmax([u.T for u in utts]))
     u = utts[j]
-    vl, pl, noise, px, cond, style = W.pad_batch([u], itts_cfm.bucket_len(u.T))
-    alone = ctx_baseline.run_padded(vl, pl, noise, px, cond, style, 16, 0.7)[0, : u.T]
+    assert lens[j] == u.T
+    alone = ctx_baseline.run(u.noise, u.prompt, u.cond, u.style, 16, 0.7)
     assert np.array_equal(alone, outs[j])

@@ -2,7 +2,7 @@
 CPU oracle (oracle/dit_oracle.c, itself pinned to the reference's compiled CPU
 functions by tests/golden/).
 
-Gates (BASELINE north_star): per-step velocity cosine >= 0.999; final mel
+Gates: per-step velocity cosine >= 0.999; final mel
 max-abs <= 2e-2 or relative L2 <= 1e-2. f16 GEMM operands with fp32
 accumulation; the "unit" bundle makes every sub-path contribute O(1)."""
 from __future__ import annotations
@@ -119,16 +119,20 @@ def test_padded_batch_vs_oracle(ctx_unit, port_unit, rng):
 
 
 def test_run_batch_buckets_equal_padded(ctx_unit, rng):
-    """itts_cfm_run_batch == itts_cfm_run_padded at each utterance's bucket length (bitwise)."""
+    """itts_cfm_run_batch == itts_cfm_run_padded at the length each
+    utterance's launch is padded to (the longest of its length class), bitwise;
+    an utterance that is the longest of its class equals itts_cfm_run."""
     import itts_cfm
 
     utts = [W.utterance(rng, T, P) for T, P in ((100, 10), (140, 20), (60, 5))]
     outs = ctx_unit.run_batch([dict(noise=u.noise, prompt=u.prompt, cond=u.cond, style=u.style) for u in utts], 2, 0.7)
-    for u, o in zip(utts, outs):
-        Tp = itts_cfm.bucket_len(u.T)
+    lens = itts_cfm.batch_padded_lengths([u.T for u in utts], 0.7)
+    assert lens == [100, 140, 100]
+    for u, o, Tp in zip(utts, outs, lens):
         vl, pl, noise, px, cond, style = W.pad_batch([u], Tp)
         ref = ctx_unit.run_padded(vl, pl, noise, px, cond, style, 2, 0.7)[0, : u.T]
         assert np.array_equal(ref, o)
+    assert np.array_equal(outs[1], ctx_unit.run(utts[1].noise, utts[1].prompt, utts[1].cond, utts[1].style, 2, 0.7))
 
 
 def test_batch_invariance_and_determinism(ctx_unit, rng):
