@@ -2,10 +2,11 @@
 // branches batched as rows [u0 cond | u0 null | u1 cond | ...]):
 //   merge GEMM (x slice, + step-invariant base) -> 13 x { [skip-in GEMM],
 //   AdaRMSNorm, QKV GEMM (+RoPE), attention, wo GEMM (+residual), AdaRMSNorm,
-//   w13 GEMM (+SwiGLU), w2 GEMM (+residual) } -> AdaRMSNorm -> skip_linear GEMM
-//   -> conv1|res GEMM (-> reflect-padded WaveNet input) -> 8 x { k=5 conv GEMM
-//   (+gate), res/skip GEMM (+update) } -> AdaLN -> final linear GEMM -> conv2
-//   GEMM -> CFG + Euler + prompt zero.
+//   w13 GEMM (+SwiGLU), w2 GEMM (+residual) } -> AdaRMSNorm -> post GEMM
+//   (skip_linear composed with conv1|res -> reflect-padded WaveNet input and
+//   the res projection) -> 8 x { k=5 conv GEMM (+gate), res/skip GEMM
+//   (+update) } -> AdaLN -> out GEMM (final linear composed with conv2) ->
+//   CFG + Euler + prompt zero.
 // Follows run_cfm_euler_cpu / run_dit_estimator_step_cpu
 // (runtime/impl/dit_cfm_bigvgan.cpp:2908-2937, 1768-1788) and the single-pass
 // Metal schedule (runtime/impl/dit_cfm_bigvgan.cpp:2367-2713).
@@ -34,7 +35,10 @@ GemmLaunch make_gemm(Operand a0, Operand a1, Operand b, int M, int N, int K, int
   std::memset(&g, 0, sizeof(g));
   int pair = 0;
   if (bn == 0) {
-    const GemmPick pk = gemm_pick(M, N, epi == kEpiSwiGLU || epi == kEpiWnGate || epi == kEpiWnResSkip);
+    // Paired epilogues need 128-column slabs; the conv1|res epilogue switches
+    // destination at column 512, which a tile must not straddle.
+    const GemmPick pk = gemm_pick(M, N, epi == kEpiSwiGLU || epi == kEpiWnGate || epi == kEpiWnResSkip ||
+                                            epi == kEpiConv1Res);
     bn = pk.bn;
     pair = pk.pair;
   }
@@ -242,14 +246,12 @@ Work* Engine::work(int B, int T, int branches) {
     w->attn16 = carve<__half>(cur, R * 512);
     w->h = carve<float>(cur, R * 512);
     w->g16 = carve<__half>(cur, R * 1536);
-    w->ls16 = carve<__half>(cur, R * 512);
     w->xp16 = carve<__half>(cur, static_cast<size_t>(w->Rp) * 512);
     w->res = carve<float>(cur, R * 512);
     w->gate16 = carve<__half>(cur, R * 512);
     w->wacc = carve<float>(cur, R * 512);
     w->fin = carve<float>(cur, R * 512);
     w->fn16 = carve<__half>(cur, R * 512);
-    w->fh16 = carve<__half>(cur, R * 512);
     w->vel = carve<float>(cur, R * 80);
     w->rope = carve<float2>(cur, static_cast<size_t>(T) * 32);
     return cur;
@@ -363,18 +365,12 @@ void Engine::build_work_launches(Work* w) {
     consumer(w->g_qkv[l]);
     consumer(w->g_w13[l]);
   }
-  w->g_sl = make_gemm(act(w->xn16, 512, R), act(w->XD, kXdLd, R), wt(w_.wsl, 512 + kXdLd, 512), R, 512, 512 + kXdLd,
-                      kASplit, 8, 0, 0,
-                      kEpiF16);
-  w->g_sl.args.bias = w_.bsl;
-  w->g_sl.args.out16 = w->ls16;
-  w->g_sl.args.ld16 = 512;
-  w->g_c1res = make_gemm(act(w->ls16, 512, R), none, wt(w_.wc1res, 512, 1024), R, 1024, 512, kAPlain, 0, 0, 0,
-                         kEpiConv1Res);
-  w->g_c1res.args.bias = w_.bc1res;
-  w->g_c1res.args.wn_xp = w->xp16;
-  w->g_c1res.args.out32 = w->res;
-  w->g_c1res.args.ld32 = 512;
+  w->g_post = make_gemm(act(w->xn16, 512, R), act(w->XD, kXdLd, R), wt(w_.wpost, 512 + kXdLd, 1024), R, 1024,
+                        512 + kXdLd, kASplit, 8, 0, 0, kEpiConv1Res);
+  w->g_post.args.bias = w_.bpost;
+  w->g_post.args.wn_xp = w->xp16;
+  w->g_post.args.out32 = w->res;
+  w->g_post.args.ld32 = 512;
   for (int l = 0; l < kWnLayers; ++l) {
     w->g_in[l] = make_gemm(act(w->xp16, 512, w->Rp), none, wt(w_.win[l], 2560, 1024), w->Rp, 1024, 2560, kAConv, 0, 8,
                            0, kEpiWnGate);
@@ -396,15 +392,11 @@ void Engine::build_work_launches(Work* w) {
     w->g_rs[l].args.wn_xp = w->xp16;
     w->g_rs[l].args.wn_acc = w->wacc;
   }
-  w->g_fin = make_gemm(act(w->fn16, 512, R), none, wt(w_.wfin, 512, 512), R, 512, 512, kAPlain, 0, 0, 0, kEpiF16);
-  w->g_fin.args.bias = w_.bfin;
-  w->g_fin.args.out16 = w->fh16;
-  w->g_fin.args.ld16 = 512;
-  w->g_c2 = make_gemm(act(w->fh16, 512, R), none, wt(w_.wc2, 512, 80), R, 80, 512, kAPlain, 0, 0, 80, kEpiF32);
-  w->g_c2.args.bias = w_.bc2;
-  w->g_c2.args.out32 = w->vel;
-  w->g_c2.args.ld32 = 80;
-  GemmLaunch* all[] = {&w->g_cp, &w->g_base, &w->g_merge, &w->g_sl, &w->g_c1res, &w->g_fin, &w->g_c2};
+  w->g_out = make_gemm(act(w->fn16, 512, R), none, wt(w_.wout, 512, 80), R, 80, 512, kAPlain, 0, 0, 80, kEpiF32);
+  w->g_out.args.bias = w_.bout;
+  w->g_out.args.out32 = w->vel;
+  w->g_out.args.ld32 = 80;
+  GemmLaunch* all[] = {&w->g_cp, &w->g_base, &w->g_merge, &w->g_post, &w->g_out};
   for (GemmLaunch* g : all) common(*g);
   for (int l = 0; l < kLayers; ++l) {
     common(w->g_qkv[l]);
@@ -502,9 +494,12 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
     }
     return b;
   };
-  auto G = [&](const char* name, const GemmLaunch& g, double K) {
+  // K: the launch's own contraction depth (for its bytes); macs: the
+  // algorithmic multiply-adds per row it stands for in the reference's op
+  // graph (N * K, or the sum over the layers a composed launch replaces).
+  auto G = [&](const char* name, const GemmLaunch& g, double K, double macs = 0.0) {
     const double rows = g.args.a_mode == kAConv ? R : static_cast<double>(g.args.M);
-    const double flops = 2.0 * rows * g.args.N * K;
+    const double flops = 2.0 * rows * (macs > 0.0 ? macs : g.args.N * K);
     P.run(name, flops, prof ? gemm_bytes(g, rows, K) : 0.0, [&] { check(gemm_run(g, stream_), name); });
   };
   // Launch copies carrying this step's folded-norm constants (nrm_w: the
@@ -531,8 +526,7 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
   P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
     check(adarms_run(w->xres, w->R, tab + kTabNorm, w_.g_norm, w->xn16, stream_), "adarms");
   });
-  G("gemm.skip_linear", w->g_sl, 592);
-  G("gemm.conv1_res", w->g_c1res, 512);
+  G("gemm.post", w->g_post, 512 + kXdLd, 592.0 * 512 + 512.0 * 1024);  // skip_linear, then conv1 | res
   for (int l = 0; l < kWnLayers; ++l) {
     GemmLaunch gi = w->g_in[l];
     gi.args.wn_cond = tab + kTabWn + l * 1024;
@@ -541,8 +535,7 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
   }
   P.run("adaln", 0.0, R * 512 * (4 + 2),
         [&] { check(adaln_run(w->fin, w->R, tab + kTabFinal, w->fn16, stream_), "adaln"); });
-  G("gemm.final_linear", w->g_fin, 512);
-  G("gemm.conv2", w->g_c2, 512);
+  G("gemm.out", w->g_out, 512, 512.0 * 512 + 80.0 * 512);  // final linear, then conv2
   if (do_update) {
     P.run("euler", 0.0, static_cast<double>(w->B) * T * 80 * 4.0 * (w->br + 2), [&] {
       check(euler_run(w->X, w->vel, w->XD, w->plen, w->B, w->T, w->br, dt, cfg, stream_), "euler");

@@ -56,14 +56,12 @@ struct Work {
   float* h = nullptr;
   __half* g16 = nullptr;
   // post + wavenet + final
-  __half* ls16 = nullptr;
   __half* xp16 = nullptr;  // [S*(T+4), 512]
   float* res = nullptr;
   __half* gate16 = nullptr;
   float* wacc = nullptr;
   float* fin = nullptr;
   __half* fn16 = nullptr;
-  __half* fh16 = nullptr;
   float* vel = nullptr;  // [R, 80]
   float2* rope = nullptr;
   CUtensorMap tm_attn;  // qkv16 viewed for the attention kernel
@@ -71,7 +69,7 @@ struct Work {
   size_t arena_bytes = 0;
   // prebuilt GEMM launches
   GemmLaunch g_cp, g_base, g_merge, g_qkv[kLayers], g_wo[kLayers], g_w13[kLayers], g_w2[kLayers],
-      g_skip[kLayers], g_sl, g_c1res, g_in[kWnLayers], g_rs[kWnLayers], g_fin, g_c2;
+      g_skip[kLayers], g_post, g_in[kWnLayers], g_rs[kWnLayers], g_out;
   // captured sampler graphs keyed by (steps, cfg bits)
   std::map<std::pair<int, uint32_t>, cudaGraphExec_t> graphs;
   std::map<std::pair<int, uint32_t>, int> graph_kernels;  // kernel nodes per captured graph

@@ -231,24 +231,39 @@ void load_weights(const Mit2Bundle& b, DevWeights* w) {
   pk.add(f32(b, P("transformer.norm.norm.weight"), 512), &w->g_norm);
   pk.add(h16(b, P("transformer.norm.project_layer.weight"), 1024 * 512), reinterpret_cast<uint16_t**>(&w->proj_norm));
   pk.add(f32(b, P("transformer.norm.project_layer.bias"), 1024), &w->projb_norm);
-  // Post-transformer projections.
+  // Post-transformer projections: skip_linear (592 -> 512) feeds conv1 and
+  // res_projection (512 -> 512 each) with no operation between them
+  // (run_dit_post_transformer_proj_cpu, runtime/impl/dit_cfm_bigvgan.cpp:
+  // 1053-1079), so the three are one 592 -> 1024 linear map.
   {
+    const auto sl = b.as_f32(P("skip_linear.weight"));  // [512][592]
+    const auto bsl = f32(b, P("skip_linear.bias"), 512);
+    auto c1 = b.as_f32(P("conv1.weight"));  // [512][512(,1)]
+    const auto rp = b.as_f32(P("res_projection.weight"));
+    if (sl.size() != 512u * 592 || c1.size() != 512u * 512 || rp.size() != 512u * 512)
+      throw std::runtime_error("bundle: post-transformer projection shapes");
+    c1.insert(c1.end(), rp.begin(), rp.end());  // [1024][512]
+    auto bc = f32(b, P("conv1.bias"), 512);
+    const auto br = f32(b, P("res_projection.bias"), 512);
+    bc.insert(bc.end(), br.begin(), br.end());
+    std::vector<float> wp(1024 * 592, 0.0f);
+    for (int o = 0; o < 1024; ++o) {
+      float* dst = &wp[static_cast<size_t>(o) * 592];
+      double bias = bc[o];
+      for (int j = 0; j < 512; ++j) {
+        const float a = c1[static_cast<size_t>(o) * 512 + j];
+        const float* src = &sl[static_cast<size_t>(j) * 592];
+        for (int k = 0; k < 592; ++k) dst[k] += a * src[k];
+        bias += static_cast<double>(a) * bsl[j];
+      }
+      bc[o] = static_cast<float>(bias);
+    }
     // [x_normed (512) | x_mel (80 -> kXdLd, zero-padded)]
-    auto sl = h16(b, P("skip_linear.weight"), 512 * 592);
-    std::vector<uint16_t> slp(512 * (512 + kXdLd), 0);
-    for (int r = 0; r < 512; ++r) std::memcpy(&slp[r * (512 + kXdLd)], &sl[r * 592], 592 * 2);
-    pk.add(std::move(slp), reinterpret_cast<uint16_t**>(&w->wsl));
-  }
-  pk.add(f32(b, P("skip_linear.bias"), 512), &w->bsl);
-  {
-    auto c1 = h16(b, P("conv1.weight"), 512 * 512);
-    auto rp = h16(b, P("res_projection.weight"), 512 * 512);
-    c1.insert(c1.end(), rp.begin(), rp.end());
-    pk.add(std::move(c1), reinterpret_cast<uint16_t**>(&w->wc1res));
-    auto b1 = f32(b, P("conv1.bias"), 512);
-    auto br = f32(b, P("res_projection.bias"), 512);
-    b1.insert(b1.end(), br.begin(), br.end());
-    pk.add(std::move(b1), &w->bc1res);
+    const auto wh = to_h(wp);
+    std::vector<uint16_t> padded(1024 * (512 + kXdLd), 0);
+    for (int o = 0; o < 1024; ++o) std::memcpy(&padded[o * (512 + kXdLd)], &wh[o * 592], 592 * 2);
+    pk.add(std::move(padded), reinterpret_cast<uint16_t**>(&w->wpost));
+    pk.add(std::move(bc), &w->bpost);
   }
   // WaveNet.
   {
@@ -280,10 +295,30 @@ void load_weights(const Mit2Bundle& b, DevWeights* w) {
   // Final layer.
   pk.add(h16(b, P("final_layer.adaLN_modulation.1.weight"), 1024 * 512), reinterpret_cast<uint16_t**>(&w->ada_w));
   pk.add(f32(b, P("final_layer.adaLN_modulation.1.bias"), 1024), &w->ada_b);
-  pk.add(to_h(weight_norm(b, P("final_layer.linear"), 512, 512)), reinterpret_cast<uint16_t**>(&w->wfin));
-  pk.add(f32(b, P("final_layer.linear.bias"), 512), &w->bfin);
-  pk.add(h16(b, P("conv2.weight"), 80 * 512), reinterpret_cast<uint16_t**>(&w->wc2));
-  pk.add(f32(b, P("conv2.bias"), 80), &w->bc2);
+  // final_layer.linear (512 -> 512, weight-normed) then conv2 (1x1, 512 -> 80)
+  // with nothing between them (run_dit_final_layer_cpu, :1172-1199, and the
+  // conv2 that follows it): one 512 -> 80 linear map.
+  {
+    const auto fl = weight_norm(b, P("final_layer.linear"), 512, 512);
+    const auto bfl = f32(b, P("final_layer.linear.bias"), 512);
+    const auto c2 = b.as_f32(P("conv2.weight"));  // [80][512(,1)]
+    if (c2.size() != 80u * 512) throw std::runtime_error("bundle: conv2 shape");
+    auto bo = f32(b, P("conv2.bias"), 80);
+    std::vector<float> wo(80 * 512, 0.0f);
+    for (int o = 0; o < 80; ++o) {
+      double bias = bo[o];
+      for (int j = 0; j < 512; ++j) {
+        const float a = c2[static_cast<size_t>(o) * 512 + j];
+        const float* src = &fl[static_cast<size_t>(j) * 512];
+        float* dst = &wo[static_cast<size_t>(o) * 512];
+        for (int k = 0; k < 512; ++k) dst[k] += a * src[k];
+        bias += static_cast<double>(a) * bfl[j];
+      }
+      bo[o] = static_cast<float>(bias);
+    }
+    pk.add(to_h(wo), reinterpret_cast<uint16_t**>(&w->wout));
+    pk.add(std::move(bo), &w->bout);
+  }
 
   pk.upload(w);
 }

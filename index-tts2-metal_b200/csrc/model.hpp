@@ -6,8 +6,10 @@
 //   - w1/w3, WaveNet in_layers and res_skip_layers rows interleaved in 64-row
 //     groups [a | b] for the paired GEMM epilogues;
 //   - WaveNet k=5 conv weights permuted from [out][in][k] to [out][k][in];
-//   - conv1 and res_projection stacked into one 1024-row matrix;
-//   - the merge weight split into its x slice [512][80] and the rest [512][784].
+//   - the merge weight split into its x slice [512][80] and the rest [512][784];
+//   - linear layers with nothing between them composed into one matrix (in
+//     fp32, then rounded to f16 once): [conv1 ; res_projection] . skip_linear
+//     (592 -> 1024) and conv2 . final_layer.linear (512 -> 80).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -67,18 +69,14 @@ struct DevWeights {
   __half* wx = nullptr;     // cond_x_merge_linear x slice [512][kXdLd] (zero-padded)
   __half* wrest = nullptr;  // remaining merge columns [512][kUld] (zero-padded)
   float* bm = nullptr;
-  __half* wsl = nullptr;  // skip_linear [512][512 + kXdLd] (zero-padded)
-  float* bsl = nullptr;
-  __half* wc1res = nullptr;  // [conv1 ; res_projection] [1024][512]
-  float* bc1res = nullptr;
+  __half* wpost = nullptr;  // [conv1 ; res_projection] . skip_linear: [1024][512 + kXdLd] (x_mel columns zero-padded)
+  float* bpost = nullptr;   // [1024] [conv1 ; res_projection] . skip_linear.bias + [conv1.bias ; res_projection.bias]
   __half* win[kWnLayers] = {};  // [1024][2560] paired, tap-major K
   float* bin[kWnLayers] = {};
   __half* wrs[kWnLayers] = {};  // [1024][512] paired (l < 7), [512][512] (l = 7)
   float* brs[kWnLayers] = {};
-  __half* wfin = nullptr;  // final_layer.linear (weight-normed) [512][512]
-  float* bfin = nullptr;
-  __half* wc2 = nullptr;  // conv2 [80][512]
-  float* bc2 = nullptr;
+  __half* wout = nullptr;  // conv2 . final_layer.linear (weight-normed): [80][512]
+  float* bout = nullptr;   // [80] conv2 . final_layer.linear.bias + conv2.bias
   __half* ada_w = nullptr;  // final_layer.adaLN_modulation.1 [1024][512]
   float* ada_b = nullptr;
   float* wcond = nullptr;  // wavenet.cond_layer (weight-normed) [8192][512] fp32
