@@ -113,24 +113,39 @@ __global__ void __launch_bounds__(256) adaln_kernel(const float* __restrict__ x,
 __global__ void euler_kernel(float* __restrict__ X, const float* __restrict__ V, __half* __restrict__ XD,
                              const int* __restrict__ prompt_len, int B, int T, int branches, float dt, float cfg) {
   pdl_entry();
-  const size_t total = static_cast<size_t>(B) * T * 80;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int c = static_cast<int>(i % 80);
-    const size_t ut = i / 80;
-    const int u = static_cast<int>(ut / T);
-    const int t = static_cast<int>(ut - static_cast<size_t>(u) * T);
+  // One thread per 4 consecutive mel bins of a frame (20 per 80-bin row).
+  const size_t total = static_cast<size_t>(B) * T * 20;
+  for (size_t q = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; q < total;
+       q += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t f = q / 20;  // frame index u * T + t
+    const int c4 = static_cast<int>(q - f * 20);
+    const int u = static_cast<int>(f / static_cast<size_t>(T));
+    const int t = static_cast<int>(f - static_cast<size_t>(u) * T);
     const size_t cond_row = (static_cast<size_t>(u) * branches) * T + t;
-    float v = V[cond_row * 80 + c];
+    float4 v = reinterpret_cast<const float4*>(V + cond_row * 80)[c4];
     if (branches == 2) {
-      const float vu = V[(cond_row + T) * 80 + c];
-      v = (1.0f + cfg) * v - cfg * vu;
+      const float4 vu = reinterpret_cast<const float4*>(V + (cond_row + T) * 80)[c4];
+      v.x = (1.0f + cfg) * v.x - cfg * vu.x;
+      v.y = (1.0f + cfg) * v.y - cfg * vu.y;
+      v.z = (1.0f + cfg) * v.z - cfg * vu.z;
+      v.w = (1.0f + cfg) * v.w - cfg * vu.w;
     }
-    float x = X[i] + dt * v;
-    if (t < prompt_len[u]) x = 0.0f;
-    X[i] = x;
-    const __half xh = __float2half_rn(x);
-    for (int b = 0; b < branches; ++b) XD[(cond_row + static_cast<size_t>(b) * T) * kXdLd + c] = xh;
+    float4* xp = reinterpret_cast<float4*>(X + f * 80) + c4;
+    float4 x = *xp;
+    x.x += dt * v.x;
+    x.y += dt * v.y;
+    x.z += dt * v.z;
+    x.w += dt * v.w;
+    if (t < prompt_len[u]) x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    *xp = x;
+    union {
+      __half2 h[2];
+      uint2 u2;
+    } pk;
+    pk.h[0] = __floats2half2_rn(x.x, x.y);
+    pk.h[1] = __floats2half2_rn(x.z, x.w);
+    for (int b = 0; b < branches; ++b)
+      *reinterpret_cast<uint2*>(XD + (cond_row + static_cast<size_t>(b) * T) * kXdLd + c4 * 4) = pk.u2;
   }
 }
 
@@ -266,7 +281,7 @@ cudaError_t adaln_run(const float* x, int R, const float* ss, __half* out, cudaS
 
 cudaError_t euler_run(float* X, const float* V, __half* XD, const int* prompt_len, int B, int T, int branches,
                       float dt, float cfg, cudaStream_t st) {
-  const size_t n = static_cast<size_t>(B) * T * 80;
+  const size_t n = static_cast<size_t>(B) * T * 20;
   return launch_pdl(euler_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, X, V, XD, prompt_len, B, T, branches, dt,
                     cfg);
 }
