@@ -4,7 +4,9 @@
 // 128-query tiles) round-robin. The two query tiles of an item share every
 // K/V block, and each tile has its own MMA issuer, so the tensor core works
 // for one tile while the other tile's softmax warps compute. When pairs would
-// leave SMs idle (one short utterance), an item is one query tile instead.
+// leave SMs idle (one short utterance), an item is one query tile instead and
+// both softmax warp groups work on it, each on half of every key block (own
+// running maximum, row sum and O), merging through shared memory at the end.
 // The softmax warps are bound by the special-function unit: one ex2 per
 // score, issued at about one warp instruction per 14 cycles per SM
 // sub-partition on B200 (measured); polynomial exponentials on the FMA pipe
@@ -60,8 +62,11 @@ constexpr int OFF_K = 2 * 16384;                         // kKV stages x 16 KB
 constexpr int OFF_V = OFF_K + kKV * 16384;               // kKV stages x 16 KB
 constexpr int OFF_BIAS = OFF_V + kKV * 16384;            // kKV x 128 floats
 constexpr int OFF_FLAG = OFF_BIAS + kKV * kKB * 4;       // kKV ints: block has no masked key
-constexpr int OFF_BAR = OFF_FLAG + kKV * 4;
-constexpr int kBars = 2 * 7 + 2 * kKV;  // per tile: q_full, q_empty, s_full, s_free, p_full, o_done, o_free; kv ring
+constexpr int OFF_XCH = OFF_FLAG + kKV * 4;         // key-split merge: [128 rows][64 dims + m + l] floats
+constexpr int kXchLd = 66;
+constexpr int OFF_BAR = OFF_XCH + 128 * kXchLd * 4;
+// per tile: q_full, q_empty, s_full, s_free, p_full, o_done, o_free; the kv ring; x_full, x_empty
+constexpr int kBars = 2 * 7 + 2 * kKV + 2;
 constexpr int SMEM_A = 1024 + OFF_BAR + kBars * 8 + 16;
 constexpr uint32_t TMEM_S = 0;    // + 128 * tile
 constexpr uint32_t TMEM_P = 256;  // + 64 * tile
@@ -119,45 +124,258 @@ __device__ __forceinline__ int item_tiles(const Item& I, int T, int tpi) {
   return (tpi == 2 && I.q0 + kQ < T) ? 2 : 1;
 }
 
+// Shared state of the kernel's roles (shared-memory and TMEM addresses,
+// barriers, the launch's shape).
+struct AttnCtx {
+  uint8_t* sm;
+  uint64_t *q_full, *q_empty, *s_full, *s_free, *p_full, *o_done, *o_free, *kv_full, *kv_empty, *x_full, *x_empty;
+  float* bias;
+  int* full_block;
+  uint32_t tmem;
+  __half* out;
+  unsigned int* status;
+  int T, nkb, items, units, tpi;
+};
+
+// Softmax + epilogue of one warp group (4 warps, one query row per thread).
+// NK = 128: the group owns query tile `wg` of pair items and all 128 keys of
+// every block. NK = 64 (single-tile items): both groups work on the item's
+// one tile, group `wg` on keys [64 wg, 64 wg + 64) of every block, each with
+// its own running maximum, row sum and O accumulator; at the end of the item
+// group 1 hands (O, m, l) to group 0 through shared memory, which merges the
+// halves and stores the rows.
+template <int NK>
+__device__ __forceinline__ void softmax_role(const AttnCtx& c, int wg, int quarter, int lane) {
+  constexpr bool kSplit = NK == 64;
+  const int row = quarter * 32 + lane;
+  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  const int sidx = kSplit ? 0 : wg;  // S region / barriers this group reads
+  const int kofs = kSplit ? 64 * wg : 0;  // first key of the group's share of a block
+  const uint32_t t_s = c.tmem + lane_off + TMEM_S + sidx * 128 + kofs;
+  const uint32_t t_p = c.tmem + lane_off + TMEM_P + wg * 64;
+  const uint32_t t_o = c.tmem + lane_off + TMEM_O + wg * 64;
+  const float kLog2e = 1.4426950408889634f;
+  const float kLazy = 8.0f / kLog2e;
+  float* xch = reinterpret_cast<float*>(c.sm + OFF_XCH) + row * kXchLd;
+  int g = 0;     // running K/V block count (mask rows)
+  int nblk = 0;  // running block count of this group (phase of s_full / p_full / o_done)
+  int nitem = 0;  // items this group has worked on (phase of the merge barriers)
+  bool ok = true;
+  for (int it = blockIdx.x; it < c.items && ok; it += gridDim.x) {
+    const Item I = item_at(it, c.units, c.tpi);
+    if (!kSplit && wg >= item_tiles(I, c.T, c.tpi)) {
+      g += c.nkb;
+      continue;
+    }
+    float m = -CUDART_INF_F;  // reference maximum of O and l
+    float l = 0.0f;           // row sum of P relative to m
+    for (int j = 0; j < c.nkb && ok; ++j) {
+      const int b = nblk + j;
+      if (!(ok = mbar_wait(&c.s_full[sidx], b & 1, c.status, kDevTimeoutAttn))) break;
+      [[maybe_unused]] const bool tr = row == 0 && nblk == 0 && j < 8;
+      ATTN_TRACE(tr, 84 + wg * 16 + j);
+      tc_fence_after();
+      uint32_t sr[NK];
+#pragma unroll
+      for (int q = 0; q < NK / 32; ++q) tmem_ld32_async(t_s + q * 32, sr + q * 32);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < NK / 32; ++q) reg_fence32(sr + q * 32);
+      ATTN_TRACE(tr, 116 + wg * 16 + j);
+      // S is in registers: the next block's S may overwrite it.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c.s_free[sidx]);
+      // The mask row of this block was published with kv_full (already complete).
+      const int kst = (g + j) % kKV;
+      if (!(ok = mbar_wait(&c.kv_full[kst], ((g + j) / kKV) & 1, c.status, kDevTimeoutAttn))) break;
+      if (!c.full_block[kst]) {
+        const float* brow = c.bias + kst * kKB + kofs;
+#pragma unroll
+        for (int k = 0; k < NK; ++k) sr[k] = __float_as_uint(__uint_as_float(sr[k]) + brow[k]);
+      }
+      float mp[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        mp[e] = fmax3(__uint_as_float(sr[e]), __uint_as_float(sr[4 + e]), __uint_as_float(sr[8 + e]));
+#pragma unroll
+      for (int k = 12; k < NK - 4; k += 8) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mp[e] = fmax3(mp[e], __uint_as_float(sr[k + e]), __uint_as_float(sr[k + 4 + e]));
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mp[e] = fmaxf(mp[e], __uint_as_float(sr[NK - 4 + e]));
+      const float mb = fmaxf(fmax3(mp[0], mp[1], mp[2]), mp[3]);
+      // The first live key, or a maximum grown past 2^8: move the reference
+      // maximum to this block's; O and l are rescaled below.
+      float alpha = 1.0f;
+      bool rescale = false;
+      if (mb > m + kLazy) {
+        if (m != -CUDART_INF_F) {
+          alpha = ex2_approx((m - mb) * kLog2e);
+          rescale = true;
+        }
+        m = mb;
+      }
+      // P(j - 1) must have been read by its O MMA before it is overwritten
+      // (and O is final for the rescale below).
+      if (j > 0 && !(ok = mbar_wait(&c.o_done[wg], (b - 1) & 1, c.status, kDevTimeoutAttn))) break;
+      tc_fence_after();
+      const float nref = (m == -CUDART_INF_F) ? 0.0f : -m * kLog2e;
+      float ls[2] = {0.0f, 0.0f};
+#pragma unroll
+      for (int q = 0; q < NK / 16; ++q) {  // chunks of 16 keys -> 8 columns of f16 pairs
+        uint32_t pw[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float y0 = ex2_approx(fmaf(__uint_as_float(sr[q * 16 + 2 * e]), kLog2e, nref));
+          const float y1 = ex2_approx(fmaf(__uint_as_float(sr[q * 16 + 2 * e + 1]), kLog2e, nref));
+          ls[e & 1] += y0 + y1;
+          pw[e] = pack_f16(y0, y1);
+        }
+        tmem_st8(t_p + q * 8, pw);
+      }
+      l = l * alpha + (ls[0] + ls[1]);
+      if (rescale) {
+#pragma unroll 1
+        for (int q = 0; q < 2; ++q) {
+          uint32_t ov[32];
+          tmem_ld32_async(t_o + q * 32, ov);
+          tmem_wait_ld();
+          reg_fence32(ov);
+#pragma unroll
+          for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+          tmem_st32(t_o + q * 32, ov);
+        }
+      }
+      tmem_wait_st();
+      ATTN_TRACE(tr, 148 + wg * 16 + j);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c.p_full[wg]);
+    }
+    if (!ok) break;
+    // Epilogue: the item's last O MMA of this group, then O / l for the row.
+    if (!(ok = mbar_wait(&c.o_done[wg], (nblk + c.nkb - 1) & 1, c.status, kDevTimeoutAttn))) break;
+    ATTN_TRACE(row == 0 && nblk == 0, 182 + wg);
+    tc_fence_after();
+    uint32_t ov[64];
+    tmem_ld32_async(t_o, ov);
+    tmem_ld32_async(t_o + 32, ov + 32);
+    tmem_wait_ld();
+    reg_fence32(ov);
+    reg_fence32(ov + 32);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&c.o_free[wg]);  // O may take the next item's first MMA
+    float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    bool store = true;
+    if constexpr (kSplit) {
+      // Merge the key halves: group 1 publishes (O, m, l), group 0 combines.
+      if (wg == 1) {
+        if (nitem > 0 && !(ok = mbar_wait(c.x_empty, (nitem - 1) & 1, c.status, kDevTimeoutAttn))) break;
+#pragma unroll
+        for (int d = 0; d < 64; ++d) xch[d] = __uint_as_float(ov[d]);
+        xch[64] = m;
+        xch[65] = l;
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(c.x_full);
+        store = false;
+      } else {
+        if (!(ok = mbar_wait(c.x_full, nitem & 1, c.status, kDevTimeoutAttn))) break;
+        const float mo = xch[64], lo = xch[65];
+        const float mm = fmaxf(m, mo);
+        const float as = (m == -CUDART_INF_F) ? 0.0f : ex2_approx((m - mm) * kLog2e);
+        const float ao = (mo == -CUDART_INF_F) ? 0.0f : ex2_approx((mo - mm) * kLog2e);
+        const float lsum = l * as + lo * ao;
+        const float r = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+#pragma unroll
+        for (int d = 0; d < 64; ++d) ov[d] = __float_as_uint((__uint_as_float(ov[d]) * as + xch[d] * ao) * r);
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(c.x_empty);
+        inv = 1.0f;
+      }
+    }
+    const int q = I.q0 + (kSplit ? 0 : wg * kQ) + row;
+    if (store && q < c.T) {
+      uint4* dst = reinterpret_cast<uint4*>(c.out + (static_cast<size_t>(I.s) * c.T + q) * 512 + I.h * 64);
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        union {
+          __half2 h2[4];
+          uint4 u;
+        } pk;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          pk.h2[e] = __floats2half2_rn(__uint_as_float(ov[cc * 8 + 2 * e]) * inv,
+                                       __uint_as_float(ov[cc * 8 + 2 * e + 1]) * inv);
+        dst[cc] = pk.u;
+      }
+    }
+    ATTN_TRACE(row == 0 && nblk == 0, 184 + wg);
+    nblk += c.nkb;
+    g += c.nkb;
+    ++nitem;
+  }
+}
+
 __global__ void __launch_bounds__(kThreadsA, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const float* __restrict__ row_mask, __half* __restrict__ out,
                    int S, int T, int tpi, unsigned int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* q_full = bars;              // [2] Q tile t landed
-  uint64_t* q_empty = q_full + 2;       // [2] the item's last S_t MMA is done (Q_t may be replaced)
-  uint64_t* s_full = q_empty + 2;       // [2] S_t of the current block landed
-  uint64_t* s_free = s_full + 2;        // [2] the tile's softmax warps have read S_t into registers
-  uint64_t* p_full = s_free + 2;        // [2] P_t written by the tile's softmax warps
-  uint64_t* o_done = p_full + 2;        // [2] O_t MMA of the current block done (P_t may be rewritten)
-  uint64_t* o_free = o_done + 2;        // [2] O_t of the finished item read out by the softmax warps
-  uint64_t* kv_full = o_free + 2;       // [kKV] K/V block landed and its mask row written
-  uint64_t* kv_empty = kv_full + kKV;   // [kKV] both tiles' O MMAs of the block are done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kv_empty + kKV);
-  float* bias = reinterpret_cast<float*>(sm + OFF_BIAS);
-  int* full_block = reinterpret_cast<int*>(sm + OFF_FLAG);
+  AttnCtx c;
+  c.sm = sm;
+  c.q_full = bars;              // [2] Q tile t landed
+  c.q_empty = c.q_full + 2;     // [2] the item's last S_t MMA is done (Q_t may be replaced)
+  c.s_full = c.q_empty + 2;     // [2] S_t of the current block landed
+  c.s_free = c.s_full + 2;      // [2] the softmax warps reading S_t have read it into registers
+  c.p_full = c.s_free + 2;      // [2] P of warp group t written
+  c.o_done = c.p_full + 2;      // [2] O MMA of warp group t for the current block done (its P may be rewritten)
+  c.o_free = c.o_done + 2;      // [2] O of warp group t read out at the end of an item
+  c.kv_full = c.o_free + 2;     // [kKV] K/V block landed and its mask row written
+  c.kv_empty = c.kv_full + kKV; // [kKV] both O MMAs of the block are done
+  c.x_full = c.kv_empty + kKV;  // key-split merge: group 1's (O, m, l) published
+  c.x_empty = c.x_full + 1;     // key-split merge: group 0 has read them
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c.x_empty + 1);
+  c.bias = reinterpret_cast<float*>(sm + OFF_BIAS);
+  c.full_block = reinterpret_cast<int*>(sm + OFF_FLAG);
+  c.out = out;
+  c.status = status;
+  c.T = T;
+  c.tpi = tpi;
+  c.nkb = (T + kKB - 1) / kKB;
+  const int tiles = (T + kQ - 1) / kQ;
+  c.units = (tiles + tpi - 1) / tpi;  // work items per (sequence, head)
+  c.items = S * 8 * c.units;
+  const bool split = tpi == 1;  // single-tile items: both warp groups share the tile's keys
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nkb = (T + kKB - 1) / kKB;
-  const int tiles = (T + kQ - 1) / kQ;
-  const int units = (tiles + tpi - 1) / tpi;  // work items per (sequence, head)
-  const int items = S * 8 * units;
+  const int nkb = c.nkb, items = c.items, units = c.units;
+  uint64_t *q_full = c.q_full, *q_empty = c.q_empty, *s_full = c.s_full, *s_free = c.s_free, *p_full = c.p_full,
+           *o_done = c.o_done, *o_free = c.o_free, *kv_full = c.kv_full, *kv_empty = c.kv_empty;
+  float* bias = c.bias;
+  int* full_block = c.full_block;
 
   if (warp == 0 && lane == 0) {
     for (int t = 0; t < 2; ++t) {
       mbar_init(&q_full[t], 1);
       mbar_init(&q_empty[t], 1);
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], kSoftWarps);
+      mbar_init(&s_free[t], (split && t == 0) ? 2 * kSoftWarps : kSoftWarps);
       mbar_init(&p_full[t], kSoftWarps);
       mbar_init(&o_done[t], 1);
       mbar_init(&o_free[t], kSoftWarps);
     }
     for (int i = 0; i < kKV; ++i) {
       mbar_init(&kv_full[i], 1 + 32);  // producer expect_tx + 32 lanes writing the mask row
-      mbar_init(&kv_empty[i], 2);      // one commit per query tile (the only tile commits twice)
+      mbar_init(&kv_empty[i], 2);      // one commit per issuer (the only issuer of a block commits twice)
     }
+    mbar_init(c.x_full, kSoftWarps);
+    mbar_init(c.x_empty, kSoftWarps);
     fence_barrier_init();
     fence_proxy_async_shared();
     prefetch_tmap(&tm);
@@ -170,6 +388,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  c.tmem = tmem;
   griddep_wait();
   griddep_launch();
   ATTN_TRACE(threadIdx.x == 0, 180);
@@ -219,15 +438,19 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       }
     }
   } else if (warp == 1 || warp == kIssuer1) {
-    // ---- MMA issuer of query tile t ----
+    // ---- MMA issuer t: S and O of query tile t (pairs), or, for single-tile
+    // items, S and O of key half 0 (t = 0) / O of key half 1 (t = 1) ----
     const int t = warp == 1 ? 0 : 1;
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(128, kKB);
       constexpr uint32_t idesc_o = idesc_f16_f32(128, 64) | (1u << 16);  // B (V) MN-major
       const uint32_t sq = smem_u32(sm + OFF_Q + t * 16384);
+      const bool issues_s = !split || t == 0;
+      const int o_steps = split ? 4 : 8;                // K16 steps of the O MMA (64 or 128 keys)
+      const uint32_t v_off = split ? t * 8192 : 0;       // the key rows of V this issuer's O reads
       int g = 0;     // running K/V block count
-      int nblk = 0;  // running block count of this tile (phase of s_full / s_free / p_full / o_done)
-      int nq = 0;    // items so far in which this tile was active (phase of q_full / o_free)
+      int nblk = 0;  // running block count of this issuer (phase of s_full / s_free / p_full / o_done)
+      int nq = 0;    // items so far in which this issuer was active (phase of q_full / o_free)
       int s_trace = 0;  // S MMAs issued (trace slots of the first item)
       bool ok = true;
       // S_t = Q_t K_block^T.
@@ -244,22 +467,24 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         const Item I = item_at(it, units, tpi);
         const int nt = item_tiles(I, T, tpi);
-        if (t >= nt) {  // this tile is past the end of the sequence for the item
+        if (!split && t >= nt) {  // this tile is past the end of the sequence for the item
           g += nkb;
           continue;
         }
-        // S_t(0): Q_t and K/V block 0 landed, and the softmax warps have read
-        // the previous item's last S_t.
-        if (!(ok = mbar_wait(&q_full[t], nq & 1, status, kDevTimeoutAttn))) break;
-        if (!(ok = mbar_wait(&kv_full[g % kKV], (g / kKV) & 1, status, kDevTimeoutAttn))) break;
-        if (nblk > 0 && !(ok = mbar_wait(&s_free[t], (nblk - 1) & 1, status, kDevTimeoutAttn))) break;
-        tc_fence_after();
-        issue_s(g % kKV);
-        if (nkb == 1) umma_commit(&q_empty[t]);
+        if (issues_s) {
+          // S_t(0): Q_t and K/V block 0 landed, and the softmax warps have read
+          // the previous item's last S_t.
+          if (!(ok = mbar_wait(&q_full[t], nq & 1, status, kDevTimeoutAttn))) break;
+          if (!(ok = mbar_wait(&kv_full[g % kKV], (g / kKV) & 1, status, kDevTimeoutAttn))) break;
+          if (nblk > 0 && !(ok = mbar_wait(&s_free[t], (nblk - 1) & 1, status, kDevTimeoutAttn))) break;
+          tc_fence_after();
+          issue_s(g % kKV);
+          if (nkb == 1) umma_commit(&q_empty[t]);
+        }
         for (int j = 0; j < nkb && ok; ++j) {
           const int b = nblk + j;
           const int st = (g + j) % kKV;
-          if (j + 1 < nkb) {
+          if (issues_s && j + 1 < nkb) {
             // S_t(j+1) as soon as K/V block j+1 landed and S_t(j) has been read out.
             const int gn = g + j + 1;
             if (!(ok = mbar_wait(&kv_full[gn % kKV], (gn / kKV) & 1, status, kDevTimeoutAttn))) break;
@@ -268,20 +493,19 @@ __global__ void __launch_bounds__(kThreadsA, 1)
             issue_s(gn % kKV);
             if (j + 2 == nkb) umma_commit(&q_empty[t]);
           }
-          // O_t (+)= P_t(j) V(j) once P_t(j) is written (and, for the item's
-          // first block, the previous item's O_t has been read out).
+          // O (+)= P(j) V(j) once P(j) is written (and, for the item's first
+          // block, the previous item's O has been read out).
           if (!(ok = mbar_wait(&p_full[t], b & 1, status, kDevTimeoutAttn))) break;
           if (j == 0 && nq > 0 && !(ok = mbar_wait(&o_free[t], (nq - 1) & 1, status, kDevTimeoutAttn))) break;
           tc_fence_after();
           ATTN_TRACE(nq == 0 && j < 8, 52 + t * 16 + j);
-          const uint32_t sv = smem_u32(sm + OFF_V + st * 16384);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
+          const uint32_t sv = smem_u32(sm + OFF_V + st * 16384) + v_off;
+          for (int kk = 0; kk < o_steps; ++kk)
             umma_f16_ts(tmem + TMEM_O + t * 64, tmem + TMEM_P + t * 64 + kk * 8, sdesc_mn_sw128(sv + kk * 2048),
                         idesc_o, (j != 0 || kk != 0) ? 1u : 0u);
           umma_commit(&o_done[t]);
           umma_commit(&kv_empty[st]);
-          if (nt == 1) umma_commit(&kv_empty[st]);  // the absent tile's share of the stage release
+          if (!split && nt == 1) umma_commit(&kv_empty[st]);  // the absent tile's share of the stage release
         }
         nblk += nkb;
         ++nq;
@@ -290,146 +514,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     }
     __syncwarp();
   } else {
-    // ---- softmax + epilogue: warps 2..5 tile 0, warps 6..9 tile 1 ----
-    const int t = (warp - 2) / kSoftWarps;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t t_s = tmem + lane_off + TMEM_S + t * 128;
-    const uint32_t t_p = tmem + lane_off + TMEM_P + t * 64;
-    const uint32_t t_o = tmem + lane_off + TMEM_O + t * 64;
-    const float kLog2e = 1.4426950408889634f;
-    const float kLazy = 8.0f / kLog2e;
-    int g = 0;     // running K/V block count (mask rows)
-    int nblk = 0;  // running block count of this tile
-    bool ok = true;
-    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-      const Item I = item_at(it, units, tpi);
-      if (t >= item_tiles(I, T, tpi)) {
-        g += nkb;
-        continue;
-      }
-      float m = -CUDART_INF_F;  // reference maximum of O_t and l
-      float l = 0.0f;           // row sum of P relative to m
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int b = nblk + j;
-        if (!(ok = mbar_wait(&s_full[t], b & 1, status, kDevTimeoutAttn))) break;
-        const bool tr = row == 0 && nblk == 0 && j < 8;
-        ATTN_TRACE(tr, 84 + t * 16 + j);
-        tc_fence_after();
-        uint32_t sr[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32_async(t_s + c * 32, sr + c * 32);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) reg_fence32(sr + c * 32);
-        ATTN_TRACE(tr, 116 + t * 16 + j);
-        // S_t is in registers: the next block's S may overwrite it.
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[t]);
-        // The mask row of this block was published with kv_full (already complete).
-        const int kst = (g + j) % kKV;
-        if (!(ok = mbar_wait(&kv_full[kst], ((g + j) / kKV) & 1, status, kDevTimeoutAttn))) break;
-        if (!full_block[kst]) {
-          const float* brow = bias + kst * kKB;
-#pragma unroll
-          for (int k = 0; k < 128; ++k) sr[k] = __float_as_uint(__uint_as_float(sr[k]) + brow[k]);
-        }
-        float mp[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          mp[e] = fmax3(__uint_as_float(sr[e]), __uint_as_float(sr[4 + e]), __uint_as_float(sr[8 + e]));
-#pragma unroll
-        for (int k = 12; k < 124; k += 8) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) mp[e] = fmax3(mp[e], __uint_as_float(sr[k + e]), __uint_as_float(sr[k + 4 + e]));
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) mp[e] = fmaxf(mp[e], __uint_as_float(sr[124 + e]));
-        const float mb = fmaxf(fmax3(mp[0], mp[1], mp[2]), mp[3]);
-        // The first live key, or a maximum grown past 2^8: move the reference
-        // maximum to this block's; O_t and l are rescaled below.
-        float alpha = 1.0f;
-        bool rescale = false;
-        if (mb > m + kLazy) {
-          if (m != -CUDART_INF_F) {
-            alpha = ex2_approx((m - mb) * kLog2e);
-            rescale = true;
-          }
-          m = mb;
-        }
-        // P_t(j - 1) must have been read by its O MMA before it is overwritten
-        // (and O_t is final for the rescale below).
-        if (j > 0 && !(ok = mbar_wait(&o_done[t], (b - 1) & 1, status, kDevTimeoutAttn))) break;
-        tc_fence_after();
-        const float nref = (m == -CUDART_INF_F) ? 0.0f : -m * kLog2e;
-        float ls[2] = {0.0f, 0.0f};
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {  // 8 chunks of 16 keys -> 8 columns of f16 pairs
-          uint32_t pw[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float y0 = ex2_approx(fmaf(__uint_as_float(sr[c * 16 + 2 * e]), kLog2e, nref));
-            const float y1 = ex2_approx(fmaf(__uint_as_float(sr[c * 16 + 2 * e + 1]), kLog2e, nref));
-            ls[e & 1] += y0 + y1;
-            pw[e] = pack_f16(y0, y1);
-          }
-          tmem_st8(t_p + c * 8, pw);
-        }
-        l = l * alpha + (ls[0] + ls[1]);
-        if (rescale) {
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t ov[32];
-            tmem_ld32_async(t_o + c * 32, ov);
-            tmem_wait_ld();
-            reg_fence32(ov);
-#pragma unroll
-            for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
-            tmem_st32(t_o + c * 32, ov);
-          }
-        }
-        tmem_wait_st();
-        ATTN_TRACE(tr, 148 + t * 16 + j);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t]);
-      }
-      if (!ok) break;
-      // Epilogue: the item's last O_t MMA, then O / l for this row.
-      if (!(ok = mbar_wait(&o_done[t], (nblk + nkb - 1) & 1, status, kDevTimeoutAttn))) break;
-      ATTN_TRACE(row == 0 && nblk == 0, 182 + t);
-      tc_fence_after();
-      uint32_t ov[64];
-      tmem_ld32_async(t_o, ov);
-      tmem_ld32_async(t_o + 32, ov + 32);
-      tmem_wait_ld();
-      reg_fence32(ov);
-      reg_fence32(ov + 32);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[t]);  // O_t may take the next item's first MMA
-      const int q = I.q0 + t * kQ + row;
-      if (q < T) {
-        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(I.s) * T + q) * 512 + I.h * 64);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          union {
-            __half2 h2[4];
-            uint4 u;
-          } pk;
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            pk.h2[e] = __floats2half2_rn(__uint_as_float(ov[c * 8 + 2 * e]) * inv,
-                                         __uint_as_float(ov[c * 8 + 2 * e + 1]) * inv);
-          dst[c] = pk.u;
-        }
-      }
-      ATTN_TRACE(row == 0 && nblk == 0, 184 + t);
-      nblk += nkb;
-      g += nkb;
+    // ---- softmax + epilogue: warps 2..5 group 0, warps 6..9 group 1 ----
+    const int wg = (warp - 2) / kSoftWarps;
+    if (split) {
+      softmax_role<64>(c, wg, warp & 3, lane);
+    } else {
+      softmax_role<128>(c, wg, warp & 3, lane);
     }
   }
   tc_fence_before();

@@ -138,7 +138,8 @@ def test_conv5_reflect(ctx_unit, S, T):
 
 
 @pytest.mark.parametrize("S,T,masked", [(1, 1, False), (2, 5, True), (3, 64, False), (2, 65, True), (2, 333, True),
-                                         (1, 800, False), (20, 300, True), (40, 800, True), (1, 4096, False)])
+                                         (1, 800, False), (2, 800, True), (20, 300, True), (40, 800, True),
+                                         (1, 4096, False)])
 def test_attention(ctx_unit, S, T, masked):
     dev = _dev()
     g = torch.Generator(device="cpu").manual_seed(S * 100 + T)
