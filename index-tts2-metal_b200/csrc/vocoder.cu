@@ -88,10 +88,21 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
     }
     return;
   }
-  for (int i = w; i < kActTT + 12; i += 8) {
+  // Warp w stages rows w, w + 8, ..., all its loads issued before the first
+  // shared-memory store, so their DRAM latencies overlap.
+  constexpr int kRowsPerWarp = (kActTT + 12 + 7) / 8;
+  float ld[kRowsPerWarp];
+#pragma unroll
+  for (int j = 0; j < kRowsPerWarp; ++j) {
+    const int i = w + 8 * j;
     int r = t0 - 6 + i;
     r = r < 0 ? 0 : (r > T - 1 ? T - 1 : r);
-    xs[i][lane] = cok ? x[static_cast<size_t>(r) * ldx + c] : 0.0f;
+    ld[j] = (cok && i < kActTT + 12) ? x[static_cast<size_t>(r) * ldx + c] : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < kRowsPerWarp; ++j) {
+    const int i = w + 8 * j;
+    if (i < kActTT + 12) xs[i][lane] = ld[j];
   }
   __syncthreads();
   const float a = cok ? alpha[c] : 1.0f;
@@ -109,13 +120,32 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
     for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * f.up[2 * i];
     return 2.0f * acc;
   };
-  for (int q = w; q < kActPos / 2; q += 8) {
+  // Warp w computes the pairs q = 9 w .. 9 w + 8 (q < 70). Interior pairs read
+  // their rows q .. q + 6 of xs from a register window of rows 9 w .. 9 w + 14,
+  // loaded once per warp; pairs at the sequence edges take the clamped path.
+  constexpr int kPairsPerWarp = 9;
+  float xw[kPairsPerWarp + 6];
+#pragma unroll
+  for (int i = 0; i < kPairsPerWarp + 6; ++i) {
+    const int r = kPairsPerWarp * w + i;
+    xw[i] = r < kActTT + 12 ? xs[r][lane] : 0.0f;
+  }
+#pragma unroll
+  for (int jq = 0; jq < kPairsPerWarp; ++jq) {
+    const int q = kPairsPerWarp * w + jq;
+    if (q >= kActPos / 2) break;
     const int m = t0 - 3 + q;  // positions 2m = 2 t0 - 6 + 2q and 2m + 1
     float v0, v1;
     if (2 * m >= 0 && 2 * m + 1 < 2 * T) {
-      // Rows m - 3 .. m + 3 lie in xs (indices q .. q + 6) for every pair.
-      v0 = snake(u_even(q + 5), a, ib);
-      v1 = snake(u_odd(q + 6), a, ib);
+      // Rows m - 3 .. m + 3 are xs rows q .. q + 6, i.e. xw[jq .. jq + 6].
+      float ue = 0.0f, uo = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 6; ++i) {
+        ue += xw[jq + 5 - i] * f.up[2 * i + 1];
+        uo += xw[jq + 6 - i] * f.up[2 * i];
+      }
+      v0 = snake(2.0f * ue, a, ib);
+      v1 = snake(2.0f * uo, a, ib);
     } else {
       // Edge: each position takes v at its clamped position j.
       float vv[2];
@@ -162,24 +192,52 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
 // (out = 0; out += rb / 3 per resblock, runtime/impl/dit_cfm_bigvgan.cpp:
 // 3982-3994): acc = (first ? 0 : acc) + rb / 3 over rows x C. With h16 (the
 // last resblock) it also writes the f16 operand of the next upsampler, rows
-// of ldh >= C columns with the padding columns set to 0.
+// of ldh >= C columns with the padding columns set to 0. Each thread handles
+// 4 consecutive channels (C and ldh are multiples of 4: every stage width is);
+// the grid covers rows x (w / 4) groups with a 32-bit row/group split per
+// grid-stride step (w / 4 <= 384).
 __global__ void __launch_bounds__(256) group_mean_kernel(float* __restrict__ acc, const float* __restrict__ rb,
                                                          size_t rows, int C, int first, __half* __restrict__ h16,
                                                          int ldh) {
-  const int w = h16 ? ldh : C;
-  const size_t n = rows * w;
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t r = i / w;
-    const int c = static_cast<int>(i - r * w);
-    if (c >= C) {
-      h16[i] = __float2half_rn(0.0f);
-      continue;
+  const unsigned w4 = static_cast<unsigned>((h16 ? ldh : C) >> 2);
+  const unsigned c4n = static_cast<unsigned>(C >> 2);
+  const size_t n = rows * w4;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  // Row and group of the first index; later steps advance by the stride's
+  // (rows, groups) decomposition, so no 64-bit division runs in the loop.
+  size_t r = i / w4;
+  unsigned g = static_cast<unsigned>(i - r * w4);
+  const size_t sr = stride / w4;
+  const unsigned sg = static_cast<unsigned>(stride - sr * w4);
+  for (; r < rows;) {
+    if (g >= c4n) {
+      const __half2 z = __float2half2_rn(0.0f);
+      __half2* hp = reinterpret_cast<__half2*>(h16 + r * ldh + 4 * g);
+      hp[0] = z;
+      hp[1] = z;
+    } else {
+      const size_t k = r * C + 4 * g;
+      const float4 b = *reinterpret_cast<const float4*>(rb + k);
+      float4 v = first ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : *reinterpret_cast<const float4*>(acc + k);
+      v.x += b.x / 3.0f;
+      v.y += b.y / 3.0f;
+      v.z += b.z / 3.0f;
+      v.w += b.w / 3.0f;
+      *reinterpret_cast<float4*>(acc + k) = v;
+      if (h16) {
+        __half2* hp = reinterpret_cast<__half2*>(h16 + r * ldh + 4 * g);
+        hp[0] = __floats2half2_rn(v.x, v.y);
+        hp[1] = __floats2half2_rn(v.z, v.w);
+      }
     }
-    const size_t k = r * C + c;
-    const float v = (first ? 0.0f : acc[k]) + rb[k] / 3.0f;
-    acc[k] = v;
-    if (h16) h16[i] = __float2half_rn(v);
+    r += sr;
+    g += sg;
+    if (g >= w4) {
+      g -= w4;
+      ++r;
+    }
   }
 }
 
@@ -681,7 +739,7 @@ void Vocoder::enqueue(Plan* p, std::vector<KernelTiming>* prof) {
       const size_t n = static_cast<size_t>(tg) * C;
       __half* h16 = (j == 2 && i < 5) ? p->in16 : nullptr;
       P.run("group_mean", 0.0, n * (4.0 * (j == 0 ? 2 : 3)) + (h16 ? tg * cp * 2.0 : 0.0), [&] {
-        group_mean_kernel<<<grid_for(static_cast<size_t>(tg) * (h16 ? cp : C)), 256, 0, stream_>>>(
+        group_mean_kernel<<<grid_for(static_cast<size_t>(tg) * (h16 ? cp : C) / 4), 256, 0, stream_>>>(
             p->acc32, p->xr32, static_cast<size_t>(tg), C, j == 0 ? 1 : 0, h16, cp);
         check(cudaGetLastError(), "group mean");
       });

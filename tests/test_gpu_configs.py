@@ -1,8 +1,9 @@
 """Benchmark configurations 3 and 4 at their full sizes on the GPU, through the C ABI.
 
 Config 4 (one utterance of T=4096, P=300, 25 steps, CFG 0.7) stresses the
-masked RoPE attention at long sequence length: one teacher-forced guided step
-is checked against the CPU oracle, and the full sampler for determinism.
+masked RoPE attention at long sequence length: the guided velocity (both CFG
+branches) at three timesteps of the schedule is checked against the CPU
+oracle, and the full sampler for determinism.
 Config 3 (64 utterances, lengths drawn from 200..1500, 16 steps, CFG 0.7,
 length-bucketed with key-padding masks) is run whole through
 itts_cfm_run_batch; the shortest utterance is checked against the oracle's
@@ -38,19 +39,26 @@ def _mel_ok(ref, got):
     assert c["max_abs"] <= MEL_MAX_ABS or c["rel_l2"] <= MEL_REL_L2, c
 
 
-@pytest.mark.timeout(900)
-def test_config4_long_utterance_step_vs_oracle(ctx_baseline, port_baseline):
-    """T=4096 (config 4): one guided step at t=0.48 on a noisy state, both CFG
-    branches on the GPU; the conditional velocity against the oracle."""
+@pytest.mark.timeout(1500)
+@pytest.mark.parametrize("t", [0.0, 0.48, 0.96])
+def test_config4_long_utterance_guided_step_vs_oracle(ctx_baseline, port_baseline, t):
+    """T=4096 (config 4): the guided velocity of one step at the first, a
+    middle and the last timestep of the 25-step schedule, both CFG branches
+    against the oracle (and their CFG 0.7 mix)."""
     u = W.config_utterances(4)[0]
     assert u.T == 4096
     x = u.noise.copy()
     x[: u.P] = 0
     px = u.prompt_x()
     mask = np.ones((1, u.T), np.uint32)
-    vel = ctx_baseline.estimator(x[None], px[None], u.cond[None], u.style[None], mask, t=0.48, branches=2)
+    vel = ctx_baseline.estimator(x[None], px[None], u.cond[None], u.style[None], mask, t=t, branches=2)
     assert np.isfinite(vel).all()
-    _vel_ok(port_baseline.estimator(x, px, u.cond, u.style, 0.48, mask[0]), vel[0, 0])
+    ref_c = port_baseline.estimator(x, px, u.cond, u.style, t, mask[0])
+    ref_u = port_baseline.estimator(x, np.zeros_like(px), np.zeros_like(u.cond), np.zeros_like(u.style), t, mask[0])
+    _vel_ok(ref_c, vel[0, 0])
+    _vel_ok(ref_u, vel[0, 1])
+    cfg = np.float32(0.7)
+    _vel_ok((1 + cfg) * ref_c - cfg * ref_u, (1 + cfg) * vel[0, 0] - cfg * vel[0, 1])
 
 
 @pytest.mark.timeout(600)
