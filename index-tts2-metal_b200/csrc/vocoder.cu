@@ -61,33 +61,25 @@ __device__ __forceinline__ float snake(float u, float a, float ib) {
 }
 
 // The two 12-tap filters travel by value (kernel parameters live in the
-// constant bank, which FMAs read as an operand without a load).
+// constant bank, which FMAs read as an operand without a load). up2 holds
+// 2 * up: the upsampler's factor 2 folded into the taps, which is exact (a
+// power-of-two scale commutes with every rounding of the FMA chain, outside
+// the subnormal range).
 struct SnakeFilters {
-  float up[12];
+  float up2[12];
   float down[12];
 };
 
-// Output columns [C, cw) (the f16 operand's channel padding) are written as 0;
-// a block whose 32 channels are all padding only writes those zeros.
-template <bool F16OUT>
-__global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__ x, int ldx, int T, int C, int cw,
-                                                       const float* __restrict__ alpha,
-                                                       const float* __restrict__ inv_beta, const SnakeFilters f,
-                                                       void* __restrict__ out, int ldo) {
-  __shared__ float xs[kActTT + 12][kActCC];  // xs[i] = x[clamp(t0 - 6 + i)]
-  __shared__ float vs[kActPos][kActCC];      // vs[i] = v(clamp(2 t0 - 6 + i))
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int t0 = blockIdx.x * kActTT;
-  const int c = blockIdx.y * kActCC + lane;
+// One block's tile (tokens t0 .. t0 + 63, 32 channels). EDGE = false is the
+// interior form: every input row, pair and output of the tile lies inside
+// [0, T), so no index is clamped and no position is checked.
+template <bool F16OUT, bool EDGE>
+__device__ __forceinline__ void snake_tile(float (&xs)[kActTT + 12][kActCC], float (&vs)[kActPos][kActCC],
+                                           const float* __restrict__ x, int ldx, int T, int C, int cw,
+                                           const float* __restrict__ alpha, const float* __restrict__ inv_beta,
+                                           const SnakeFilters& f, void* __restrict__ out, int ldo, int t0, int c,
+                                           int lane, int w) {
   const bool cok = c < C;
-  if (blockIdx.y * kActCC >= C) {  // padding columns only
-    if constexpr (F16OUT) {
-      if (c < cw)
-        for (int tt = w; tt < kActTT && t0 + tt < T; tt += 8)
-          static_cast<__half*>(out)[static_cast<size_t>(t0 + tt) * ldo + c] = __float2half_rn(0.0f);
-    }
-    return;
-  }
   // Warp w stages rows w, w + 8, ..., all its loads issued before the first
   // shared-memory store, so their DRAM latencies overlap.
   constexpr int kRowsPerWarp = (kActTT + 12 + 7) / 8;
@@ -96,7 +88,7 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
   for (int j = 0; j < kRowsPerWarp; ++j) {
     const int i = w + 8 * j;
     int r = t0 - 6 + i;
-    r = r < 0 ? 0 : (r > T - 1 ? T - 1 : r);
+    if constexpr (EDGE) r = r < 0 ? 0 : (r > T - 1 ? T - 1 : r);
     ld[j] = (cok && i < kActTT + 12) ? x[static_cast<size_t>(r) * ldx + c] : 0.0f;
   }
 #pragma unroll
@@ -111,14 +103,14 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
   auto u_even = [&](int xi) {  // u(2m), xi = index of row m + 2
     float acc = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * f.up[2 * i + 1];
-    return 2.0f * acc;
+    for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * f.up2[2 * i + 1];
+    return acc;
   };
   auto u_odd = [&](int xi) {  // u(2m + 1), xi = index of row m + 3
     float acc = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * f.up[2 * i];
-    return 2.0f * acc;
+    for (int i = 0; i < 6; ++i) acc += xs[xi - i][lane] * f.up2[2 * i];
+    return acc;
   };
   // Warp w computes the pairs q = 9 w .. 9 w + 8 (q < 70). Interior pairs read
   // their rows q .. q + 6 of xs from a register window of rows 9 w .. 9 w + 14,
@@ -136,16 +128,16 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
     if (q >= kActPos / 2) break;
     const int m = t0 - 3 + q;  // positions 2m = 2 t0 - 6 + 2q and 2m + 1
     float v0, v1;
-    if (2 * m >= 0 && 2 * m + 1 < 2 * T) {
+    if (!EDGE || (m >= 0 && m < T)) {
       // Rows m - 3 .. m + 3 are xs rows q .. q + 6, i.e. xw[jq .. jq + 6].
       float ue = 0.0f, uo = 0.0f;
 #pragma unroll
       for (int i = 0; i < 6; ++i) {
-        ue += xw[jq + 5 - i] * f.up[2 * i + 1];
-        uo += xw[jq + 6 - i] * f.up[2 * i];
+        ue += xw[jq + 5 - i] * f.up2[2 * i + 1];
+        uo += xw[jq + 6 - i] * f.up2[2 * i];
       }
-      v0 = snake(2.0f * ue, a, ib);
-      v1 = snake(2.0f * uo, a, ib);
+      v0 = snake(ue, a, ib);
+      v1 = snake(uo, a, ib);
     } else {
       // Edge: each position takes v at its clamped position j.
       float vv[2];
@@ -172,19 +164,47 @@ __global__ void __launch_bounds__(256) snake_aa_kernel(const float* __restrict__
   float win[26];
 #pragma unroll
   for (int i = 0; i < 26; ++i) win[i] = vs[2 * tb + 1 + i][lane];
+  const size_t o0 = static_cast<size_t>(t0 + tb) * ldo + c;
 #pragma unroll
   for (int o = 0; o < 8; ++o) {
-    const int t = t0 + tb + o;
-    if (t >= T) break;
+    if (EDGE && t0 + tb + o >= T) break;
     float acc = 0.0f;
 #pragma unroll
     for (int k = 0; k < 12; ++k) acc += win[2 * o + k] * f.down[k];
     if (!cok) acc = 0.0f;
     if constexpr (F16OUT) {
-      static_cast<__half*>(out)[static_cast<size_t>(t) * ldo + c] = __float2half_rn(acc);
+      static_cast<__half*>(out)[o0 + static_cast<size_t>(o) * ldo] = __float2half_rn(acc);
     } else {
-      static_cast<float*>(out)[static_cast<size_t>(t) * ldo + c] = acc;
+      static_cast<float*>(out)[o0 + static_cast<size_t>(o) * ldo] = acc;
     }
+  }
+}
+
+// Output columns [C, cw) (the f16 operand's channel padding) are written as 0;
+// a block whose 32 channels are all padding only writes those zeros.
+template <bool F16OUT>
+__global__ void __launch_bounds__(256, 6) snake_aa_kernel(const float* __restrict__ x, int ldx, int T, int C, int cw,
+                                                       const float* __restrict__ alpha,
+                                                       const float* __restrict__ inv_beta, const SnakeFilters f,
+                                                       void* __restrict__ out, int ldo) {
+  __shared__ float xs[kActTT + 12][kActCC];  // xs[i] = x[clamp(t0 - 6 + i)]
+  __shared__ float vs[kActPos][kActCC];      // vs[i] = v(clamp(2 t0 - 6 + i))
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * kActTT;
+  const int c = blockIdx.y * kActCC + lane;
+  if (blockIdx.y * kActCC >= C) {  // padding columns only
+    if constexpr (F16OUT) {
+      if (c < cw)
+        for (int tt = w; tt < kActTT && t0 + tt < T; tt += 8)
+          static_cast<__half*>(out)[static_cast<size_t>(t0 + tt) * ldo + c] = __float2half_rn(0.0f);
+    }
+    return;
+  }
+  // Interior tile: rows t0 - 6 .. t0 + 69 all inside [0, T).
+  if (t0 >= 6 && t0 + kActTT + 6 <= T) {
+    snake_tile<F16OUT, false>(xs, vs, x, ldx, T, C, cw, alpha, inv_beta, f, out, ldo, t0, c, lane, w);
+  } else {
+    snake_tile<F16OUT, true>(xs, vs, x, ldx, T, C, cw, alpha, inv_beta, f, out, ldo, t0, c, lane, w);
   }
 }
 
@@ -703,7 +723,7 @@ void Vocoder::enqueue(Plan* p, std::vector<KernelTiming>* prof) {
     const dim3 grid((tg + kActTT - 1) / kActTT, (cw + kActCC - 1) / kActCC);
     const double bytes = static_cast<double>(tg) * a.c * (4.0 + (f16 ? 2.0 : 4.0));
     SnakeFilters filt;
-    std::memcpy(filt.up, a.up, sizeof(filt.up));
+    for (int k = 0; k < 12; ++k) filt.up2[k] = 2.0f * a.up[k];
     std::memcpy(filt.down, a.down, sizeof(filt.down));
     P.run(name, 0.0, bytes, [&] {
       if (f16) {
