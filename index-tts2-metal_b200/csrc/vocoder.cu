@@ -7,6 +7,8 @@
 #include <stdexcept>
 
 #include "bundle.hpp"
+#include "launch.cuh"
+#include "ptx.cuh"
 
 namespace itts {
 
@@ -157,6 +159,9 @@ __device__ __forceinline__ void snake_tile(float (&xs)[kActTT + 12][kActCC], flo
     vs[2 * q + 1][lane] = v1;
   }
   __syncthreads();
+  // The next kernel (a conv GEMM) may start its prologue once every block is
+  // in its store phase; it waits for this grid before reading `out`.
+  griddep_launch();
   if (c >= cw) return;
   // Warp w: outputs t0 + 8w .. t0 + 8w + 7; output t reads positions
   // 2t - 5 .. 2t + 6, i.e. vs[2(t - t0) + 1 .. 2(t - t0) + 12].
@@ -189,6 +194,10 @@ __global__ void __launch_bounds__(256, 6) snake_aa_kernel(const float* __restric
                                                        void* __restrict__ out, int ldo) {
   __shared__ float xs[kActTT + 12][kActCC];  // xs[i] = x[clamp(t0 - 6 + i)]
   __shared__ float vs[kActPos][kActCC];      // vs[i] = v(clamp(2 t0 - 6 + i))
+  // Launched with programmatic dependent launch: nothing of the previous
+  // kernel's memory (its output x, or the operand `out` it may still read) is
+  // touched before this wait.
+  griddep_wait();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int t0 = blockIdx.x * kActTT;
   const int c = blockIdx.y * kActCC + lane;
@@ -219,6 +228,8 @@ __global__ void __launch_bounds__(256, 6) snake_aa_kernel(const float* __restric
 __global__ void __launch_bounds__(256) group_mean_kernel(float* __restrict__ acc, const float* __restrict__ rb,
                                                          size_t rows, int C, int first, __half* __restrict__ h16,
                                                          int ldh) {
+  griddep_wait();
+  griddep_launch();
   const unsigned w4 = static_cast<unsigned>((h16 ? ldh : C) >> 2);
   const unsigned c4n = static_cast<unsigned>(C >> 2);
   const size_t n = rows * w4;
@@ -264,6 +275,8 @@ __global__ void __launch_bounds__(256) group_mean_kernel(float* __restrict__ acc
 // mel [T][80] f32 -> [T][128] f16 operand of conv_pre (columns >= 80 zero).
 __global__ void __launch_bounds__(256) mel_to_f16_kernel(const float* __restrict__ mel, int T,
                                                          __half* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const size_t n = static_cast<size_t>(T) * 128;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -280,6 +293,8 @@ __global__ void __launch_bounds__(256) mel_to_f16_kernel(const float* __restrict
 __global__ void __launch_bounds__(256) conv_post_kernel(const float* __restrict__ a, int T,
                                                         const float* __restrict__ w, float* __restrict__ wave) {
   __shared__ float ws[24 * 7];
+  griddep_wait();
+  griddep_launch();
   for (int i = threadIdx.x; i < 24 * 7; i += blockDim.x) ws[i] = w[i];
   __syncthreads();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
@@ -726,17 +741,17 @@ void Vocoder::enqueue(Plan* p, std::vector<KernelTiming>* prof) {
     for (int k = 0; k < 12; ++k) filt.up2[k] = 2.0f * a.up[k];
     std::memcpy(filt.down, a.down, sizeof(filt.down));
     P.run(name, 0.0, bytes, [&] {
-      if (f16) {
-        snake_aa_kernel<true><<<grid, 256, 0, stream_>>>(x, a.c, tg, a.c, cw, a.alpha, a.inv_beta, filt, out, ldo);
-      } else {
-        snake_aa_kernel<false><<<grid, 256, 0, stream_>>>(x, a.c, tg, a.c, cw, a.alpha, a.inv_beta, filt, out, ldo);
-      }
-      check(cudaGetLastError(), "snake activation");
+      check(f16 ? launch_pdl(snake_aa_kernel<true>, grid, dim3(256), 0, stream_, x, a.c, tg, a.c, cw, a.alpha,
+                             a.inv_beta, filt, out, ldo)
+                : launch_pdl(snake_aa_kernel<false>, grid, dim3(256), 0, stream_, x, a.c, tg, a.c, cw, a.alpha,
+                             a.inv_beta, filt, out, ldo),
+            "snake activation");
     });
   };
   P.run("mel_to_f16", 0.0, T * (80.0 * 4 + 128.0 * 2), [&] {
-    mel_to_f16_kernel<<<grid_for(static_cast<size_t>(T) * 128), 256, 0, stream_>>>(p->mel32, T, p->mel16);
-    check(cudaGetLastError(), "mel to f16");
+    check(launch_pdl(mel_to_f16_kernel, dim3(grid_for(static_cast<size_t>(T) * 128)), dim3(256), 0, stream_,
+                     p->mel32, T, p->mel16),
+          "mel to f16");
   });
   G("conv_pre", p->pre, pre_);
   int tg = T;
@@ -759,16 +774,18 @@ void Vocoder::enqueue(Plan* p, std::vector<KernelTiming>* prof) {
       const size_t n = static_cast<size_t>(tg) * C;
       __half* h16 = (j == 2 && i < 5) ? p->in16 : nullptr;
       P.run("group_mean", 0.0, n * (4.0 * (j == 0 ? 2 : 3)) + (h16 ? tg * cp * 2.0 : 0.0), [&] {
-        group_mean_kernel<<<grid_for(static_cast<size_t>(tg) * (h16 ? cp : C) / 4), 256, 0, stream_>>>(
-            p->acc32, p->xr32, static_cast<size_t>(tg), C, j == 0 ? 1 : 0, h16, cp);
-        check(cudaGetLastError(), "group mean");
+        check(launch_pdl(group_mean_kernel, dim3(grid_for(static_cast<size_t>(tg) * (h16 ? cp : C) / 4)), dim3(256),
+                         0, stream_, p->acc32, static_cast<const float*>(p->xr32), static_cast<size_t>(tg), C,
+                         j == 0 ? 1 : 0, h16, cp),
+              "group mean");
       });
     }
   }
   A("snake_aa.post", post_act_, p->acc32, tg, p->h32, 24, false);
   P.run("conv_post", 2.0 * tg * 24 * 7, tg * (24.0 * 4 + 4.0), [&] {
-    conv_post_kernel<<<(tg + 255) / 256, 256, 0, stream_>>>(p->h32, tg, post_w_, p->wave);
-    check(cudaGetLastError(), "conv_post");
+    check(launch_pdl(conv_post_kernel, dim3((tg + 255) / 256), dim3(256), 0, stream_, static_cast<const float*>(p->h32),
+                     tg, static_cast<const float*>(post_w_), p->wave),
+          "conv_post");
   });
   P.finish();
 }
