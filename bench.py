@@ -71,6 +71,27 @@ def gemm_family(prof: list[dict]) -> dict:
             "flops": sum(d["flops"] for d in rows), "bytes": sum(d["bytes"] for d in rows)}
 
 
+def gemm_bound_frac(prof: list[dict], tflops_peak: float, hbm_peak: float) -> dict:
+    """Fraction of each GEMM's own roofline: the time the measured peaks allow
+    a launch (the larger of its FLOPs at the tensor peak and its compulsory
+    bytes at the HBM peak), summed over the GEMM family and divided by the
+    family's measured time. Also the share of that family time whose bound is
+    HBM (the f32 residual-stream epilogues at large M)."""
+    rows = [d for d in prof if d["name"].startswith("gemm")]
+    bound = hbm_bound = meas = 0.0
+    for d in rows:
+        t_f = d["flops"] / (tflops_peak * 1e12)
+        t_b = d["bytes"] / (hbm_peak * 1e9)
+        bound += max(t_f, t_b)
+        meas += d["ms"] / 1e3
+        if t_b > t_f:
+            hbm_bound += d["ms"] / 1e3
+    return {"frac": bound / meas if meas > 0 else None,
+            "hbm_bound_time_share": hbm_bound / meas if meas > 0 else None,
+            "method": "sum over GEMM launches of max(FLOPs / tensor peak, compulsory bytes / HBM peak) "
+                      "/ summed event-timed GEMM time"}
+
+
 def kernel_row(d: dict, reps: int) -> dict:
     """One profiled kernel kind per CFM step: launches, time, TFLOP/s and
     compulsory-HBM GB/s over its summed event-timed launch durations."""
@@ -1008,6 +1029,7 @@ def main():
                    "ms_per_run": bms, "ms_per_cfm_step": bms / cfg["steps"],
                    "tflops": step_flops_total(Bb, T, cfg) * cfg["steps"] / (bms / 1e3) / 1e12,
                    "gemm_tflops": b_ach, "gemm_frac": b_ach / peak,
+                   "gemm_roofline_bound": gemm_bound_frac(bprof, peak, float(peaks.get("hbm_gbs", 6546.0))),
                    "kernels": [kernel_row(d, 2) for d in bprof]}
 
     condition = None
