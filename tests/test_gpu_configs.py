@@ -7,8 +7,13 @@ oracle, and the full sampler for determinism.
 Config 3 (64 utterances, lengths drawn from 200..1500, 16 steps, CFG 0.7,
 length-bucketed with key-padding masks) is run whole through
 itts_cfm_run_batch; the shortest utterance is checked against the oracle's
-masked sampler at its bucket length, and the longest against a padded run of
-itself alone (bitwise: rows never mix across sequences).
+masked sampler at its bucket length, and the longest against a run of itself
+alone. Rows never mix across sequences, but the attention kernel splits its
+work by the launch's size (pairs of query tiles per CTA in a large batch, each
+tile's keys split between two warp groups when pairs would leave SMs idle),
+and the two splits sum a row's scores in different orders: the lone run is
+held to a tolerance 100x tighter than the parity gate, and a repeated batch
+run to bitwise equality.
 
 Gates as in test_gpu_parity: velocity cosine >= 0.999 and rel-L2 <= 1e-2;
 final mel max-abs <= 2e-2 or rel-L2 <= 1e-2."""
@@ -94,10 +99,17 @@ def test_config3_bucketed_batch_full_size(ctx_baseline, port_baseline):
     mask = (np.arange(Tp) < u.T).astype(np.uint32)
     ref = port_baseline.euler(noise[0], px[0], cond[0], style[0], u.P, 16, 0.7, mask=mask)
     _mel_ok(ref[: u.T], outs[i])
-    # Longest utterance: its launch is padded to its own length, so it equals
-    # the single-utterance sampler bit for bit (rows never mix across sequences).
+    # Longest utterance: its launch is padded to its own length; alone it runs
+    # with the key-split attention (too few tile pairs to fill the SMs), in the
+    # batch with tile pairs, so the two agree to summation-order rounding.
     j = int(np.argmax([u.T for u in utts]))
     u = utts[j]
     assert lens[j] == u.T
     alone = ctx_baseline.run(u.noise, u.prompt, u.cond, u.style, 16, 0.7)
-    assert np.array_equal(alone, outs[j])
+    c = O.compare(alone, outs[j])
+    assert c["cosine"] >= 0.99999 and c["rel_l2"] <= 1e-4, c
+    # The same batch again: bitwise identical.
+    again = ctx_baseline.run_batch(
+        [dict(noise=v.noise, prompt=v.prompt, cond=v.cond, style=v.style) for v in utts], 16, 0.7)
+    for o, a in zip(outs, again):
+        assert np.array_equal(o, a)
