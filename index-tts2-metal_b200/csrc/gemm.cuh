@@ -59,6 +59,7 @@ struct GemmArgs {
   __half* wn_xp;          // [S*(T+4),512] reflect-padded WaveNet activations
   int wn_first;
   int pad_rows;           // kEpiF32 only: A rows are the padded S*(T+4) space; write compact rows
+  int tma_o32;            // kEpiF32: out32 is written by TMA stores through GemmLaunch::tmO (set by gemm_run)
   unsigned int* status;   // device status word
   // AdaRMSNorm folded across a producer/consumer GEMM pair:
   //   y = w*g*(x*inv) + b,  inv = 1/sqrt(mean_k x^2 + 1e-5)
@@ -84,6 +85,7 @@ struct GemmLaunch {
   CUtensorMap tmA0;
   CUtensorMap tmA1;
   CUtensorMap tmB;  // box rows: bn, or bn / 2 for the CTA-pair form
+  CUtensorMap tmO;  // kEpiF32 out32 as fp32 {N, M}, box 32 x 32, 128-byte swizzle (encoded by gemm_run)
   GemmArgs args;
   int bn;
   int pair;  // 1: CTA-pair form (clusters of 2, cta_group::2 MMA over 256-row tiles)
