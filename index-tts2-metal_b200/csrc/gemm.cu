@@ -140,6 +140,36 @@ __device__ __forceinline__ void flush_f32(const float4* stg, const float* my_row
   }
 }
 
+// f16 stage of a 32 x 32 block for a TMA store with the 64-byte swizzle: row r
+// (64 B) holds 16-byte chunk c (columns 8c .. 8c + 7) at chunk position
+// c ^ ((r >> 1) & 3). Writes columns c16 .. c16 + 15 of row r, rounded as
+// flush_f16 rounds.
+__device__ __forceinline__ void stage_put16_h(float4* stg, int r, int c16, const float* v) {
+  uint4* row = reinterpret_cast<uint4*>(stg) + r * 4;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int c = (c16 >> 3) + k;
+    union {
+      __half2 h[4];
+      uint4 u;
+    } pk;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pk.h[e] = __floats2half2_rn(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]);
+    row[c ^ ((r >> 1) & 3)] = pk.u;
+  }
+}
+
+// One TMA store of the warp's staged 32-row block (this lane's staged values
+// made visible to the async proxy first); lane 0 issues and commits it.
+__device__ __forceinline__ void stage_tma_store(const CUtensorMap* tmo, const float4* stg, int x, int y, int lane) {
+  fence_proxy_async_shared();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmo, stg, x, y);
+    bulk_commit();
+  }
+}
+
 // Store staged columns [0, ncols) of all 32 rows as f16 at (row_ptr + col0).
 __device__ __forceinline__ void flush_f16(const float4* stg, const __half* my_row, int col0, int ncols, int lane) {
 #pragma unroll
@@ -297,8 +327,14 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, const CUtens
     // res/skip update (x and skip values share the stage).
     constexpr int G = EPI == kEpiWnResSkip ? 1 : 2;
     float xg[16 * G], bg[16];
+    // SwiGLU: every group is 32 output channels of contiguous rows.
+    const bool t16 = EPI == kEpiSwiGLU && args.tma_o16 && m0 + (row & ~31) < args.M;
 #pragma unroll 1
     for (int q2 = q_begin; q2 < q_end; q2 += G) {
+      if (t16) {  // a TMA store of the previous group may still be reading the stage
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+      }
 #pragma unroll
       for (int h = 0; h < G; ++h) {
         const int q = q2 + h;
@@ -348,7 +384,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, const CUtens
 #pragma unroll
           for (int e = 0; e < 16; ++e) ac_cur[e] = ac_nxt[e];
         }
-        stage_put16(stg, lane, h * 16, xg + h * 16);
+        if (t16) {
+          stage_put16_h(stg, lane, h * 16, xg + h * 16);
+        } else {
+          stage_put16(stg, lane, h * 16, xg + h * 16);
+        }
         if constexpr (EPI == kEpiWnResSkip) stage_put16(stg, lane, 16, bg);
         if (more) {
           tmem_wait_ld();
@@ -367,6 +407,8 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, const CUtens
         flush_f16(stg, xp_row, ch0, 16, lane);
         if (row_ok) write_halos<16>(args.wn_xp, s, t, T, ch0, xg);
         flush_f32(stg, acc_row, ch0, 16, lane, 4);
+      } else if (t16) {
+        stage_tma_store(tmo, stg, ch0, m0 + (row & ~31), lane);
       } else {
         flush_f16(stg, out16_row, ch0, 32, lane);
       }
@@ -459,13 +501,15 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, const CUtens
 #pragma unroll 1
     for (int cp = c_begin; cp < c_end; cp += 2) {
       float sc = 0.0f;  // folded-norm producer: sum of squares over this 32-column group
-      if constexpr (EPI == kEpiF32) {
-        // A TMA store of the previous group may still be reading the stage.
-        if (args.tma_o32) {
-          if (lane == 0) bulk_wait_read_all();
-          __syncwarp();
-        }
+      // A TMA store of the previous group may still be reading the stage.
+      if ((EPI == kEpiF32 && args.tma_o32) || ((EPI == kEpiQKV || EPI == kEpiF16) && args.tma_o16)) {
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
       }
+      // QKV / F16: a full 32-column group of in-range rows is staged as f16
+      // for one TMA store; other groups go through the fp32 stage.
+      const bool t16 = (EPI == kEpiQKV || EPI == kEpiF16) && args.tma_o16 && cp + 1 < c_end &&
+                       n0 + cp * 16 < args.N && m0 + (row & ~31) < args.M;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = cp + h;
@@ -507,7 +551,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, const CUtens
 #pragma unroll
             for (int e = 0; e < 16; ++e) v[e] = (x0_cur[e] + v[e]) * msk + x1_cur[e];
           }
-          stage_put16(stg, lane, h * 16, v);
+          if (t16) {
+            stage_put16_h(stg, lane, h * 16, v);
+          } else {
+            stage_put16(stg, lane, h * 16, v);
+          }
           if (more) {
             tmem_wait_ld();
             reg_fence16(tn);
@@ -533,19 +581,18 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, const CUtens
       const bool tr = threadIdx.x == 64 && parity == 0 && cp == c_begin;
       if (tr) GEMM_TRACE(24);
       if constexpr (EPI == kEpiF16 || EPI == kEpiQKV) {
-        flush_f16(stg, static_cast<const __half*>(d0), ng, ncols, lane);
+        if (t16) {
+          stage_tma_store(tmo, stg, ng, m0 + (row & ~31), lane);
+        } else {
+          flush_f16(stg, static_cast<const __half*>(d0), ng, ncols, lane);
+        }
       } else if constexpr (EPI == kEpiF32) {
         // A full 32-column group leaves through one TMA store of the stage (its
         // layout is the 128-byte swizzle of the tensor map; rows >= M and
         // columns >= N are not written); a 16-column remainder through the
         // lanes' coalesced stores.
         if (args.tma_o32 && cp + 1 < c_end && ng < args.N && m0 + (row & ~31) < args.M) {
-          fence_proxy_async_shared();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(tmo, stg, ng, m0 + (row & ~31));
-            bulk_commit();
-          }
+          stage_tma_store(tmo, stg, ng, m0 + (row & ~31), lane);
         } else {
           flush_f32(stg, static_cast<const float*>(d0), ng, ncols, lane);
         }
@@ -843,10 +890,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (local == 0 && warp == 2 && lane == 0) GEMM_TRACE(6);
     }
     // This warp's TMA stores complete before it leaves.
-    if constexpr (EPI == kEpiF32) {
-      if (args.tma_o32 && lane == 0) bulk_wait_all();
-      __syncwarp();
-    }
+    if ((args.tma_o32 || args.tma_o16) && lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   if constexpr (PAIR) {
     // Neither CTA frees its TMEM (or exits, which would drop the barriers the
@@ -1003,6 +1048,20 @@ bool make_tmap_f16(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t ro
 // Tensor map of an fp32 output [rows][cols] (row stride ld floats) for the
 // epilogue's TMA stores: box 32 columns x 32 rows with the 128-byte swizzle
 // of the warp stages.
+static bool make_tmap_out_f16(CUtensorMap* tm, const __half* base, uint64_t cols, uint64_t rows, uint64_t ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || !base || cols == 0 || rows == 0 || cols > ld) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static bool make_tmap_out_f32(CUtensorMap* tm, const float* base, uint64_t cols, uint64_t rows, uint64_t ld) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || !base || cols == 0 || rows == 0 || cols > ld) return false;
@@ -1026,6 +1085,12 @@ cudaError_t gemm_run(const GemmLaunch& g_in, cudaStream_t stream) {
       make_tmap_out_f32(&g.tmO, g.args.out32, static_cast<uint64_t>(g.args.N), static_cast<uint64_t>(g.args.M),
                         static_cast<uint64_t>(g.args.ld32)))
     g.args.tma_o32 = 1;
+  g.args.tma_o16 = 0;
+  const int e = g.args.epi;
+  if ((e == kEpiF16 || e == kEpiQKV || e == kEpiSwiGLU) && g.args.out16 && !g.pair &&
+      make_tmap_out_f16(&g.tmO, g.args.out16, static_cast<uint64_t>(e == kEpiSwiGLU ? g.args.N / 2 : g.args.N),
+                        static_cast<uint64_t>(g.args.M), static_cast<uint64_t>(g.args.ld16)))
+    g.args.tma_o16 = 1;
   if (g.pair) {
     switch (g.bn) {
       case 64: return launch_epi<64, true>(g, stream);

@@ -60,6 +60,7 @@ struct GemmArgs {
   int wn_first;
   int pad_rows;           // kEpiF32 only: A rows are the padded S*(T+4) space; write compact rows
   int tma_o32;            // kEpiF32: out32 is written by TMA stores through GemmLaunch::tmO (set by gemm_run)
+  int tma_o16;            // kEpiF16 / kEpiQKV / kEpiSwiGLU: out16 likewise (set by gemm_run)
   unsigned int* status;   // device status word
   // AdaRMSNorm folded across a producer/consumer GEMM pair:
   //   y = w*g*(x*inv) + b,  inv = 1/sqrt(mean_k x^2 + 1e-5)
@@ -85,7 +86,8 @@ struct GemmLaunch {
   CUtensorMap tmA0;
   CUtensorMap tmA1;
   CUtensorMap tmB;  // box rows: bn, or bn / 2 for the CTA-pair form
-  CUtensorMap tmO;  // kEpiF32 out32 as fp32 {N, M}, box 32 x 32, 128-byte swizzle (encoded by gemm_run)
+  CUtensorMap tmO;  // the TMA-stored output (encoded by gemm_run): kEpiF32 out32 as fp32 {N, M} with the
+                    // 128-byte swizzle, or out16 as f16 {columns, M} with the 64-byte swizzle; box 32 x 32
   GemmArgs args;
   int bn;
   int pair;  // 1: CTA-pair form (clusters of 2, cta_group::2 MMA over 256-row tiles)
