@@ -1,13 +1,19 @@
 // tcgen05/TMEM GEMM with fused DiT-CFM epilogues (sm_100a).
 //
 // Persistent, warp-specialised: one CTA per SM walks the 128 x BN output
-// tiles (static round-robin over the grid). Warp roles (192 threads):
-//   warp 0 lane 0 : TMA producer (A and B k-blocks into a STAGES-deep ring)
-//   warp 1        : allocates 2*BN TMEM columns; lane 0 issues tcgen05.mma
-//                   (M=128, N=BN, K=16) into accumulator buffer (tile & 1)
-//   warps 2..5    : epilogue, one accumulator row per thread (TMEM lane
-//                   quarter = warp % 4); drains buffer (tile & 1) while the
-//                   MMA warp fills the other one.
+// tiles (static round-robin over the grid). Warp roles (352 threads):
+//   warp 0 lane 0  : TMA producer of the A k-blocks (STAGES-deep ring)
+//   warp 10 lane 0 : TMA producer of the B (weight) k-blocks; the first
+//                    tile's are issued before the grid-dependency wait
+//   warp 1         : allocates TMEM for two accumulator buffers; lane 0
+//                    issues tcgen05.mma (M=128, N=BN, K=16) into buffer
+//                    (tile & 1)
+//   warps 2..9     : epilogue, one accumulator row per thread (TMEM lane
+//                    quarter = warp % 4), two warps per quarter each owning
+//                    half of the columns; drains buffer (tile & 1) while the
+//                    MMA warp fills the other one.
+// Outputs leave through a per-warp shared-memory stage: by TMA stores where
+// the destination rows are contiguous, else by the lanes' coalesced stores.
 // Replaces the reference's MPS GEMM calls and the elementwise kernels that
 // followed them (bias prefill, RoPE rotate, silu_mul_split, add, wavenet gate,
 // wavenet res/skip update, reflect pad, concat), metal/kernels.metal:131-239,
@@ -103,13 +109,16 @@ __device__ __forceinline__ void store_tile_consts(float* sconst, int etid, const
   }
 }
 
-// ---- coalesced epilogue stores through a per-warp shared-memory stage ----
+// ---- epilogue stores through a per-warp shared-memory stage ----
 // Each epilogue warp owns 32 accumulator rows (one per lane). Values of a
 // 32-column group are first written row-wise into a 32 x 32 fp32 stage (16-byte
-// chunks swizzled by row), then read column-wise so that 8 (fp32) or 4 (f16)
-// lanes cover one destination row segment and every store is a full 128 B / 64 B
-// line piece. Destination rows come from the owning lane by shuffle, so any
-// per-row remapping (padded WaveNet rows, compact rows) is supported.
+// chunk j of row r at r * 8 + (j ^ (r & 7)): the 128-byte swizzle). With
+// contiguous destination rows the block leaves through one TMA store (f32, or
+// an f16 copy of the block in the 64-byte swizzle, stage_put16_h); otherwise
+// it is read column-wise so that 8 (fp32) or 4 (f16) lanes cover one
+// destination row segment and every store is a full 128 B / 64 B line piece,
+// destination rows coming from the owning lane by shuffle (any per-row
+// remapping: padded WaveNet rows, compact rows).
 constexpr int kStageFloats = 32 * 32;  // per warp
 
 __device__ __forceinline__ void stage_put16(float4* stg, int r, int c16, const float* v) {
