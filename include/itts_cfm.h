@@ -95,9 +95,14 @@ int itts_cfm_run(itts_cfm_ctx* ctx, const float* noise, const float* prompt, con
  * to its longest utterance with zero rows and key-padding masks. A padded
  * utterance equals the single-utterance sampler run at the padded length with
  * its mask (reflect padding and masking make it differ slightly from the
- * unpadded run; an utterance as long as its launch gives exactly
- * itts_cfm_run). Has no single reference function: it batches calls of
- * run_cfm_euler_metal (runtime/impl/tts_synthesis/synthesis_pipeline.cpp:1085).
+ * unpadded run; an utterance as long as its launch gives itts_cfm_run's
+ * result, bitwise when the attention splits its work the same way for both
+ * launch sizes, else up to that split's summation order). Inputs and outputs
+ * pass through a page-locked ring of the context (reserved at creation for
+ * utterances of up to 1600 rows, grown for longer ones): host threads pack
+ * each utterance and the copies run asynchronously. Has no single reference
+ * function: it batches calls of run_cfm_euler_metal
+ * (runtime/impl/tts_synthesis/synthesis_pipeline.cpp:1085).
  */
 int itts_cfm_run_batch(itts_cfm_ctx* ctx, uint32_t n, const itts_cfm_utt* utts, uint32_t steps, float cfg_rate);
 /* Length class of an utterance of T frames in itts_cfm_run_batch (an upper

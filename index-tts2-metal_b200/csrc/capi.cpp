@@ -10,11 +10,67 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "engine.hpp"
 #include "gemm.cuh"
 #include "kernels.cuh"
+
+// Page-locked ring for itts_cfm_run_batch: host threads pack one utterance
+// per slot (its rows and the zero padding up to the launch length), the slot
+// is copied to the launch's device buffers asynchronously, and it is reused
+// once those copies are done (an event per slot); outputs come back through
+// the same slots. The footprint is kSlots utterances, not the whole batch.
+struct PinnedRing {
+  static constexpr int kSlots = 32;
+  float* p = nullptr;
+  size_t slot = 0;  // floats per slot
+  cudaEvent_t ev[kSlots] = {};
+  bool live[kSlots] = {};  // copies reading or writing the slot may be in flight
+  PinnedRing() = default;
+  PinnedRing(const PinnedRing&) = delete;
+  PinnedRing& operator=(const PinnedRing&) = delete;
+  ~PinnedRing() { release(); }
+  void release() {
+    for (int i = 0; i < kSlots; ++i) {
+      if (ev[i]) {
+        if (live[i]) cudaEventSynchronize(ev[i]);
+        cudaEventDestroy(ev[i]);
+      }
+      ev[i] = nullptr;
+      live[i] = false;
+    }
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    slot = 0;
+  }
+  void reserve(size_t floats_per_slot) {
+    if (floats_per_slot <= slot) return;
+    release();
+    void* q = nullptr;
+    if (cudaHostAlloc(&q, static_cast<size_t>(kSlots) * floats_per_slot * sizeof(float), cudaHostAllocPortable) !=
+        cudaSuccess)
+      throw std::runtime_error("page-locked staging allocation failed");
+    p = static_cast<float*>(q);
+    slot = floats_per_slot;
+    for (int i = 0; i < kSlots; ++i)
+      if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess)
+        throw std::runtime_error("staging event creation failed");
+  }
+  float* at(int i) { return p + static_cast<size_t>(i) * slot; }
+  // Waits until no copy touches slot i.
+  void claim(int i) {
+    if (live[i] && cudaEventSynchronize(ev[i]) != cudaSuccess) throw std::runtime_error("staging copy failed");
+    live[i] = false;
+  }
+  void mark(int i, cudaStream_t st) {
+    if (cudaEventRecord(ev[i], st) != cudaSuccess) throw std::runtime_error("staging event record failed");
+    live[i] = true;
+  }
+};
+
+constexpr uint32_t kRingRowsAtCreate = 1600;
 
 struct itts_cfm_ctx {
   std::unique_ptr<itts::Engine> eng;
@@ -23,6 +79,7 @@ struct itts_cfm_ctx {
   itts::Work* staged = nullptr;
   int steps = 0;
   float cfg = 0.0f;
+  PinnedRing ring;  // destroyed before the engine
 };
 
 namespace {
@@ -94,16 +151,12 @@ void check_status(itts::Engine& e) {
 }
 
 // Copy a padded batch into workspace w (host pointers).
-void upload_padded(itts::Engine& e, itts::Work* w, const uint32_t* valid_len, const uint32_t* prompt_len,
-                   const float* noise, const float* prompt_x, const float* cond, const float* style,
-                   const uint32_t* mask_bt) {
-  const size_t BT = static_cast<size_t>(w->B) * w->T;
+// Prompt lengths and the key / WaveNet mask of a launch (from valid_len, or
+// per-row from mask_bt), uploaded from pageable vectors; returns after the
+// stream has drained them.
+void upload_masks(itts::Engine& e, itts::Work* w, const uint32_t* valid_len, const uint32_t* prompt_len,
+                  const uint32_t* mask_bt) {
   cudaStream_t st = e.stream();
-  cuda_ok(cudaMemcpyAsync(w->X0, noise, BT * 80 * sizeof(float), cudaMemcpyHostToDevice, st), "noise upload");
-  cuda_ok(cudaMemcpyAsync(w->prompt_x, prompt_x, BT * 80 * sizeof(float), cudaMemcpyHostToDevice, st), "prompt upload");
-  cuda_ok(cudaMemcpyAsync(w->cond, cond, BT * 512 * sizeof(float), cudaMemcpyHostToDevice, st), "cond upload");
-  cuda_ok(cudaMemcpyAsync(w->style, style, static_cast<size_t>(w->B) * 192 * sizeof(float), cudaMemcpyHostToDevice, st),
-          "style upload");
   std::vector<int> pl(w->B);
   std::vector<float> mask(static_cast<size_t>(w->R));
   for (int b = 0; b < w->B; ++b) {
@@ -121,6 +174,19 @@ void upload_padded(itts::Engine& e, itts::Work* w, const uint32_t* valid_len, co
   cuda_ok(cudaMemcpyAsync(w->mask, mask.data(), mask.size() * sizeof(float), cudaMemcpyHostToDevice, st), "mask upload");
   // Pageable sources: the copies above complete before the host vectors die.
   cuda_ok(cudaStreamSynchronize(st), "upload sync");
+}
+
+void upload_padded(itts::Engine& e, itts::Work* w, const uint32_t* valid_len, const uint32_t* prompt_len,
+                   const float* noise, const float* prompt_x, const float* cond, const float* style,
+                   const uint32_t* mask_bt) {
+  const size_t BT = static_cast<size_t>(w->B) * w->T;
+  cudaStream_t st = e.stream();
+  cuda_ok(cudaMemcpyAsync(w->X0, noise, BT * 80 * sizeof(float), cudaMemcpyHostToDevice, st), "noise upload");
+  cuda_ok(cudaMemcpyAsync(w->prompt_x, prompt_x, BT * 80 * sizeof(float), cudaMemcpyHostToDevice, st), "prompt upload");
+  cuda_ok(cudaMemcpyAsync(w->cond, cond, BT * 512 * sizeof(float), cudaMemcpyHostToDevice, st), "cond upload");
+  cuda_ok(cudaMemcpyAsync(w->style, style, static_cast<size_t>(w->B) * 192 * sizeof(float), cudaMemcpyHostToDevice, st),
+          "style upload");
+  upload_masks(e, w, valid_len, prompt_len, mask_bt);
 }
 
 void stage(itts_cfm_ctx* ctx, uint32_t B, uint32_t T, const uint32_t* valid_len, const uint32_t* prompt_len,
@@ -167,6 +233,15 @@ int itts_cfm_create_ex(const char* bundle_dir, int device, uint32_t flags, itts_
   try {
     auto ctx = std::make_unique<itts_cfm_ctx>();
     ctx->eng = std::make_unique<itts::Engine>(bundle_dir, device, (flags & ITTS_CREATE_VERIFY_SHA256) != 0);
+    // The batch entry point's page-locked ring, sized for utterances of up to
+    // kRingRowsAtCreate rows (~138 MB), so a first itts_cfm_run_batch does not
+    // pay for pinning it; longer utterances grow it on demand. A failure here
+    // only defers the allocation to that call.
+    try {
+      ctx->ring.reserve(static_cast<size_t>(kRingRowsAtCreate) * (2 * 80 + 512));
+    } catch (const std::exception&) {
+      ctx->ring.release();
+    }
     *out = ctx.release();
     return ITTS_OK;
   } catch (const std::exception& e) {
@@ -249,6 +324,13 @@ int itts_cfm_run_batch(itts_cfm_ctx* ctx, uint32_t n, const itts_cfm_utt* utts, 
     // unpadded, exactly as itts_cfm_run would.
     std::map<uint32_t, std::vector<uint32_t>> buckets;
     for (uint32_t i = 0; i < n; ++i) buckets[itts_cfm_bucket_len(utts[i].T)].push_back(i);
+    // Launch list.
+    struct Launch {
+      const std::vector<uint32_t>* idx;
+      size_t off;
+      uint32_t B, Tp;
+    };
+    std::vector<Launch> launches;
     for (auto& kv : buckets) {
       std::stable_sort(kv.second.begin(), kv.second.end(),
                        [&](uint32_t a, uint32_t b) { return utts[a].T > utts[b].T; });
@@ -256,28 +338,109 @@ int itts_cfm_run_batch(itts_cfm_ctx* ctx, uint32_t n, const itts_cfm_utt* utts, 
       for (size_t off = 0; off < kv.second.size(); off += per) {
         const uint32_t B = static_cast<uint32_t>(std::min<size_t>(per, kv.second.size() - off));
         const uint32_t Tp = utts[kv.second[off]].T;
-        std::vector<float> noise(static_cast<size_t>(B) * Tp * 80, 0.0f), px(noise.size(), 0.0f),
-            cond(static_cast<size_t>(B) * Tp * 512, 0.0f), style(static_cast<size_t>(B) * 192, 0.0f),
-            out(noise.size(), 0.0f);
-        std::vector<uint32_t> vl(B), pl(B);
-        for (uint32_t b = 0; b < B; ++b) {
-          const itts_cfm_utt& u = utts[kv.second[off + b]];
-          vl[b] = u.T;
-          pl[b] = u.P;
-          std::memcpy(&noise[static_cast<size_t>(b) * Tp * 80], u.noise, static_cast<size_t>(u.T) * 80 * 4);
-          if (u.P) std::memcpy(&px[static_cast<size_t>(b) * Tp * 80], u.prompt, static_cast<size_t>(u.P) * 80 * 4);
-          std::memcpy(&cond[static_cast<size_t>(b) * Tp * 512], u.cond, static_cast<size_t>(u.T) * 512 * 4);
-          std::memcpy(&style[static_cast<size_t>(b) * 192], u.style, 192 * 4);
-        }
-        stage(ctx, B, Tp, vl.data(), pl.data(), noise.data(), px.data(), cond.data(), style.data(), steps, cfg_rate);
-        ctx->eng->enqueue_sampler(ctx->staged, ctx->steps, ctx->cfg, true);
-        check_status(*ctx->eng);
-        fetch(ctx, out.data());
-        for (uint32_t b = 0; b < B; ++b) {
-          const itts_cfm_utt& u = utts[kv.second[off + b]];
-          std::memcpy(u.out_mel, &out[static_cast<size_t>(b) * Tp * 80], static_cast<size_t>(u.T) * 80 * 4);
+        launches.push_back(Launch{&kv.second, off, B, Tp});
+      }
+    }
+    // Packing and unpacking run over a group's utterances on up to 16 host threads.
+    auto parallel = [](uint32_t count, const auto& body) {
+      const uint32_t hw = std::max(1u, std::thread::hardware_concurrency());
+      const uint32_t nt = std::min<uint32_t>(std::min<uint32_t>(hw, 16u), count);
+      if (nt <= 1) {
+        for (uint32_t i = 0; i < count; ++i) body(i);
+        return;
+      }
+      std::vector<std::thread> th;
+      for (uint32_t t = 0; t < nt; ++t)
+        th.emplace_back([&, t] {
+          for (uint32_t i = t; i < count; i += nt) body(i);
+        });
+      for (auto& x : th) x.join();
+    };
+    PinnedRing& ring = ctx->ring;
+    uint32_t t_max = 0;
+    for (const Launch& L : launches) t_max = std::max(t_max, L.Tp);
+    ring.reserve(static_cast<size_t>(t_max) * (2 * 80 + 512));  // once, for the longest launch
+    constexpr int kHalf = PinnedRing::kSlots / 2;  // utterances per group; groups alternate ring halves
+    itts::Engine& e = *ctx->eng;
+    cudaStream_t st = e.stream();
+    for (const Launch& L : launches) {
+      const uint32_t B = L.B, Tp = L.Tp;
+      check_run_args(B, Tp, steps, cfg_rate, branches);
+      itts::Work* w = e.work(static_cast<int>(B), static_cast<int>(Tp), static_cast<int>(branches));
+      const size_t n80 = static_cast<size_t>(Tp) * 80, n512 = static_cast<size_t>(Tp) * 512;
+      std::vector<uint32_t> vl(B), pl(B);
+      std::vector<float> style(static_cast<size_t>(B) * 192);
+      for (uint32_t b = 0; b < B; ++b) {
+        const itts_cfm_utt& u = utts[(*L.idx)[L.off + b]];
+        vl[b] = u.T;
+        pl[b] = u.P;
+        std::memcpy(&style[static_cast<size_t>(b) * 192], u.style, 192 * 4);
+      }
+      // Inputs: a group is packed into its ring half while the previous
+      // group's copies (in the other half) run.
+      for (uint32_t g0 = 0; g0 < B; g0 += kHalf) {
+        const int base = static_cast<int>((g0 / kHalf) & 1) * kHalf;
+        const uint32_t cnt = std::min<uint32_t>(kHalf, B - g0);
+        for (uint32_t i = 0; i < cnt; ++i) ring.claim(base + static_cast<int>(i));
+        parallel(cnt, [&](uint32_t i) {
+          const itts_cfm_utt& u = utts[(*L.idx)[L.off + g0 + i]];
+          float* sl = ring.at(base + static_cast<int>(i));
+          float* noise = sl;
+          float* px = sl + n80;
+          float* cond = sl + 2 * n80;
+          std::memcpy(noise, u.noise, static_cast<size_t>(u.T) * 80 * 4);
+          std::memset(noise + static_cast<size_t>(u.T) * 80, 0, static_cast<size_t>(Tp - u.T) * 80 * 4);
+          if (u.P) std::memcpy(px, u.prompt, static_cast<size_t>(u.P) * 80 * 4);
+          std::memset(px + static_cast<size_t>(u.P) * 80, 0, static_cast<size_t>(Tp - u.P) * 80 * 4);
+          std::memcpy(cond, u.cond, static_cast<size_t>(u.T) * 512 * 4);
+          std::memset(cond + static_cast<size_t>(u.T) * 512, 0, static_cast<size_t>(Tp - u.T) * 512 * 4);
+        });
+        for (uint32_t i = 0; i < cnt; ++i) {
+          const int sidx = base + static_cast<int>(i);
+          const size_t b = g0 + i;
+          const float* sl = ring.at(sidx);
+          cuda_ok(cudaMemcpyAsync(w->X0 + b * n80, sl, n80 * 4, cudaMemcpyHostToDevice, st), "noise upload");
+          cuda_ok(cudaMemcpyAsync(w->prompt_x + b * n80, sl + n80, n80 * 4, cudaMemcpyHostToDevice, st),
+                  "prompt upload");
+          cuda_ok(cudaMemcpyAsync(w->cond + b * n512, sl + 2 * n80, n512 * 4, cudaMemcpyHostToDevice, st),
+                  "cond upload");
+          ring.mark(sidx, st);
         }
       }
+      cuda_ok(cudaMemcpyAsync(w->style, style.data(), style.size() * 4, cudaMemcpyHostToDevice, st), "style upload");
+      upload_masks(e, w, vl.data(), pl.data(), nullptr);  // also drains the copies above
+      ctx->staged = w;
+      ctx->steps = static_cast<int>(steps);
+      ctx->cfg = cfg_rate;
+      e.enqueue_sampler(w, ctx->steps, ctx->cfg, true);
+      check_status(e);
+      // Outputs: each group is copied into a ring half, then unpacked by the
+      // host threads while the next group's copies run.
+      uint32_t prev_g0 = 0, prev_cnt = 0;
+      int prev_base = 0;
+      auto unpack = [&](uint32_t g0, uint32_t cnt, int base) {
+        for (uint32_t i = 0; i < cnt; ++i) ring.claim(base + static_cast<int>(i));
+        parallel(cnt, [&](uint32_t i) {
+          const itts_cfm_utt& u = utts[(*L.idx)[L.off + g0 + i]];
+          std::memcpy(u.out_mel, ring.at(base + static_cast<int>(i)), static_cast<size_t>(u.T) * 80 * 4);
+        });
+      };
+      for (uint32_t g0 = 0; g0 < B; g0 += kHalf) {
+        const int base = static_cast<int>((g0 / kHalf) & 1) * kHalf;
+        const uint32_t cnt = std::min<uint32_t>(kHalf, B - g0);
+        for (uint32_t i = 0; i < cnt; ++i) {
+          const int sidx = base + static_cast<int>(i);
+          ring.claim(sidx);
+          cuda_ok(cudaMemcpyAsync(ring.at(sidx), w->X + (g0 + i) * n80, n80 * 4, cudaMemcpyDeviceToHost, st),
+                  "mel download");
+          ring.mark(sidx, st);
+        }
+        if (prev_cnt) unpack(prev_g0, prev_cnt, prev_base);
+        prev_g0 = g0;
+        prev_cnt = cnt;
+        prev_base = base;
+      }
+      if (prev_cnt) unpack(prev_g0, prev_cnt, prev_base);
     }
   });
 }
