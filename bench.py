@@ -592,8 +592,8 @@ def run_reference(args, rank):
     """The reference arm: the reference's compiled run_dit_estimator_step_cpu
     on the configuration-2 utterance at its full length (T=800). The timed
     region runs `steps` guided CFM steps (2 * steps estimator calls at
-    T=800) spread over all host threads; frames/s is that of full 25-step
-    sampler runs. Configuration 1 (one guided step at T=400, P=150, t=0.5) is
+    T=800), rounded up to whole rounds of the host threads, spread over all
+    of them; frames/s is that of full 25-step sampler runs. Configuration 1 (one guided step at T=400, P=150, t=0.5) is
     measured exactly on one thread while the warm-up calls run."""
     if rank != 0:
         return 0
@@ -624,16 +624,22 @@ def run_reference(args, rank):
     warm = [c for _ in range(args.warmup) for c in _guided_step_calls(ref, u)]
     _ref_call_pool(warm, max(1, threads - 1))
     th1.join()
-    calls = [c for _ in range(args.steps) for c in _guided_step_calls(ref, u)]
+    # Whole rounds of calls keep every host thread busy: `steps` guided steps
+    # rounded up to a multiple of threads / 2 (a partly idle last round would
+    # understate the reference's throughput).
+    per_round = max(1, threads // 2)
+    steps_run = ((args.steps + per_round - 1) // per_round) * per_round
+    calls = [c for _ in range(steps_run) for c in _guided_step_calls(ref, u)]
     per_call = []
     wall = _ref_call_pool(calls, threads, per_call)
-    fps = args.steps * u.T / (cfg["steps"] * wall)
-    sample = (f"{args.steps} guided CFM steps of the config-{args.workload} utterance at its full length "
-              f"(T={u.T}, P={u.P}): {2 * args.steps} run_dit_estimator_step_cpu calls (conditional + null) over "
-              f"{threads} host threads, {wall:.1f} s; frames/s = steps*T/({cfg['steps']} CFM steps * wall)")
+    fps = steps_run * u.T / (cfg["steps"] * wall)
+    sample = (f"{steps_run} guided CFM steps ({args.steps} requested, rounded up to whole rounds of the host "
+              f"threads) of the config-{args.workload} utterance at its full length (T={u.T}, P={u.P}): "
+              f"{2 * steps_run} run_dit_estimator_step_cpu calls (conditional + null) over {threads} host threads, "
+              f"{wall:.1f} s; frames/s = guided steps*T/({cfg['steps']} CFM steps * wall)")
     line = {
         "impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * wall / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": 1e3 * wall / steps_run, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"config {args.workload}", "T": u.T, "P": u.P, "steps_cfm": cfg["steps"],
                    "cfg_rate": cfg["cfg"]},
