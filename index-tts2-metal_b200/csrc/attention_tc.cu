@@ -189,7 +189,12 @@ __device__ __forceinline__ void softmax_role(const AttnCtx& c, int wg, int quart
       // The mask row of this block was published with kv_full (already complete).
       const int kst = (g + j) % kKV;
       if (!(ok = mbar_wait(&c.kv_full[kst], ((g + j) / kKV) & 1, c.status, kDevTimeoutAttn))) break;
-      if (!c.full_block[kst]) {
+      const int bflag = c.full_block[kst];
+      // Chunks of 16 keys of this group's share that hold a live key; the rest
+      // (keys past the end of the sequence in its last block, or masked) have
+      // P = 2^(-inf) = +0 exactly and are written as zeros without an ex2.
+      const int live = (bflag >> 8) - kofs / 16;
+      if (!(bflag & 1)) {
         const float* brow = c.bias + kst * kKB + kofs;
 #pragma unroll
         for (int k = 0; k < NK; ++k) sr[k] = __float_as_uint(__uint_as_float(sr[k]) + brow[k]);
@@ -226,12 +231,17 @@ __device__ __forceinline__ void softmax_role(const AttnCtx& c, int wg, int quart
 #pragma unroll
       for (int q = 0; q < NK / 16; ++q) {  // chunks of 16 keys -> 8 columns of f16 pairs
         uint32_t pw[8];
+        if (q < live) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float y0 = ex2_approx(fmaf(__uint_as_float(sr[q * 16 + 2 * e]), kLog2e, nref));
-          const float y1 = ex2_approx(fmaf(__uint_as_float(sr[q * 16 + 2 * e + 1]), kLog2e, nref));
-          ls[e & 1] += y0 + y1;
-          pw[e] = pack_f16(y0, y1);
+          for (int e = 0; e < 8; ++e) {
+            const float y0 = ex2_approx(fmaf(__uint_as_float(sr[q * 16 + 2 * e]), kLog2e, nref));
+            const float y1 = ex2_approx(fmaf(__uint_as_float(sr[q * 16 + 2 * e + 1]), kLog2e, nref));
+            ls[e & 1] += y0 + y1;
+            pw[e] = pack_f16(y0, y1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pw[e] = 0u;
         }
         tmem_st8(t_p + q * 8, pw);
       }
@@ -421,17 +431,21 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           tma_load_3d(sm + OFF_K + st * 16384, &tm, &kv_full[st], 0, seq0 + j * kKB, 8 + I.h);
           tma_load_3d(sm + OFF_V + st * 16384, &tm, &kv_full[st], 0, seq0 + j * kKB, 16 + I.h);
         }
-        bool valid4 = true;
+        bool valid4 = true, any4 = false;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int k = lane * 4 + i;
           const int key = j * kKB + k;
           const bool valid = key < T && row_mask[seq0 + key] != 0.0f;
           valid4 = valid4 && valid;
+          any4 = any4 || valid;
           bias[st * kKB + k] = valid ? 0.0f : -CUDART_INF_F;
         }
         const bool all_valid = __all_sync(0xffffffffu, valid4);
-        if (lane == 0) full_block[st] = all_valid ? 1 : 0;
+        // 16-key chunks (4 lanes each) up to the last one holding a live key.
+        const unsigned live_lanes = __ballot_sync(0xffffffffu, any4);
+        const int live_chunks = live_lanes ? (31 - __clz(live_lanes)) / 4 + 1 : 0;
+        if (lane == 0) full_block[st] = (all_valid ? 1 : 0) | (live_chunks << 8);
         __syncwarp();
         mbar_arrive(&kv_full[st]);
         ATTN_TRACE(lane == 0 && g < 8, 10 + g);

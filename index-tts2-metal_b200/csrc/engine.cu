@@ -3,6 +3,7 @@
 //   merge GEMM (x slice, + step-invariant base) -> 13 x { [skip-in GEMM],
 //   AdaRMSNorm, QKV GEMM (+RoPE), attention, wo GEMM (+residual), AdaRMSNorm,
 //   w13 GEMM (+SwiGLU), w2 GEMM (+residual) } -> AdaRMSNorm -> post GEMM
+//   (w2 of layers 6..11 is composed into the next layer's skip-in GEMM)
 //   (skip_linear composed with conv1|res -> reflect-padded WaveNet input and
 //   the res projection) -> 8 x { k=5 conv GEMM (+gate), res/skip GEMM
 //   (+update) } -> AdaLN -> out GEMM (final linear composed with conv2) ->
@@ -21,6 +22,10 @@
 namespace itts {
 
 namespace {
+
+// Layers 6..11: feed_forward.w2 is composed at load into the skip_in_linear
+// of layer l + 1 (a linear map of [h | g | skip]), so it has no launch of its own.
+constexpr bool w2_composed(int l) { return l >= kLayers / 2 && l < kLayers - 1; }
 
 struct Operand {
   const __half* p = nullptr;
@@ -238,14 +243,13 @@ Work* Engine::work(int B, int T, int branches) {
     w->U = carve<__half>(cur, R * kUld);
     w->base = carve<float>(cur, R * 512);
     w->xres = carve<float>(cur, R * 512);
-    w->x16 = carve<__half>(cur, R * 512);
     for (int i = 0; i < 6; ++i) w->skip16[i] = carve<__half>(cur, R * 512);
     w->xn16 = carve<__half>(cur, R * 512);
     w->ss = carve<float>(cur, R * 16);
     w->qkv16 = carve<__half>(cur, R * 1536);
     w->attn16 = carve<__half>(cur, R * 512);
     w->h = carve<float>(cur, R * 512);
-    w->g16 = carve<__half>(cur, R * 1536);
+    w->cat16 = carve<__half>(cur, R * 2048);
     w->xp16 = carve<__half>(cur, static_cast<size_t>(w->Rp) * 512);
     w->res = carve<float>(cur, R * 512);
     w->gate16 = carve<__half>(cur, R * 512);
@@ -308,9 +312,11 @@ void Engine::build_work_launches(Work* w) {
   for (int l = 0; l < kLayers; ++l) {
     const LayerW& L = w_.L[l];
     if (l > kLayers / 2) {
+      // skip_in_linear composed with the previous layer's w2: [h | g] from
+      // cat16 (32 k-blocks), then the skip source (8 k-blocks).
       GemmLaunch& g = w->g_skip[l];
-      g = make_gemm(act(w->x16, 512, R), act(w->skip16[kLayers - 1 - l], 512, R), wt(L.wskip, 1024, 512), R, 512,
-                    1024, kASplit, 8, 0, 0, kEpiF32);
+      g = make_gemm(Operand{w->cat16, 2048, R, 2048}, act(w->skip16[kLayers - 1 - l], 512, R),
+                    wt(L.wskip, 2560, 512), R, 512, 2560, kASplit, 32, 0, 0, kEpiF32);
       g.args.bias = L.bskip;
       g.args.out32 = w->xres;
       g.args.ld32 = 512;
@@ -321,21 +327,26 @@ void Engine::build_work_launches(Work* w) {
     w->g_wo[l] = make_gemm(act(w->attn16, 512, R), none, wt(L.wo, 512, 512), R, 512, 512, kAPlain, 0, 0, 0, kEpiF32);
     w->g_wo[l].args.resid32 = w->xres;
     w->g_wo[l].args.ldr = 512;
-    w->g_wo[l].args.out32 = w->h;
     w->g_wo[l].args.ld32 = 512;
+    if (w2_composed(l)) {
+      // h is read only as the f16 operand of the next layer's composed skip GEMM.
+      w->g_wo[l].args.out16 = w->cat16;
+      w->g_wo[l].args.ld16 = 2048;
+    } else {
+      w->g_wo[l].args.out32 = w->h;
+    }
     w->g_w13[l] = make_gemm(act(w->xn16, 512, R), none, wt(L.w13, 512, 3072), R, 3072, 512, kAPlain, 0, 0, 0, kEpiSwiGLU);
-    w->g_w13[l].args.out16 = w->g16;
-    w->g_w13[l].args.ld16 = 1536;
-    w->g_w2[l] = make_gemm(act(w->g16, 1536, R), none, wt(L.w2, 1536, 512), R, 512, 1536, kAPlain, 0, 0, 0, kEpiF32);
+    w->g_w13[l].args.out16 = w->cat16 + 512;
+    w->g_w13[l].args.ld16 = 2048;
+    if (w2_composed(l)) continue;
+    w->g_w2[l] = make_gemm(Operand{w->cat16 + 512, 1536, R, 2048}, none, wt(L.w2, 1536, 512), R, 512, 1536, kAPlain,
+                           0, 0, 0, kEpiF32);
     w->g_w2[l].args.resid32 = w->h;
     w->g_w2[l].args.ldr = 512;
     w->g_w2[l].args.out32 = w->xres;
     w->g_w2[l].args.ld32 = 512;
     if (l < kLayers / 2) {
       w->g_w2[l].args.out16 = w->skip16[l];
-      w->g_w2[l].args.ld16 = 512;
-    } else if (l < kLayers - 1) {
-      w->g_w2[l].args.out16 = w->x16;
       w->g_w2[l].args.ld16 = 512;
     }
   }
@@ -483,7 +494,7 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
       case kEpiQKV: b += rows * N * 2.0; break;
       case kEpiSwiGLU: case kEpiWnGate: b += rows * N; break;
       case kEpiF32:
-        b += rows * N * 4.0 * (a.resid32 ? 2.0 : 1.0);
+        b += rows * N * 4.0 * ((a.out32 ? 1.0 : 0.0) + (a.resid32 ? 1.0 : 0.0));
         if (a.out16) b += rows * N * 2.0;
         if (a.nrm16) b += rows * N * 2.0 + rows * (N / 16.0) * 4.0;
         break;
@@ -514,14 +525,16 @@ void Engine::enqueue_step(Work* w, const float* tab, float dt, float cfg, bool d
   };
   G("gemm.merge", with_w(w->g_merge, tab + kTabAttn), 80);
   for (int l = 0; l < kLayers; ++l) {
-    if (l > kLayers / 2) G("gemm.skip_in", with_w(w->g_skip[l], tab + kTabAttn + l * 1024), 1024);
+    // (the skip GEMM stands for skip_in_linear and the previous layer's w2)
+    if (l > kLayers / 2)
+      G("gemm.skip_in", with_w(w->g_skip[l], tab + kTabAttn + l * 1024), 2560, 1024.0 * 512 + 1536.0 * 512);
     G("gemm.qkv", with_bias(w->g_qkv[l], tab + kTabQkvC + l * 1536), 512);
     P.run("attention", S * 4.0 * T * T * 512.0, R * (1536 + 512) * 2.0,
           [&] { check(attention_tc_run(w->tm_attn, w->mask, w->attn16, w->S, w->T, d_status_, stream_), "attention"); });
     G("gemm.wo", with_w(w->g_wo[l], tab + kTabFfn + l * 1024), 512);
     G("gemm.w13", with_bias(w->g_w13[l], tab + kTabW13C + l * 3072), 512);
     if (l + 1 <= kLayers / 2) G("gemm.w2", with_w(w->g_w2[l], tab + kTabAttn + (l + 1) * 1024), 1536);
-    else G("gemm.w2", w->g_w2[l], 1536);
+    else if (!w2_composed(l)) G("gemm.w2", w->g_w2[l], 1536);
   }
   P.run("adarms", 0.0, R * 512 * (4 + 2), [&] {
     check(adarms_run(w->xres, w->R, tab + kTabNorm, w_.g_norm, w->xn16, stream_), "adarms");

@@ -47,14 +47,16 @@ struct Work {
   float* base = nullptr;  // [R, 512]
   // transformer
   float* xres = nullptr;
-  __half* x16 = nullptr;
   __half* skip16[6] = {};
   __half* xn16 = nullptr;  // normalised GEMM operand (folded AdaRMS: x * w * g)
   float* ss = nullptr;     // [16][R] per-32-column partial sums of squares of the normalised x
   __half* qkv16 = nullptr;
   __half* attn16 = nullptr;
   float* h = nullptr;
-  __half* g16 = nullptr;
+  // [R, 2048] f16: columns 512.. hold every layer's SwiGLU activations g;
+  // columns 0..511 f16(h) of layers 6..11, whose w2 is composed into the next
+  // layer's skip_in_linear (that GEMM reads [h | g | skip] directly).
+  __half* cat16 = nullptr;
   // post + wavenet + final
   __half* xp16 = nullptr;  // [S*(T+4), 512]
   float* res = nullptr;

@@ -600,9 +600,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, const CUtens
         // layout is the 128-byte swizzle of the tensor map; rows >= M and
         // columns >= N are not written); a 16-column remainder through the
         // lanes' coalesced stores.
+        // (out32 may be null when only the f16 outputs are read downstream.)
         if (args.tma_o32 && cp + 1 < c_end && ng < args.N && m0 + (row & ~31) < args.M) {
           stage_tma_store(tmo, stg, ng, m0 + (row & ~31), lane);
-        } else {
+        } else if (args.out32) {
           flush_f32(stg, static_cast<const float*>(d0), ng, ncols, lane);
         }
         if (tr) GEMM_TRACE(25);

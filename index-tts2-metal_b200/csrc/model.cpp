@@ -224,7 +224,30 @@ void load_weights(const Mit2Bundle& b, DevWeights* w) {
     }
     pk.add(h16(b, p + "feed_forward.w2.weight", 512 * 1536), reinterpret_cast<uint16_t**>(&L.w2));
     if (l > kLayers / 2) {
-      pk.add(h16(b, p + "skip_in_linear.weight", 512 * 1024), reinterpret_cast<uint16_t**>(&L.wskip));
+      // skip_in_linear reads [x | skip] where x = h + W2 . g is the output of
+      // layer l - 1 (h: its stream after attention, g: its SwiGLU activations;
+      // feed_forward.w2 has no bias) and nothing else reads x, so
+      //   Wsk . [x ; skip] = Wx . h + (Wx . W2) . g + Ws . skip
+      // is one 2560 -> 512 linear map over [h | g | skip] (Wx, Ws: the x and
+      // skip halves of skip_in_linear.weight). Composed in fp32, rounded to f16 once.
+      const auto wsk = b.as_f32(p + "skip_in_linear.weight");  // [512][1024]
+      const auto w2p = b.as_f32(P("transformer.layers." + std::to_string(l - 1) + ".feed_forward.w2.weight"));
+      if (wsk.size() != 512u * 1024 || w2p.size() != 512u * 1536)
+        throw std::runtime_error("bundle: skip_in_linear / feed_forward.w2 shapes");
+      std::vector<float> wc(static_cast<size_t>(512) * 2560, 0.0f);
+      for (int o = 0; o < 512; ++o) {
+        float* dst = &wc[static_cast<size_t>(o) * 2560];
+        const float* src = &wsk[static_cast<size_t>(o) * 1024];
+        std::memcpy(dst, src, 512 * sizeof(float));
+        std::memcpy(dst + 2048, src + 512, 512 * sizeof(float));
+        float* mid = dst + 512;
+        for (int j = 0; j < 512; ++j) {
+          const float a = src[j];
+          const float* w2r = &w2p[static_cast<size_t>(j) * 1536];
+          for (int k = 0; k < 1536; ++k) mid[k] += a * w2r[k];
+        }
+      }
+      pk.add(to_h(wc), reinterpret_cast<uint16_t**>(&L.wskip));
       pk.add(f32(b, p + "skip_in_linear.bias", 512), &L.bskip);
     }
   }

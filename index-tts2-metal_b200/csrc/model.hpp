@@ -9,7 +9,9 @@
 //   - the merge weight split into its x slice [512][80] and the rest [512][784];
 //   - linear layers with nothing between them composed into one matrix (in
 //     fp32, then rounded to f16 once): [conv1 ; res_projection] . skip_linear
-//     (592 -> 1024) and conv2 . final_layer.linear (512 -> 80).
+//     (592 -> 1024), conv2 . final_layer.linear (512 -> 80), and for layers
+//     7..12 skip_in_linear with the feed_forward.w2 of layer l - 1 (the residual
+//     add between them is linear): [h | g | skip] (2560) -> 512.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -41,7 +43,7 @@ struct LayerW {
   __half* wo = nullptr;     // [512][512]
   __half* w13 = nullptr;    // [3072][512] interleaved w1/w3
   __half* w2 = nullptr;     // [512][1536]
-  __half* wskip = nullptr;  // [512][1024], layers 7..12
+  __half* wskip = nullptr;  // layers 7..12: [512][2560] = [Wx | Wx . W2(l-1) | Ws] over [h | g | skip]
   float* bskip = nullptr;
   float* g_attn = nullptr;  // attention_norm.norm.weight [512]
   float* g_ffn = nullptr;   // ffn_norm.norm.weight [512]
